@@ -1,0 +1,438 @@
+#!/usr/bin/env python3
+"""Paged decode-attention benchmark (B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload olmoe|qwen3-fp8]
+
+Workloads (synthetic, seeded):
+  olmoe      16 layers x 16 KV heads (MHA), head_dim 128, fp16, 16-token pages,
+             64 sequences x context 4096 per GPU, one query token per
+             sequence, block tables a random permutation of a pool of 18,750
+             all-layer pages (= 300,000 layer-pages of 128 KiB).
+  qwen3-fp8  36 layers, 32 query / 8 KV heads, head_dim 128, FP8-e4m3 KV with
+             per-page fp32 scales, bf16 queries, 128 sequences x context 16384.
+
+A step = for every layer: append one new K/V token per sequence (scatter
+through the block table), then paged decode attention for every sequence.
+The step keeps the context fixed (the new token rewrites slot ctx-1).
+
+One JSON line on rank 0. `value` = KV GB/s over all ranks (algorithmic bytes
+of attention + append per step / step time, inputs resident in HBM). `e2e`
+= the same metric through the pool's public calls with inputs copied from
+pinned host memory each step and outputs read back. `roofline` = the decode
+attention op's algorithmic bytes per launch / its average CUDA-event time.
+Under torchrun each rank owns its own pool and sequences (sequence sharding,
+no collective on the data path; weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+if "--impl" in sys.argv and "reference" in sys.argv:
+    _n = str(os.cpu_count() or 1)
+    for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ.setdefault(_v, _n)
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PAGE = 16
+WORKLOADS = {
+    "olmoe": dict(model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="fp16", qdt=torch.float16,
+                  batch=64, ctx=4096, pool_pages=18750),
+    "qwen3-fp8": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="fp8_e4m3",
+                      qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
+}
+
+
+def kv_bytes_per_elem(kv: str) -> int:
+    return 2 if kv in ("fp16", "bf16") else 1
+
+
+def attn_bytes_per_launch(w) -> int:
+    """Algorithmic bytes one decode-attention launch must move."""
+    B, T, hkv, hq, d = w["batch"], w["ctx"], w["hkv"], w["hq"], w["d"]
+    b = kv_bytes_per_elem(w["kv"])
+    kv = B * T * hkv * d * 2 * b
+    scales = B * (T // PAGE) * hkv * 2 * 4 if w["kv"] == "fp8_e4m3" else 0
+    bt = B * (T // PAGE) * 4
+    qo = B * hq * d * 2 * 2
+    return kv + scales + bt + qo
+
+
+def append_bytes_per_launch(w) -> int:
+    B, hkv, d = w["batch"], w["hkv"], w["d"]
+    src = B * hkv * d * 2 * 2          # read K and V rows (16-bit source)
+    dst = B * hkv * d * 2 * kv_bytes_per_elem(w["kv"])
+    return src + dst
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        mhz, mx, reasons = [], 0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not mhz:
+            return None
+        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peak_gbs():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    f = REPO / "profiles" / f"decode_attn_{workload}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device(f"cuda:{local}"))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- our arm
+def build_state(w, rank: int):
+    from synapcore_b200.pool import KVPool
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L, hq, hkv, d, B, T = w["layers"], w["hq"], w["hkv"], w["d"], w["batch"], w["ctx"]
+    pool = KVPool(L, hkv, d, w["pool_pages"], w["kv"], device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    view = pool.pool_view()
+    if w["kv"] == "fp8_e4m3":
+        # random e4m3 codes (no NaN bytes 0x7f / 0xff) and per-page-head scales U[0.5,4]/448*4
+        for l in range(L):
+            codes = torch.randint(0, 0x7F, view[l].shape, dtype=torch.uint8, device=dev, generator=g)
+            sign = torch.randint(0, 2, view[l].shape, dtype=torch.uint8, device=dev, generator=g) << 7
+            view[l].copy_(codes | sign)
+        pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
+    else:
+        for l in range(L):
+            view[l].normal_(generator=g)
+    n_blocks = T // PAGE
+    rng = np.random.default_rng(rank)
+    perm = rng.permutation(w["pool_pages"])[: B * n_blocks].astype(np.int32)
+    bt = torch.from_numpy(perm.reshape(B, n_blocks)).to(dev)
+    ctx = torch.full((B,), T, dtype=torch.int32, device=dev)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    start = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
+    q = torch.randn((L, B, hq, d), generator=g, device=dev).to(w["qdt"])
+    src_dt = torch.float16 if w["kv"] == "fp16" else torch.bfloat16
+    kn = torch.randn((L, B, hkv, d), generator=g, device=dev).to(src_dt)
+    vn = torch.randn((L, B, hkv, d), generator=g, device=dev).to(src_dt)
+    out = torch.empty((L, B, hq, d), dtype=w["qdt"], device=dev)
+    ws = torch.empty(pool.decode_workspace_bytes(B, hq, n_blocks), dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+    return dict(pool=pool, bt=bt, ctx=ctx, cu=cu, start=start, q=q, kn=kn, vn=vn, out=out, ws=ws)
+
+
+def run_step(w, s, attn_events=None):
+    pool = s["pool"]
+    for l in range(w["layers"]):
+        pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=l)
+        if attn_events is not None:
+            attn_events.append(torch.cuda.Event(enable_timing=True))
+            attn_events[-1].record()
+        pool.decode_attn(l, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
+        if attn_events is not None:
+            attn_events.append(torch.cuda.Event(enable_timing=True))
+            attn_events[-1].record()
+
+
+def bench_ours(args, w, world, rank, local):
+    s = build_state(w, rank)
+    pool = s["pool"]
+    for _ in range(args.warmup):
+        run_step(w, s)
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    attn_ev = []
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run_step(w, s, attn_ev)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    attn_ms = [attn_ev[i].elapsed_time(attn_ev[i + 1]) for i in range(0, len(attn_ev), 2)]
+    attn_avg_ms = max_over_ranks(float(np.mean(attn_ms)), world)
+    pool.raise_on_status()
+
+    # ---- e2e through the public calls, host buffers in pinned memory
+    L = w["layers"]
+    h_q = s["q"].cpu().pin_memory()
+    h_k = s["kn"].cpu().pin_memory()
+    h_v = s["vn"].cpu().pin_memory()
+    h_out = torch.empty(s["out"].shape, dtype=s["out"].dtype).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(s["q"]), torch.empty_like(s["kn"]), torch.empty_like(s["vn"])
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        for l in range(L):
+            pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=l)
+            pool.decode_attn(l, d_q[l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
+        h_out.copy_(s["out"], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    h2d = h_q.numel() * h_q.element_size() + 2 * h_k.numel() * h_k.element_size()
+    d2h = h_out.numel() * h_out.element_size()
+    pool.raise_on_status()
+
+    step_bytes = L * (attn_bytes_per_launch(w) + append_bytes_per_launch(w))
+    ms_step = ms_total / args.steps
+    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+    e2e_value = world * step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    achieved = attn_bytes_per_launch(w) / (attn_avg_ms * 1e-3) / 1e9
+    traffic = profiled_traffic(args.workload)
+    res = {
+        "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w["kv"],
+        "data": "synthetic (seeded N(0,1) KV pages, random block-table permutation)",
+        "tok_per_s": round(world * w["batch"] / (ms_step * 1e-3), 1),
+        "pct_hbm_peak": round(100.0 * value / world / peak, 2),
+        "config": {
+            "workload": f"{args.workload}: paged decode attention, {w['model']} shape {w['layers']}L x "
+                        f"{w['hq']}q/{w['hkv']}kv heads x d{w['d']}, {w['kv']} KV, page 16, batch {w['batch']}/GPU, "
+                        f"context {w['ctx']}, pool {w['pool_pages']} all-layer pages",
+            "global_batch": world * w["batch"],
+            "seq_len": w["ctx"],
+            "parallelism": f"sequence-sharded x{world} (independent pools)",
+            "l2": "inputs larger than L2 (KV per layer launch >> 126 MB)",
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(args.steps * L * 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "decode_kernel (+combine) per layer launch",
+                     "bytes_per_launch": attn_bytes_per_launch(w), "avg_launch_ms": round(attn_avg_ms, 4)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+    pool.close()
+    return res
+
+
+# ----------------------------------------------------------------------------- CPU (reference) arm
+def cpu_sample(w, n_seqs: int, ctx: int, seed: int = 0):
+    """A bounded slice of the workload on the host: one layer x n_seqs."""
+    rng = np.random.default_rng(seed)
+    hq, hkv, d = w["hq"], w["hkv"], w["d"]
+    q = rng.standard_normal((n_seqs, hq, d)).astype(np.float32)
+    k = rng.standard_normal((n_seqs, hkv, ctx, d)).astype(np.float16)
+    v = rng.standard_normal((n_seqs, hkv, ctx, d)).astype(np.float16)
+    return q, k, v
+
+
+def cpu_baseline(w, budget_s: float = 15.0):
+    """The reference's NumPy decode SDPA (oracle port of models/adapters.py:1209-1229)
+    on one layer x 8 sequences at the workload's context, repeated for ~budget_s."""
+    from oracle.kv_oracle import sdpa_decode
+
+    n_seqs = 8
+    q, k, v = cpu_sample(w, n_seqs, w["ctx"])
+    if w["kv"] == "fp8_e4m3":
+        from oracle.kv_oracle import fp8_decode, fp8_encode
+
+        s = (np.abs(k.astype(np.float32)).max(axis=(2, 3), keepdims=True) / 448).astype(np.float32)
+        kc = fp8_encode(k.astype(np.float32) / s)
+        vc = fp8_encode(v.astype(np.float32) / s)
+    per_call_bytes = n_seqs * w["ctx"] * w["hkv"] * w["d"] * 2 * kv_bytes_per_elem(w["kv"])
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for b in range(n_seqs):
+            if w["kv"] == "fp8_e4m3":
+                kk = fp8_decode(kc[b]) * s[b]
+                vv = fp8_decode(vc[b]) * s[b]
+                sdpa_decode(q[b], kk, vv)
+            else:
+                sdpa_decode(q[b], k[b], v[b])
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    gbs = reps * per_call_bytes / el / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
+            or (os.cpu_count() or 1), "kind": "port",
+            "sample": f"1 layer x {n_seqs} seqs x ctx {w['ctx']} ({w['kv']} KV), {reps} reps in {el:.1f}s; "
+                      f"tok/s extrapolated to the full step = {w['batch'] * gbs * 1e9 / (w['layers'] * attn_bytes_per_launch(w)):.3f}"}
+
+
+def bench_reference(args, w, world, rank):
+    if rank != 0:
+        return None
+    steps = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(w, budget_s=args.cpu_seconds / max(1, args.steps))
+        if i >= args.warmup:
+            steps.append(r["value"])
+    val = float(np.mean(steps))
+    cores = os.cpu_count() or 1
+    return {
+        "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
+        "impl": "reference",
+        "value": round(val, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w["kv"],
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{args.workload}: reference NumPy decode SDPA on a bounded host sample",
+                   "global_batch": w["batch"], "seq_len": w["ctx"], "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"per step: 1 layer x 8 seqs x ctx {w['ctx']}, ~{args.cpu_seconds / max(1, args.steps):.1f}s"},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="olmoe")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            res = bench_reference(args, w, world, rank)
+        else:
+            res = bench_ours(args, w, world, rank, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

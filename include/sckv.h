@@ -1,0 +1,275 @@
+/*
+ * sckv.h — C ABI of the B200 paged KV-cache library (libsckv.so).
+ *
+ * Plain pointers, sizes and int status codes; no framework types. Every
+ * device-side call is asynchronous and ordered on the `stream` argument
+ * (a cudaStream_t passed as void*, NULL = legacy default stream). A pool
+ * handle is not thread-safe: callers serialise calls on one handle (the
+ * Python façade holds an RLock, as the reference arena does).
+ *
+ * Device layout of a pool (one allocation, element type = kv dtype):
+ *     data  [num_layers][max_pages][2 (K,V)][num_kv_heads][page_tokens][head_dim]
+ *     int8 scales  [num_layers][max_pages][2][num_kv_heads][page_tokens]   fp16
+ *     fp8  scales  [num_layers][max_pages][2][num_kv_heads]                fp32
+ * A page id therefore names the same 16-token slot in every layer, which is
+ * the reference's page: one id covers [L,1,H,16,D] of K and of V
+ * (native/native_engine.py:250-257).
+ *
+ * Status codes mirror the reference C ABI (native/synapcore_native.mm:45-49).
+ */
+#ifndef SCKV_H
+#define SCKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SCKV_API __attribute__((visibility("default")))
+#else
+#define SCKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (native/synapcore_native.mm:45-49 for 0, -1, -3, -4) ---- */
+#define SCKV_OK                 0
+#define SCKV_ERR_INVALID_ARG   -1
+#define SCKV_ERR_BOUNDS        -3   /* page id / block index / length out of range */
+#define SCKV_ERR_ALIGNMENT     -4
+#define SCKV_ERR_CUDA          -5   /* a CUDA runtime call failed */
+#define SCKV_ERR_POOL_EXHAUSTED -6  /* allocation needs more pages than exist */
+#define SCKV_ERR_TIMEOUT       -7   /* a bounded in-kernel wait gave up */
+#define SCKV_ERR_UNSUPPORTED   -8   /* dtype / head_dim combination not built */
+
+/* ---- element types ---- */
+#define SCKV_DTYPE_F16       0
+#define SCKV_DTYPE_BF16      1
+#define SCKV_DTYPE_INT8      2   /* reference int8 mode: per-(token,head) fp16 scale */
+#define SCKV_DTYPE_FP8_E4M3  3   /* per-(layer,page,K|V,head) fp32 scale = max|x|/448 */
+#define SCKV_DTYPE_F32       4   /* query / output / source type only */
+
+typedef struct sckv_pool sckv_pool;
+
+/* ========================================================================== */
+/* Pool lifetime                                                               */
+/* ========================================================================== */
+
+/* Byte sizes of the three device regions a pool needs.
+ * alloc_bytes covers the on-device allocator (free ring, LRU clocks,
+ * refcounts, control words, status word). */
+SCKV_API int sckv_pool_required_bytes(int num_layers, int num_kv_heads, int head_dim,
+                             int page_tokens, int64_t max_pages, int kv_dtype,
+                             size_t* data_bytes, size_t* scale_bytes,
+                             size_t* alloc_bytes);
+
+/* Allocate and zero a pool on `device` (cudaMalloc). Replaces the pool
+ * allocation of PagedKVArena.__init__ (native/native_engine.py:232-295).
+ * page_tokens must be 16 (PagedKVArena.PAGE_TOKENS, native_engine.py:230). */
+SCKV_API int sckv_pool_create(int num_layers, int num_kv_heads, int head_dim,
+                     int page_tokens, int64_t max_pages, int kv_dtype,
+                     int device, sckv_pool** out);
+
+/* Same, over caller-owned device memory of the sizes returned by
+ * sckv_pool_required_bytes (the library neither zeroes nor frees it except
+ * through sckv_alloc_reset, which initialises the allocator region). */
+SCKV_API int sckv_pool_wrap(int num_layers, int num_kv_heads, int head_dim,
+                   int page_tokens, int64_t max_pages, int kv_dtype,
+                   int device, void* data, void* scales, void* alloc_state,
+                   sckv_pool** out);
+
+/* Release a pool (frees memory only if sckv_pool_create allocated it).
+ * Replaces PagedKVArena.clear's pool drop (native/native_engine.py:421-432). */
+SCKV_API void sckv_pool_destroy(sckv_pool* pool);
+
+/* Device pointers of the pool regions (for zero-copy host views). */
+SCKV_API int sckv_pool_pointers(const sckv_pool* pool, void** data, void** scales,
+                       void** alloc_state);
+
+/* ========================================================================== */
+/* Kernel 1 — scatter-append through the block table                          */
+/* ========================================================================== */
+
+/* Append new K/V tokens of `n_seqs` sequences into their pages.
+ * Replaces the per-request concatenate-append of
+ * ModularAttentionEngine.forward_numpy (models/adapters.py:1194-1207).
+ *
+ * k_new, v_new : [n_layers][n_tokens][num_kv_heads][head_dim] of src_dtype
+ *                (F16 / BF16 / F32); tokens of sequence b occupy rows
+ *                cu_tokens[b] .. cu_tokens[b+1]-1, in position order.
+ * cu_tokens    : int32 [n_seqs+1] device, cu_tokens[0] = 0.
+ * start_pos    : int32 [n_seqs] device, position of the first new token.
+ * block_table  : int32 [n_seqs][bt_stride] device; entry j = page id of
+ *                positions 16j..16j+15 (only the first max_blocks are used).
+ * Writes pool layers layer0 .. layer0+n_layers-1. Pools of type INT8
+ * quantise per (token, head) exactly as quantize_kv_int8_numpy
+ * (native/native_engine.py:207-216); FP8 pools keep a per-page-head scale
+ * max|x|/448 that grows as tokens arrive (older codes of that page-head
+ * are re-encoded under the grown scale). */
+SCKV_API int sckv_append(sckv_pool* pool, int layer0, int n_layers,
+                const void* k_new, const void* v_new, int src_dtype,
+                int n_seqs, int n_tokens, const int32_t* cu_tokens,
+                const int32_t* start_pos, const int32_t* block_table,
+                int64_t bt_stride, int max_blocks, void* stream);
+
+/* Write whole pages: k_src/v_src are [n_pages][num_layers][num_kv_heads][16][head_dim]
+ * of src_dtype — the reference page layout [L,1,H,16,D] without its unit
+ * axis. Replaces the copy / quantise body of PagedKVArena.write_page_fp16
+ * (native/native_engine.py:339-359). */
+SCKV_API int sckv_write_pages(sckv_pool* pool, const int32_t* page_ids, int n_pages,
+                     const void* k_src, const void* v_src, int src_dtype,
+                     void* stream);
+
+/* Write int8 codes + fp16 scales: kq/vq [n][L][H][16][D] int8,
+ * ks/vs [n][L][H][16] fp16. INT8 pools store them as given; F16 pools store
+ * the dequantised fp16(q * f32(scale)). Replaces
+ * PagedKVArena.write_page_quantized (native/native_engine.py:361-386). */
+SCKV_API int sckv_write_pages_quantized(sckv_pool* pool, const int32_t* page_ids,
+                               int n_pages, const int8_t* kq, const void* ks,
+                               const int8_t* vq, const void* vs, void* stream);
+
+/* ========================================================================== */
+/* Kernel 2 — paged gather / compaction and copy-on-write page copy           */
+/* ========================================================================== */
+
+/* Gather pages, in list order, into contiguous
+ * out_k/out_v [n_layers][num_kv_heads][n_tokens][head_dim] of out_dtype
+ * (F16 / BF16 / F32), token t taken from page page_ids[t/16] slot t%16;
+ * n_tokens <= 16*n_pages. INT8 / FP8 pools are dequantised
+ * (dequantize_kv_int8_numpy, native/native_engine.py:219-221).
+ * Replaces PagedKVArena.gather_contiguous_kv_numpy and read_page_fp16
+ * (native/native_engine.py:388-419). */
+SCKV_API int sckv_gather(sckv_pool* pool, int layer0, int n_layers,
+                const int32_t* page_ids, int n_pages, int n_tokens,
+                void* out_k, void* out_v, int out_dtype, void* stream);
+
+/* Copy pages src_ids[i] -> dst_ids[i] in every layer, K, V and scales.
+ * The device half of a copy-on-write fork: replaces the eager per-layer
+ * copy of a matched prefix in ContinuousBatchScheduler._prefill_request_numpy
+ * (engine/scheduler.py:150-152). */
+SCKV_API int sckv_copy_pages(sckv_pool* pool, const int32_t* src_ids,
+                    const int32_t* dst_ids, int n_pages, void* stream);
+
+/* ========================================================================== */
+/* Kernels 3+4 — paged decode attention (split-K), fused FP8 dequant          */
+/* ========================================================================== */
+
+/* Bytes of scratch sckv_decode_attn needs for these sizes (split partials). */
+SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
+                                   int num_q_heads, int max_blocks,
+                                   int chunk_pages);
+
+/* One query token per sequence: out[b][hq] = softmax(scale * q[b][hq] . K^T) V
+ * over the first ctx_lens[b] tokens of sequence b in layer `layer`, with
+ * q head hq reading kv head hq / (num_q_heads / num_kv_heads).
+ * Replaces the SDPA of ModularAttentionEngine.forward_numpy
+ * (models/adapters.py:1209-1229; GQA repeat at :1211-1215, scale at :1121).
+ *
+ * q   : [n_seqs][num_q_heads][head_dim] of q_dtype (F16 / BF16 / F32)
+ * out : [n_seqs][num_q_heads][head_dim] of out_dtype (F16 / BF16 / F32)
+ * chunk_pages : pages per split (split-K unit); <= 0 picks one.
+ * workspace   : device scratch of sckv_decode_workspace_bytes bytes.
+ * Pool dtypes F16, BF16, FP8_E4M3; accumulation is fp32. */
+SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype,
+                     int num_q_heads, const int32_t* block_table,
+                     int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
+                     int n_seqs, float scale, void* out, int out_dtype,
+                     void* workspace, size_t workspace_bytes, int chunk_pages,
+                     void* stream);
+
+/* ========================================================================== */
+/* Kernel 5 — on-device free list allocator and LRU eviction                  */
+/* ========================================================================== */
+/* The allocator restates PagedKVArena's bookkeeping on the device
+ * (native/native_engine.py:289-337): a FIFO free ring initialised to
+ * 0..max_pages-1, a step clock, a last-used clock per page, and LRU victim
+ * choice (smallest last-used) when the ring is empty. Pages with a nonzero
+ * pin count are never victims. */
+
+/* Reset: ring = 0..P-1, clock = 0, all pages free, counters 0. */
+SCKV_API int sckv_alloc_reset(sckv_pool* pool, void* stream);
+
+/* Allocate n pages in order, as n successive _allocate_page_slot_unlocked
+ * calls for new keys (native/native_engine.py:318-337): each takes the ring
+ * head, else evicts the least recently used unpinned allocated page; the
+ * clock advances by one per page and the page's last-used becomes the clock.
+ * out_ids[i] = page id; out_victims[i] = evicted page id or -1 (may be NULL).
+ * If pin != 0 the pages start with pin count 1. Fails with
+ * SCKV_ERR_POOL_EXHAUSTED (status word) if fewer than n pages can be had. */
+SCKV_API int sckv_alloc_pages(sckv_pool* pool, int n, int pin, int32_t* out_ids,
+                     int32_t* out_victims, void* stream);
+
+/* Return pages to the ring tail (FIFO), as PagedKVArena.evict_prefix_hash
+ * (native/native_engine.py:307-316). Unallocated ids are skipped. */
+SCKV_API int sckv_free_pages(sckv_pool* pool, const int32_t* ids, int n, void* stream);
+
+/* Touch pages in order, as n successive lookup_page_id calls
+ * (native/native_engine.py:297-305): clock += 1 each; a valid id's last-used
+ * becomes the clock; an id of -1 is a miss (clock only). */
+SCKV_API int sckv_touch_pages(sckv_pool* pool, const int32_t* ids, int n, void* stream);
+
+/* Add `delta` to the pin counts of pages (copy-on-write sharing). */
+SCKV_API int sckv_pin_pages(sckv_pool* pool, const int32_t* ids, int n, int delta,
+                   void* stream);
+
+/* Evict the n least recently used unpinned allocated pages to the ring
+ * tail, oldest first; out_ids (may be NULL) receives them, -1 padded. */
+SCKV_API int sckv_evict_lru(sckv_pool* pool, int n, int32_t* out_ids, void* stream);
+
+/* Decode-step page reservation, fully on device: for b in 0..n_seqs-1 in
+ * order, if ctx_lens[b] % 16 == 0 a page is allocated (as sckv_alloc_pages,
+ * pinned) into block_table[b][ctx_lens[b]/16]; then ctx_lens[b] += 1. */
+SCKV_API int sckv_reserve_decode(sckv_pool* pool, int32_t* block_table,
+                        int64_t bt_stride, int max_blocks, int32_t* ctx_lens,
+                        int n_seqs, void* stream);
+
+/* Read allocator counters (synchronises `stream`):
+ * out[0] ring head, out[1] ring tail (free = tail-head), out[2] step clock,
+ * out[3] evictions, out[4] allocated pages. */
+SCKV_API int sckv_alloc_state(const sckv_pool* pool, int64_t out[5], void* stream);
+
+/* ========================================================================== */
+/* Status word                                                                 */
+/* ========================================================================== */
+/* Kernels never trap; they record the first error in a device status word:
+ * out[0] code (SCKV_ERR_*), out[1] detail (offending index / value),
+ * out[2] kernel id, out[3] count of errors. Synchronises `stream`. */
+SCKV_API int sckv_get_status(const sckv_pool* pool, int32_t out[4], void* stream);
+SCKV_API int sckv_clear_status(sckv_pool* pool, void* stream);
+
+/* ========================================================================== */
+/* KV prefix hash table (host, C++)                                            */
+/* ========================================================================== */
+/* Open-addressed 1024-slot table of 80-byte slots, laid out exactly as the
+ * reference's NativeKVPrefixSlot {u8 prefix_hash[32]; u8 parent_hash[32];
+ * u32 occupied; u32 token_end; f64 created_at} (native/synapcore_native.mm:
+ * 93-100), operating on caller memory `table` (1024*80 bytes; e.g. the KV
+ * region of an index file mapping). Home slot = u32le(hash[0:4]) & 1023,
+ * 64 linear probes. */
+
+/* Replaces synapcore_native_kv_lookup (native/synapcore_native.mm:716-734):
+ * 1 if present (out_token_end set when non-NULL), else 0. */
+SCKV_API int sckv_kv_lookup(const uint8_t* table, const uint8_t* prefix_hash32,
+                   uint32_t* out_token_end);
+
+/* Replaces synapcore_native_kv_insert (native/synapcore_native.mm:736-780):
+ * 1 = stored in an empty or equal slot; 2 = overwrote the probe window's
+ * oldest created_at slot, whose hash goes to out_evicted_hash32 (if not
+ * NULL) and *evictions is incremented (if not NULL); SCKV_ERR_INVALID_ARG on
+ * NULL table/hash. */
+SCKV_API int sckv_kv_insert(uint8_t* table, const uint8_t* prefix_hash32,
+                   const uint8_t* parent_hash32, uint32_t token_end,
+                   double timestamp, uint8_t* out_evicted_hash32,
+                   uint64_t* evictions);
+
+/* ========================================================================== */
+/* Misc                                                                        */
+/* ========================================================================== */
+SCKV_API const char* sckv_version(void);
+SCKV_API const char* sckv_status_string(int code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SCKV_H */

@@ -1,0 +1,282 @@
+"""Device page pool: torch-owned HBM regions driven through the libsckv C ABI.
+
+`KVPool` owns three device regions (page data, quantisation scales, allocator
+state) allocated by torch and handed to the library with `sckv_pool_wrap`.
+All methods take device tensors and launch on the current torch stream;
+nothing here synchronises except the explicit status / state readers.
+
+Layout: data[layer][page][K|V][kv_head][16][head_dim]; a page id names the
+same 16-token slot in every layer, as the reference's all-layer page does
+(native/native_engine.py:250-257).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _native as N
+
+PAGE_TOKENS = 16
+
+DTYPE_CODES = {
+    "fp16": N.DTYPE_F16,
+    "bf16": N.DTYPE_BF16,
+    "int8": N.DTYPE_INT8,
+    "fp8_e4m3": N.DTYPE_FP8_E4M3,
+}
+TORCH_POOL_DTYPE = {
+    "fp16": torch.float16,
+    "bf16": torch.bfloat16,
+    "int8": torch.int8,
+    "fp8_e4m3": torch.uint8,
+}
+_TORCH_TO_CODE = {torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16, torch.float32: N.DTYPE_F32}
+
+
+def torch_dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _TORCH_TO_CODE[dt]
+    except KeyError:
+        raise TypeError(f"unsupported tensor dtype {dt}; expected float16, bfloat16 or float32") from None
+
+
+def _stream_ptr(stream: Optional[torch.cuda.Stream]) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _dev_i32(x, device) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        t = x.to(device=device, dtype=torch.int32)
+    else:
+        t = torch.as_tensor(x, dtype=torch.int32, device=device)
+    return t.contiguous()
+
+
+class KVPool:
+    """One page pool on one GPU."""
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_pages: int,
+                 kv_dtype: str = "fp16", device: Optional[torch.device] = None):
+        if kv_dtype not in DTYPE_CODES:
+            raise ValueError(f"kv_dtype must be one of {sorted(DTYPE_CODES)}, got {kv_dtype!r}")
+        self.lib = N.lib()
+        self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
+        if self.device.type != "cuda":
+            raise ValueError("KVPool lives in GPU memory; pass a cuda device")
+        self.num_layers, self.num_kv_heads, self.head_dim = int(num_layers), int(num_kv_heads), int(head_dim)
+        self.max_pages = int(max_pages)
+        self.kv_dtype = kv_dtype
+        self.code = DTYPE_CODES[kv_dtype]
+        data_b, scale_b, alloc_b = N.required_bytes(self.num_layers, self.num_kv_heads, self.head_dim, PAGE_TOKENS,
+                                                    self.max_pages, self.code)
+        with torch.cuda.device(self.device):
+            self.data = torch.zeros(data_b, dtype=torch.uint8, device=self.device)
+            self.scales = torch.zeros(max(scale_b, 16), dtype=torch.uint8, device=self.device) if scale_b else None
+            self.alloc_state = torch.zeros(alloc_b, dtype=torch.uint8, device=self.device)
+            h = ctypes.c_void_p()
+            N.check(self.lib.sckv_pool_wrap(self.num_layers, self.num_kv_heads, self.head_dim, PAGE_TOKENS,
+                                            self.max_pages, self.code, self.device.index, self.data.data_ptr(),
+                                            _ptr(self.scales), self.alloc_state.data_ptr(), ctypes.byref(h)),
+                    "sckv_pool_wrap")
+            self.handle = h
+            self.alloc_reset()
+        self._workspace: Optional[torch.Tensor] = None
+
+    # ------------------------------------------------------------------ views
+    @property
+    def bytes_per_page(self) -> int:
+        """Bytes one page id occupies across all layers (data + scales)."""
+        el = 2 if self.kv_dtype in ("fp16", "bf16") else 1
+        b = 2 * self.num_layers * self.num_kv_heads * PAGE_TOKENS * self.head_dim * el
+        if self.kv_dtype == "int8":
+            b += 2 * self.num_layers * self.num_kv_heads * PAGE_TOKENS * 2
+        elif self.kv_dtype == "fp8_e4m3":
+            b += 2 * self.num_layers * self.num_kv_heads * 4
+        return b
+
+    def pool_view(self) -> torch.Tensor:
+        """[L, P, 2, H, 16, D] view of the page data (pool element type)."""
+        shape = (self.num_layers, self.max_pages, 2, self.num_kv_heads, PAGE_TOKENS, self.head_dim)
+        return self.data.view(TORCH_POOL_DTYPE[self.kv_dtype]).view(shape)
+
+    def scale_view(self) -> Optional[torch.Tensor]:
+        if self.kv_dtype == "int8":
+            n = self.num_layers * self.max_pages * 2 * self.num_kv_heads * PAGE_TOKENS
+            return self.scales[: n * 2].view(torch.float16).view(
+                self.num_layers, self.max_pages, 2, self.num_kv_heads, PAGE_TOKENS)
+        if self.kv_dtype == "fp8_e4m3":
+            n = self.num_layers * self.max_pages * 2 * self.num_kv_heads
+            return self.scales[: n * 4].view(torch.float32).view(self.num_layers, self.max_pages, 2,
+                                                                  self.num_kv_heads)
+        return None
+
+    # ---------------------------------------------------------------- kernel 1
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, cu_tokens: torch.Tensor, start_pos: torch.Tensor,
+               block_table: torch.Tensor, layer0: int = 0, max_blocks: Optional[int] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> None:
+        """k_new, v_new: [n_layers, n_tokens, H, D] (or [n_tokens, H, D] for one layer)."""
+        if k_new.dim() == 3:
+            k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+        nl, nt = k_new.shape[0], k_new.shape[1]
+        n_seqs = cu_tokens.numel() - 1
+        bt = block_table if block_table.dim() == 2 else block_table.view(1, -1)
+        mb = bt.shape[1] if max_blocks is None else int(max_blocks)
+        N.check(self.lib.sckv_append(self.handle, layer0, nl, k_new.data_ptr(), v_new.data_ptr(),
+                                     torch_dtype_code(k_new.dtype), n_seqs, nt, cu_tokens.data_ptr(),
+                                     start_pos.data_ptr(), bt.data_ptr(), bt.stride(0), mb, _stream_ptr(stream)),
+                "sckv_append")
+
+    def write_pages(self, page_ids: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        """k_src, v_src: [n, L, H, 16, D] float16 / bfloat16 / float32."""
+        k_src, v_src = k_src.contiguous(), v_src.contiguous()
+        N.check(self.lib.sckv_write_pages(self.handle, page_ids.data_ptr(), page_ids.numel(), k_src.data_ptr(),
+                                          v_src.data_ptr(), torch_dtype_code(k_src.dtype), _stream_ptr(stream)),
+                "sckv_write_pages")
+
+    def write_pages_quantized(self, page_ids: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor,
+                              vs: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """kq/vq int8 [n, L, H, 16, D]; ks/vs float16 [n, L, H, 16]."""
+        kq, ks, vq, vs = (t.contiguous() for t in (kq, ks, vq, vs))
+        N.check(self.lib.sckv_write_pages_quantized(self.handle, page_ids.data_ptr(), page_ids.numel(),
+                                                    kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
+                                                    _stream_ptr(stream)),
+                "sckv_write_pages_quantized")
+
+    # ---------------------------------------------------------------- kernel 2
+    def gather(self, page_ids: torch.Tensor, n_tokens: Optional[int] = None, layer0: int = 0,
+               n_layers: Optional[int] = None, out_dtype: torch.dtype = torch.float16,
+               out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Contiguous [n_layers, H, n_tokens, D] K and V of the listed pages."""
+        n_pages = page_ids.numel()
+        nt = n_pages * PAGE_TOKENS if n_tokens is None else int(n_tokens)
+        nl = self.num_layers - layer0 if n_layers is None else int(n_layers)
+        shape = (nl, self.num_kv_heads, nt, self.head_dim)
+        if out is None:
+            ok = torch.empty(shape, dtype=out_dtype, device=self.device)
+            ov = torch.empty(shape, dtype=out_dtype, device=self.device)
+        else:
+            ok, ov = out
+        N.check(self.lib.sckv_gather(self.handle, layer0, nl, page_ids.data_ptr(), n_pages, nt, ok.data_ptr(),
+                                     ov.data_ptr(), torch_dtype_code(ok.dtype), _stream_ptr(stream)),
+                "sckv_gather")
+        return ok, ov
+
+    def copy_pages(self, src_ids: torch.Tensor, dst_ids: torch.Tensor,
+                   stream: Optional[torch.cuda.Stream] = None) -> None:
+        N.check(self.lib.sckv_copy_pages(self.handle, src_ids.data_ptr(), dst_ids.data_ptr(), src_ids.numel(),
+                                         _stream_ptr(stream)), "sckv_copy_pages")
+
+    # -------------------------------------------------------------- kernels 3+4
+    def decode_workspace_bytes(self, n_seqs: int, num_q_heads: int, max_blocks: int, chunk_pages: int = 0) -> int:
+        return int(self.lib.sckv_decode_workspace_bytes(self.handle, n_seqs, num_q_heads, max_blocks, chunk_pages))
+
+    def decode_attn(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor,
+                    scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                    out_dtype: Optional[torch.dtype] = None, max_blocks: Optional[int] = None,
+                    chunk_pages: int = 0, workspace: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """q [B, Hq, D] -> out [B, Hq, D]: softmax(scale q K^T) V over each
+        sequence's first ctx_lens[b] tokens of `layer`."""
+        q = q.contiguous()
+        B, hq, d = q.shape
+        mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
+        if scale is None:
+            scale = float(d) ** -0.5
+        if out is None:
+            out = torch.empty((B, hq, d), dtype=out_dtype or q.dtype, device=self.device)
+        need = self.decode_workspace_bytes(B, hq, mb, chunk_pages)
+        if workspace is None:
+            if self._workspace is None or self._workspace.numel() < need:
+                self._workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=self.device)
+            workspace = self._workspace
+        N.check(self.lib.sckv_decode_attn(self.handle, layer, q.data_ptr(), torch_dtype_code(q.dtype), hq,
+                                          block_table.data_ptr(), block_table.stride(0), mb, ctx_lens.data_ptr(), B,
+                                          float(scale), out.data_ptr(), torch_dtype_code(out.dtype),
+                                          workspace.data_ptr(), workspace.numel(), chunk_pages, _stream_ptr(stream)),
+                "sckv_decode_attn")
+        return out
+
+    # ---------------------------------------------------------------- kernel 5
+    def alloc_reset(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        N.check(self.lib.sckv_alloc_reset(self.handle, _stream_ptr(stream)), "sckv_alloc_reset")
+
+    def alloc_pages(self, n: int, pin: bool = False, stream: Optional[torch.cuda.Stream] = None
+                    ) -> Tuple[torch.Tensor, torch.Tensor]:
+        ids = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
+        vic = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
+        N.check(self.lib.sckv_alloc_pages(self.handle, n, 1 if pin else 0, ids.data_ptr(), vic.data_ptr(),
+                                          _stream_ptr(stream)), "sckv_alloc_pages")
+        return ids[:n], vic[:n]
+
+    def free_pages(self, ids: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> None:
+        ids = _dev_i32(ids, self.device)
+        N.check(self.lib.sckv_free_pages(self.handle, ids.data_ptr(), ids.numel(), _stream_ptr(stream)),
+                "sckv_free_pages")
+
+    def touch_pages(self, ids: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> None:
+        ids = _dev_i32(ids, self.device)
+        N.check(self.lib.sckv_touch_pages(self.handle, ids.data_ptr(), ids.numel(), _stream_ptr(stream)),
+                "sckv_touch_pages")
+
+    def pin_pages(self, ids: torch.Tensor, delta: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+        ids = _dev_i32(ids, self.device)
+        N.check(self.lib.sckv_pin_pages(self.handle, ids.data_ptr(), ids.numel(), int(delta), _stream_ptr(stream)),
+                "sckv_pin_pages")
+
+    def evict_lru(self, n: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        out = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
+        N.check(self.lib.sckv_evict_lru(self.handle, n, out.data_ptr(), _stream_ptr(stream)), "sckv_evict_lru")
+        return out[:n]
+
+    def reserve_decode(self, block_table: torch.Tensor, ctx_lens: torch.Tensor, n_seqs: Optional[int] = None,
+                       max_blocks: Optional[int] = None, stream: Optional[torch.cuda.Stream] = None) -> None:
+        n = ctx_lens.numel() if n_seqs is None else int(n_seqs)
+        mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
+        N.check(self.lib.sckv_reserve_decode(self.handle, block_table.data_ptr(), block_table.stride(0), mb,
+                                             ctx_lens.data_ptr(), n, _stream_ptr(stream)), "sckv_reserve_decode")
+
+    def alloc_state(self, stream: Optional[torch.cuda.Stream] = None) -> Dict[str, int]:
+        arr = (ctypes.c_int64 * 5)()
+        N.check(self.lib.sckv_alloc_state(self.handle, arr, _stream_ptr(stream)), "sckv_alloc_state")
+        head, tail, clock, ev, alloc = (int(x) for x in arr)
+        return {"head": head, "tail": tail, "free": tail - head, "clock": clock, "evictions": ev,
+                "allocated": alloc}
+
+    # ------------------------------------------------------------ status word
+    def status(self, stream: Optional[torch.cuda.Stream] = None) -> Tuple[int, int, int, int]:
+        arr = (ctypes.c_int32 * 4)()
+        N.check(self.lib.sckv_get_status(self.handle, arr, _stream_ptr(stream)), "sckv_get_status")
+        return int(arr[0]), int(arr[1]), int(arr[2]), int(arr[3])
+
+    def clear_status(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        N.check(self.lib.sckv_clear_status(self.handle, _stream_ptr(stream)), "sckv_clear_status")
+
+    def raise_on_status(self) -> None:
+        code, detail, kernel, count = self.status()
+        if code != N.SCKV_OK:
+            self.clear_status()
+            err = N.SCKVPoolExhausted if code == N.SCKV_ERR_POOL_EXHAUSTED else (
+                N.SCKVBoundsError if code == N.SCKV_ERR_BOUNDS else N.SCKVError)
+            e = err(code, f"device status (kernel {kernel}, detail {detail}, {count} errors)")
+            raise e
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.sckv_pool_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,134 @@
+"""Kernels 3+4: paged decode attention against the oracle SDPA.
+
+Tolerance (fp32 accumulation): max|o - o_ref| / max|o_ref| <= 2e-3 per
+sequence, with o_ref the reference SDPA (models/adapters.py:1209-1229) run
+on the oracle's gather of the same pages. For FP8 pools o_ref runs on the
+dequantised pages (codes * per-page scale), so the 2e-3 bound covers the
+kernel; the FP8-vs-bf16 quantisation error is reported separately.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle.kv_oracle import PAGE_TOKENS, PagedPoolOracle, bf16_bits_to_f32, sdpa_decode
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def _rel_err(o, r):
+    return float(np.max(np.abs(o - r)) / max(np.max(np.abs(r)), 1e-30))
+
+
+def _make_case(cuda_device, kv_dtype, hq, hkv, ctx_lens, pool_pages, seed, layers=2, kv_scale=None):
+    from synapcore_b200.pool import KVPool
+
+    rng = np.random.default_rng(seed)
+    D = 128
+    pool = KVPool(layers, hkv, D, pool_pages, kv_dtype, device=cuda_device)
+    ora = PagedPoolOracle(layers, hkv, D, pool_pages, kv_dtype)
+    # fill every page with N(0,1) (times a per-head factor) through write_pages
+    k = rng.standard_normal((pool_pages, layers, hkv, PAGE_TOKENS, D)).astype(np.float32)
+    v = rng.standard_normal((pool_pages, layers, hkv, PAGE_TOKENS, D)).astype(np.float32)
+    if kv_scale is not None:
+        f = rng.uniform(kv_scale[0], kv_scale[1], size=(1, layers, hkv, 1, 1)).astype(np.float32)
+        k *= f
+        v *= f
+    src_t = torch.float16 if kv_dtype in ("fp16", "int8") else torch.bfloat16
+    k_t = torch.from_numpy(k).to(src_t)
+    v_t = torch.from_numpy(v).to(src_t)
+    ids = np.arange(pool_pages, dtype=np.int32)
+    pool.write_pages(torch.from_numpy(ids).to(cuda_device), k_t.to(cuda_device), v_t.to(cuda_device))
+    ora.write_pages(ids, k_t.float().numpy(), v_t.float().numpy())
+    B = len(ctx_lens)
+    max_blocks = max(1, max((c + PAGE_TOKENS - 1) // PAGE_TOKENS for c in ctx_lens))
+    bt = np.zeros((B, max_blocks), np.int32)
+    for b in range(B):
+        bt[b] = rng.choice(pool_pages, size=max_blocks, replace=False)
+    q = rng.standard_normal((B, hq, D)).astype(np.float32)
+    return pool, ora, bt, q
+
+
+@pytest.mark.parametrize("kv_dtype,hq,hkv,qdt", [
+    ("fp16", 16, 16, torch.float16),
+    ("fp16", 8, 2, torch.float16),
+    ("bf16", 32, 8, torch.bfloat16),
+    ("bf16", 8, 8, torch.float32),
+    ("fp8_e4m3", 32, 8, torch.bfloat16),
+    ("fp8_e4m3", 16, 16, torch.float16),
+    ("fp16", 16, 2, torch.float16),
+])
+@pytest.mark.parametrize("chunk_pages", [0, 3])
+def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages):
+    ctx = [1, 15, 16, 17, 100, 333, 1024, 513]
+    pool, ora, bt, q = _make_case(cuda_device, kv_dtype, hq, hkv, ctx, pool_pages=200, seed=11,
+                                  kv_scale=(0.5, 4.0) if kv_dtype == "fp8_e4m3" else None)
+    q_t = torch.from_numpy(q).to(qdt)
+    qv = q_t.float().numpy()
+    bt_d = torch.from_numpy(bt).to(cuda_device)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+    for layer in range(pool.num_layers):
+        out = pool.decode_attn(layer, q_t.to(cuda_device), bt_d, ctx_d, out_dtype=torch.float32,
+                               chunk_pages=chunk_pages)
+        torch.cuda.synchronize()
+        ref = ora.decode(layer, qv, bt, np.array(ctx))
+        got = out.cpu().numpy()
+        for b in range(len(ctx)):
+            assert _rel_err(got[b], ref[b]) <= TOL, (layer, b, _rel_err(got[b], ref[b]))
+    assert pool.status()[0] == 0
+    pool.close()
+
+
+def test_decode_low_precision_output(cuda_device):
+    """bf16 / fp16 outputs equal the fp32 result rounded once."""
+    ctx = [40, 300, 77]
+    pool, ora, bt, q = _make_case(cuda_device, "bf16", 16, 4, ctx, pool_pages=64, seed=5, layers=1)
+    q_t = torch.from_numpy(q).to(torch.bfloat16).to(cuda_device)
+    bt_d = torch.from_numpy(bt).to(cuda_device)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+    o32 = pool.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.float32)
+    o16 = pool.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(o32.to(torch.bfloat16), o16)
+    pool.close()
+
+
+def test_decode_zero_length_sequence_outputs_zero(cuda_device):
+    ctx = [0, 20, 0]
+    pool, ora, bt, q = _make_case(cuda_device, "fp16", 16, 16, [16, 20, 16], pool_pages=16, seed=9, layers=1)
+    q_t = torch.from_numpy(q).to(torch.float16).to(cuda_device)
+    out = pool.decode_attn(0, q_t, torch.from_numpy(bt).to(cuda_device),
+                           torch.tensor(ctx, dtype=torch.int32, device=cuda_device), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    o = out.cpu().numpy()
+    assert np.all(o[0] == 0) and np.all(o[2] == 0)
+    ref = ora.decode(0, q_t.float().cpu().numpy(), bt, np.array(ctx))
+    assert _rel_err(o[1], ref[1]) <= TOL
+    pool.close()
+
+
+def test_fp8_quantisation_error_bound(cuda_device):
+    """FP8 pages vs the bf16 pages they encode: per-element error <= 2^-4
+    relative to the page-head max (half-ulp of a 3-bit mantissa at the top
+    binade), and attention output within 5% relative of the bf16 result."""
+    ctx = [512, 1000]
+    pool8, ora8, bt, q = _make_case(cuda_device, "fp8_e4m3", 32, 8, ctx, pool_pages=96, seed=21, layers=1,
+                                    kv_scale=(0.5, 4.0))
+    poolb, orab, _, _ = _make_case(cuda_device, "bf16", 32, 8, ctx, pool_pages=96, seed=21, layers=1,
+                                   kv_scale=(0.5, 4.0))
+    for page in range(96):
+        for kv in range(2):
+            x8 = ora8.values(0, page, kv)
+            xb = orab.values(0, page, kv)
+            amax = np.max(np.abs(xb), axis=(1, 2), keepdims=True)
+            assert np.all(np.abs(x8 - xb) <= amax * 2.0 ** -4 + 1e-12)
+    q_t = torch.from_numpy(q).to(torch.bfloat16).to(cuda_device)
+    bt_d = torch.from_numpy(bt).to(cuda_device)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+    o8 = pool8.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
+    ob = poolb.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
+    for b in range(len(ctx)):
+        assert _rel_err(o8[b], ob[b]) <= 0.05
+    pool8.close()
+    poolb.close()
