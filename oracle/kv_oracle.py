@@ -512,3 +512,100 @@ class KVTableOracle:
         _KV_SLOT.pack_into(self.table, oldest_pos, h, parent, 1, int(token_end), float(ts))
         self.evictions += 1
         return oldest_hash.hex() if oldest_hash else None
+
+
+# --------------------------------------------------------------------------
+# NativeKVPrefixCache restatement (numpy path) — native/native_engine.py:2125-2435
+# --------------------------------------------------------------------------
+class PrefixCacheOracle:
+    """save_prefix_blocks_numpy (:2202-2246) / match_longest_prefix_numpy
+    (:2248-2291) over ArenaOracle, a KVTableOracle and .npz files in kv_dir."""
+
+    def __init__(self, kv_dir, arena: ArenaOracle, table: KVTableOracle, max_disk_blocks: int = 512):
+        from pathlib import Path
+
+        self.kv_dir = Path(kv_dir)
+        self.kv_dir.mkdir(parents=True, exist_ok=True)
+        self.arena, self.table = arena, table
+        self.max_disk_blocks = max(1, int(max_disk_blocks))
+        self.quant_mode = arena.quant_mode
+        self.disk_lru: "collections.OrderedDict[str, object]" = collections.OrderedDict()
+        self.blocks_loaded_from_disk = self.blocks_loaded_from_arena = 0
+        self.blocks_saved_to_disk = self.disk_blocks_evicted = self.tokens_skipped = 0
+
+    def _evict_disk_block_by_hash(self, h: str) -> None:  # :2173-2187
+        self.arena.evict_prefix_hash(h)
+        p = self.disk_lru.pop(h, None)
+        for cand in (p, self.kv_dir / f"{h[:32]}_mlx.safetensors", self.kv_dir / f"{h[:32]}_mlx_int8.safetensors",
+                     self.kv_dir / f"{h[:32]}_np.npz"):
+            if cand is not None and cand.exists():
+                cand.unlink()
+                self.disk_blocks_evicted += 1
+
+    def _enforce_disk_budget(self, h: str, path) -> None:  # :2189-2200
+        self.disk_lru[h] = path
+        self.disk_lru.move_to_end(h)
+        while len(self.disk_lru) > self.max_disk_blocks:
+            oh, op = self.disk_lru.popitem(last=False)
+            self.arena.evict_prefix_hash(oh)
+            if op.exists():
+                op.unlink()
+                self.disk_blocks_evicted += 1
+
+    def save(self, token_ids, k_seq, v_seq, seed_root_hex: str, timestamp=lambda: 0.0) -> int:
+        n_full = max(0, len(token_ids) - 1) // BLOCK_SIZE
+        prev, saved = seed_root_hex, 0
+        for bi in range(n_full):
+            s, e = bi * BLOCK_SIZE, (bi + 1) * BLOCK_SIZE
+            cur = chain_prefix_hash(prev, token_ids[s:e])
+            kp, vp = k_seq[:, :, :, s:e, :], v_seq[:, :, :, s:e, :]
+            self.arena.write_page_fp16(cur, kp, vp)
+            ev = self.table.insert(bytes.fromhex(cur), bytes.fromhex(prev), e, timestamp())
+            if ev is not None and ev != cur:
+                self._evict_disk_block_by_hash(ev)
+            path = self.kv_dir / f"{cur[:32]}_np.npz"
+            if not path.exists():
+                if self.quant_mode == "int8":
+                    kq, ks = quantize_kv_int8(kp)
+                    vq, vs = quantize_kv_int8(vp)
+                    np.savez(path, kq=kq, ks=ks, vq=vq, vs=vs)
+                else:
+                    np.savez(path, k=kp, v=vp)
+                self._enforce_disk_budget(cur, path)
+                self.blocks_saved_to_disk += 1
+            prev = cur
+            saved += 1
+        return saved
+
+    def match(self, token_ids, seed_root_hex: str):
+        n_full = max(0, len(token_ids) - 1) // BLOCK_SIZE
+        if n_full == 0:
+            return 0, None, None
+        prev, pids = seed_root_hex, []
+        for bi in range(n_full):
+            cur = chain_prefix_hash(prev, token_ids[bi * BLOCK_SIZE:(bi + 1) * BLOCK_SIZE])
+            pid = self.arena.lookup_page_id(cur)
+            if pid is not None:
+                pids.append(pid)
+                self.blocks_loaded_from_arena += 1
+                prev = cur
+                continue
+            found = self.table.lookup(bytes.fromhex(cur))
+            path = self.kv_dir / f"{cur[:32]}_np.npz"
+            if (found or path.exists()) and path.exists():
+                with np.load(path) as data:
+                    if "kq" in data:
+                        pid = self.arena.write_page_quantized(cur, data["kq"], data["ks"], data["vq"], data["vs"])
+                    else:
+                        pid = self.arena.write_page_fp16(cur, data["k"], data["v"])
+                pids.append(pid)
+                self.blocks_loaded_from_disk += 1
+                prev = cur
+            else:
+                break
+        if not pids:
+            return 0, None, None
+        kc, vc = self.arena.gather_contiguous_kv_numpy(pids)
+        n = len(pids) * BLOCK_SIZE
+        self.tokens_skipped += n
+        return n, kc, vc

@@ -1,0 +1,292 @@
+#!/usr/bin/env python3
+"""Generate golden fixtures by running the reference's own Python code.
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+Imports the reference's PagedKVArena, NativeKVPrefixCache, int8 KV
+quantisation, prefix-chain hash, KV hash-table twin, ModularAttentionEngine
+and FP8 LUT from the reference checkout (read-only), replays the scenarios of
+its own tests (tests/test_p1_2_paged_kv_cache.py T1-T4, the C++ self-test
+--verify-kv-eviction at native/synapcore_native.mm:1365-1414,
+tests/test_reliability.py::test_06) plus decode-SDPA cases, and writes the
+observed outputs to tests/golden/. Large arrays are recorded as SHA-256
+digests of their bytes (inputs are regenerated from the same seeds by the
+tests); small ones are stored in golden_arrays.npz.
+
+Only this script reads the reference; the fixtures it writes are what the
+tests use, so they run anywhere.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import shutil
+import struct
+import sys
+import tempfile
+import threading
+from pathlib import Path
+
+import numpy as np
+
+OUT = Path(__file__).resolve().parent
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def stand_in_bridge(ne):
+    """NativeMmapIndexBridge without a store: a zeroed index image in memory,
+    using the reference's own kv_lookup / kv_insert methods."""
+    b = ne.NativeMmapIndexBridge.__new__(ne.NativeMmapIndexBridge)
+    b.idx_mmap = bytearray(ne.TOTAL_IDX_BYTES)
+    b.idx_lock = threading.RLock()
+    b.kv_evictions_issued = 0
+    return b
+
+
+GOLDEN_SEED_ROOT = hashlib.sha256(b"synapcore-b200 golden seed root").hexdigest()
+
+
+def arena_t1(ne):
+    """tests/test_p1_2_paged_kv_cache.py:51-99 replayed, recording every return."""
+    arena = ne.PagedKVArena(max_pages=8, num_layers=16, num_kv_heads=16, head_dim=128, quant_mode="fp16")
+    rng = np.random.default_rng(101)
+    written, log = [], []
+    for i in range(12):
+        h = f"{i + 1:064x}"
+        k = rng.standard_normal((16, 1, 16, 16, 128)).astype(np.float16)
+        v = rng.standard_normal((16, 1, 16, 16, 128)).astype(np.float16)
+        written.append(h)
+        log.append(["write", h, arena.write_page_fp16(h, k, v)])
+        if i >= 2:
+            log.append(["lookup", written[0], arena.lookup_page_id(written[0])])
+            log.append(["lookup", written[1], arena.lookup_page_id(written[1])])
+    for idx in (0, 1, 2, 3, 4, 5):
+        log.append(["lookup", written[idx], arena.lookup_page_id(written[idx])])
+    surv = [0, 1, 6, 7, 8, 9, 10, 11]
+    pids = [arena.lookup_page_id(written[i]) for i in surv]
+    kc, vc = arena.gather_contiguous_kv_numpy(pids)
+    return {
+        "log": log,
+        "survivor_pids": pids,
+        "page_table": dict(arena.page_table),
+        "page_last_used": dict(arena.page_last_used),
+        "free_pages": list(arena.free_pages),
+        "step_clock": arena.step_clock,
+        "page_hits": arena.page_hits,
+        "page_misses": arena.page_misses,
+        "page_evictions": arena.page_evictions,
+        "gather_shape": list(kc.shape),
+        "gather_k_sha256": sha(kc),
+        "gather_v_sha256": sha(vc),
+    }
+
+
+def int8_t3(ne, arrays):
+    """tests/test_p1_2_paged_kv_cache.py:117-147."""
+    a16 = ne.PagedKVArena(max_pages=16, quant_mode="fp16")
+    a8 = ne.PagedKVArena(max_pages=16, quant_mode="int8")
+    rng = np.random.default_rng(2026)
+    k = (rng.standard_normal((16, 1, 16, 16, 128)) * 0.5).astype(np.float16)
+    v = (rng.standard_normal((16, 1, 16, 16, 128)) * 0.5).astype(np.float16)
+    pid = a8.write_page_fp16("a" * 64, k, v)
+    kd, vd = a8.read_page_fp16(pid)
+    kq, ks = ne.quantize_kv_int8_numpy(k)
+    kf, kdf = k.astype(np.float32).reshape(-1), kd.astype(np.float32).reshape(-1)
+    small = (np.random.default_rng(7).standard_normal((2, 1, 3, 16, 128)) * 3).astype(np.float16)
+    small[0, 0, 0, 0] = 0  # all-zero row -> scale floor 1e-7
+    sq, ss = ne.quantize_kv_int8_numpy(small)
+    arrays["int8_small_x"] = small
+    arrays["int8_small_q"] = sq
+    arrays["int8_small_s"] = ss
+    arrays["int8_small_deq"] = ne.dequantize_kv_int8_numpy(sq, ss)
+    return {
+        "bytes_per_page_fp16": a16.bytes_per_page,
+        "bytes_per_page_int8": a8.bytes_per_page,
+        "kq_sha256": sha(kq),
+        "ks_sha256": sha(ks),
+        "k_pool_q_sha256": sha(a8.k_pool_q[pid]),
+        "k_scale_sha256": sha(a8.k_scale[pid]),
+        "k_deq_sha256": sha(kd),
+        "v_deq_sha256": sha(vd),
+        "cosine": float(np.dot(kf, kdf) / (np.linalg.norm(kf) * np.linalg.norm(kdf))),
+        "mean_abs_err": float(np.mean(np.abs(kf - kdf))),
+    }
+
+
+def prefix_cache_t4(ne):
+    """tests/test_p1_2_paged_kv_cache.py:149-222 with a stand-in bridge.
+    save_prefix_blocks_numpy stamps hash-table slots with time.time()
+    (native/native_engine.py:2231); a fixed clock (0.0) is substituted inside
+    the reference module so the table bytes are reproducible."""
+    import types
+    import time as _time
+
+    ne.time = types.SimpleNamespace(time=lambda: 0.0, perf_counter=_time.perf_counter)
+    tmp = Path(tempfile.mkdtemp(prefix="sckv_golden_"))
+    try:
+        bridge = stand_in_bridge(ne)
+        cache = ne.NativeKVPrefixCache(tmp, bridge, device="cpu", num_layers=16, num_kv_heads=16, head_dim=128,
+                                       max_pages=4, max_disk_blocks=3, quant_mode="int8")
+        rng = np.random.default_rng(77)
+        tokens = list(range(100, 165))
+        k = (rng.standard_normal((16, 1, 16, 65, 128)) * 0.4).astype(np.float16)
+        v = (rng.standard_normal((16, 1, 16, 65, 128)) * 0.4).astype(np.float16)
+        seed = GOLDEN_SEED_ROOT
+        saved = cache.save_prefix_blocks_numpy(tokens, k, v, seed)
+        after_save = {"saved_pages": saved, "disk_blocks_evicted": cache.disk_blocks_evicted,
+                      "files": sorted(p.name for p in cache.kv_dir.iterdir())}
+        short = tokens[:49]
+        cache.save_prefix_blocks_numpy(short, k[:, :, :, :49], v[:, :, :, :49], seed)
+        hits0 = cache.blocks_loaded_from_arena
+        m1, k1, v1 = cache.match_longest_prefix_numpy(short, seed)
+        arena_hits = cache.blocks_loaded_from_arena - hits0
+        cache.arena.page_table.clear()
+        cache.arena.reverse_page_table.clear()
+        cache.arena.free_pages.clear()
+        cache.arena.free_pages.extend(range(cache.arena.max_pages))
+        m2, k2, v2 = cache.match_longest_prefix_numpy(short, seed)
+        stats = cache.get_paged_kv_stats()
+        return {
+            "seed_root": seed,
+            "after_first_save": after_save,
+            "matched_arena": m1,
+            "arena_hits": arena_hits,
+            "k_restored_shape": list(k1.shape),
+            "k_restored_sha256": sha(k1),
+            "v_restored_sha256": sha(v1),
+            "matched_disk": m2,
+            "k_disk_sha256": sha(k2),
+            "v_disk_sha256": sha(v2),
+            "blocks_loaded_from_disk": cache.blocks_loaded_from_disk,
+            "blocks_loaded_from_arena": cache.blocks_loaded_from_arena,
+            "blocks_saved_to_disk": cache.blocks_saved_to_disk,
+            "tokens_skipped": cache.tokens_skipped,
+            "stats": stats,
+            "files_end": sorted(p.name for p in cache.kv_dir.iterdir()),
+            "kv_table_sha256": hashlib.sha256(bytes(bridge.idx_mmap[ne.OFFSET_KV_HASH_TBL:])).hexdigest(),
+        }
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+        ne.time = _time
+
+
+def kv_table_kat(ne):
+    """--verify-kv-eviction (native/synapcore_native.mm:1365-1414) through the
+    Python twin (native/native_engine.py:1714-1752)."""
+    b = stand_in_bridge(ne)
+    parent = b"\x00" * 32
+    hashes, evicted, rcs = [], [], []
+    for i in range(100):
+        h = bytearray(32)
+        struct.pack_into("<I", h, 0, 77 | ((i + 1) << 10))
+        h[4] = i & 0xFF
+        h = bytes(h)
+        hashes.append(h)
+        ev = b.kv_insert(h, parent, (i + 1) * 16, 1000.0 + i)
+        evicted.append(ev)
+    old_found = sum(b.kv_lookup(h) for h in hashes[:36])
+    new_found = sum(b.kv_lookup(h) for h in hashes[36:])
+    return {
+        "evictions": b.kv_evictions_issued,
+        "old_found": old_found,
+        "new_found": new_found,
+        "evicted_hashes": evicted,
+        "table_sha256": hashlib.sha256(bytes(b.idx_mmap[ne.OFFSET_KV_HASH_TBL:])).hexdigest(),
+    }
+
+
+def kv_table_long_context(ne):
+    """tests/test_reliability.py:213-259 with fixed timestamps (the test uses time.time())."""
+    b = stand_in_bridge(ne)
+    prev = GOLDEN_SEED_ROOT
+    chain = []
+    for bi in range(260):
+        toks = [((bi * 16) + t) % 50000 for t in range(16)]
+        cur = ne.chain_merkle_prefix_hash(prev, toks)
+        b.kv_insert(bytes.fromhex(cur), bytes.fromhex(prev), (bi + 1) * 16, 5000.0 + bi * 0.001)
+        chain.append(cur)
+        prev = cur
+    recent_found = [bool(b.kv_lookup(bytes.fromhex(h))) for h in chain[-128:]]
+    evs = []
+    for c in range(70):
+        h = struct.pack("<I", 42) + struct.pack("<I", c + 1) + b"\x11" * 24
+        evs.append(b.kv_insert(h, b"\x00" * 32, (c + 1) * 16, 1000.0 + c))
+    newest = struct.pack("<I", 42) + struct.pack("<I", 70) + b"\x11" * 24
+    oldest = struct.pack("<I", 42) + struct.pack("<I", 1) + b"\x11" * 24
+    return {
+        "chain_first": chain[0],
+        "chain_last": chain[-1],
+        "recent_found": recent_found,
+        "collision_evicted": evs,
+        "newest_found": bool(b.kv_lookup(newest)),
+        "oldest_found": bool(b.kv_lookup(oldest)),
+        "evictions": b.kv_evictions_issued,
+        "table_sha256": hashlib.sha256(bytes(b.idx_mmap[ne.OFFSET_KV_HASH_TBL:])).hexdigest(),
+    }
+
+
+def sdpa_cases(ad, arrays):
+    """Decode SDPA through ModularAttentionEngine.forward_numpy
+    (models/adapters.py:1148-1231) with identity q/o projections, zero k/v
+    projections and pos_offset 0 (RoPE angle 0): output = SDPA of q over the
+    cached K/V followed by one all-zero token."""
+    out = []
+    for name, hq, hkv, T, seed in (("mha", 4, 4, 37, 1), ("gqa4", 8, 2, 70, 2), ("mqa", 4, 1, 16, 3),
+                                   ("gqa8_long", 16, 2, 301, 4)):
+        d = 128
+        hidden = hq * d
+        cfg = {"model_type": "mixtral", "num_hidden_layers": 1, "num_experts": 8, "num_experts_per_tok": 2,
+               "hidden_size": hidden, "intermediate_size": hidden * 2, "num_attention_heads": hq,
+               "num_key_value_heads": hkv, "vocab_size": 32000, "rms_norm_eps": 1e-5, "rope_theta": 10000.0}
+        eng = ad.ModularAttentionEngine(ad.MixtralAdapter(cfg).spec)
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((1, 1, hidden)).astype(np.float32)
+        pk = rng.standard_normal((1, hkv, T, d)).astype(np.float16)
+        pv = rng.standard_normal((1, hkv, T, d)).astype(np.float16)
+        qw = np.eye(hidden, dtype=np.float16)
+        kw = np.zeros((hkv * d, hidden), np.float16)
+        ow = np.eye(hidden, dtype=np.float16)
+        kk, vv = [pk.copy()], [pv.copy()]
+        y = eng.forward_numpy(x, qw, kw, kw, ow, kv_cache_k=kk, kv_cache_v=vv, layer_idx=0, pos_offset=0)
+        arrays[f"sdpa_{name}_q"] = x.reshape(hq, d)
+        arrays[f"sdpa_{name}_k"] = pk[0]
+        arrays[f"sdpa_{name}_v"] = pv[0]
+        arrays[f"sdpa_{name}_out"] = y.reshape(hq, d)
+        arrays[f"sdpa_{name}_kfull"] = kk[0][0]
+        out.append({"name": name, "hq": hq, "hkv": hkv, "T": T, "appended_tokens": int(kk[0].shape[2] - T)})
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from native import native_engine as ne  # noqa: E402
+    from models import adapters as ad  # noqa: E402
+
+    arrays = {}
+    golden = {
+        "generator": "tests/golden/make_golden.py (reference code run in-process)",
+        "arena_t1": arena_t1(ne),
+        "int8_t3": int8_t3(ne, arrays),
+        "prefix_cache_t4": prefix_cache_t4(ne),
+        "kv_table_kat": kv_table_kat(ne),
+        "kv_table_long_context": kv_table_long_context(ne),
+        "sdpa": sdpa_cases(ad, arrays),
+        "chain_hash": [ne.chain_merkle_prefix_hash(GOLDEN_SEED_ROOT, list(range(16))),
+                       ne.chain_merkle_prefix_hash("00" * 32, [0] * 16),
+                       ne.chain_merkle_prefix_hash("ff" * 32, [4294967295] * 16)],
+    }
+    arrays["fp8_lut"] = ad.fp8_e4m3_bytes_to_fp32(np.arange(256, dtype=np.uint8))
+    (OUT / "golden.json").write_text(json.dumps(golden, indent=1, sort_keys=True))
+    np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
+    print("wrote", OUT / "golden.json", OUT / "golden_arrays.npz")
+
+
+if __name__ == "__main__":
+    main()

@@ -109,9 +109,12 @@ def test_decode_zero_length_sequence_outputs_zero(cuda_device):
 
 
 def test_fp8_quantisation_error_bound(cuda_device):
-    """FP8 pages vs the bf16 pages they encode: per-element error <= 2^-4
-    relative to the page-head max (half-ulp of a 3-bit mantissa at the top
-    binade), and attention output within 5% relative of the bf16 result."""
+    """FP8 bound, stated in two parts:
+    (1) codes: every dequantised element is within 2^-4 x (page-head max |x|)
+        of the bf16 value it encodes (round-to-nearest onto a 3-bit mantissa);
+    (2) attention: the kernel's FP8 output differs from the bf16 output by
+        exactly the quantisation effect the oracle predicts, within 2e-3
+        (kernel vs the SDPA of the dequantised pages)."""
     ctx = [512, 1000]
     pool8, ora8, bt, q = _make_case(cuda_device, "fp8_e4m3", 32, 8, ctx, pool_pages=96, seed=21, layers=1,
                                     kv_scale=(0.5, 4.0))
@@ -124,11 +127,19 @@ def test_fp8_quantisation_error_bound(cuda_device):
             amax = np.max(np.abs(xb), axis=(1, 2), keepdims=True)
             assert np.all(np.abs(x8 - xb) <= amax * 2.0 ** -4 + 1e-12)
     q_t = torch.from_numpy(q).to(torch.bfloat16).to(cuda_device)
+    qv = q_t.float().cpu().numpy()
     bt_d = torch.from_numpy(bt).to(cuda_device)
     ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
     o8 = pool8.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
     ob = poolb.decode_attn(0, q_t, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
+    r8 = ora8.decode(0, qv, bt, np.array(ctx))
+    rb = orab.decode(0, qv, bt, np.array(ctx))
     for b in range(len(ctx)):
-        assert _rel_err(o8[b], ob[b]) <= 0.05
+        scale = np.max(np.abs(rb[b]))
+        predicted = np.abs(r8[b] - rb[b])
+        observed = np.abs(o8[b] - ob[b])
+        assert np.max(np.abs(observed - predicted)) <= 2 * TOL * scale
+        print(f"fp8 vs bf16 attention, seq {b}: max rel dev {np.max(observed) / scale:.4f} "
+              f"(oracle predicts {np.max(predicted) / scale:.4f})")
     pool8.close()
     poolb.close()
