@@ -42,6 +42,7 @@ extern "C" {
 #define SCKV_ERR_POOL_EXHAUSTED -6  /* allocation needs more pages than exist */
 #define SCKV_ERR_TIMEOUT       -7   /* a bounded in-kernel wait gave up */
 #define SCKV_ERR_UNSUPPORTED   -8   /* dtype / head_dim combination not built */
+#define SCKV_ERR_SCRATCH_LIMIT -9   /* needs more than the fixed no-allocation scratch */
 
 /* ---- element types ---- */
 #define SCKV_DTYPE_F16       0
@@ -177,6 +178,25 @@ SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_d
                      int n_seqs, float scale, void* out, int out_dtype,
                      void* workspace, size_t workspace_bytes, int chunk_pages,
                      void* stream);
+
+/* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
+#define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* sckv_decode_attn for callers that cannot allocate device memory; this entry
+ * point has no counterpart in the reference. The split-K partials go to a
+ * fixed SCKV_NOALLOC_SCRATCH_BYTES device array inside the library (one per
+ * GPU, held until exit) instead of a caller workspace; nothing is allocated
+ * per call. chunk_pages <= 0 picks a split that fits; a request whose
+ * partials cannot fit (n_seqs * num_q_heads * splits * 520 bytes) returns
+ * SCKV_ERR_SCRATCH_LIMIT before launching anything. The first call on a
+ * device resolves the array's device address, so make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race. */
+SCKV_API int sckv_decode_attn_noalloc(sckv_pool* pool, int layer, const void* q,
+                             int q_dtype, int num_q_heads,
+                             const int32_t* block_table, int64_t bt_stride,
+                             int max_blocks, const int32_t* ctx_lens,
+                             int n_seqs, float scale, void* out, int out_dtype,
+                             int chunk_pages, void* stream);
 
 /* ========================================================================== */
 /* Kernel 5 — on-device free list allocator and LRU eviction                  */

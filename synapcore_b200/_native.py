@@ -24,6 +24,7 @@ SCKV_ERR_CUDA = -5
 SCKV_ERR_POOL_EXHAUSTED = -6
 SCKV_ERR_TIMEOUT = -7
 SCKV_ERR_UNSUPPORTED = -8
+SCKV_ERR_SCRATCH_LIMIT = -9
 
 # Element types.
 DTYPE_F16 = 0
@@ -72,6 +73,9 @@ _SIGNATURES = [
     ("sckv_decode_attn", c_int,
      [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p, c_int, c_float, c_void_p, c_int,
       c_void_p, c_size_t, c_int, c_void_p]),
+    ("sckv_decode_attn_noalloc", c_int,
+     [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p, c_int, c_float, c_void_p, c_int,
+      c_int, c_void_p]),
     ("sckv_alloc_reset", c_int, [c_void_p, c_void_p]),
     ("sckv_alloc_pages", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     ("sckv_free_pages", c_int, [c_void_p, c_void_p, c_int, c_void_p]),

@@ -548,3 +548,65 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
     default: return SCKV_ERR_UNSUPPORTED;
   }
 }
+
+// ---------------------------------------------------------------------------
+// Decode attention for callers that cannot allocate device memory.
+//
+// Some hosts of this library have no way to obtain scratch memory for a call:
+// a serving process whose device memory is owned up front by another
+// allocator (the page pool plus a fixed arena take nearly all of HBM, and a
+// stray cudaMalloc would fail or stall every stream on the device), or a
+// language binding that exposes only the pool handle and its own buffers.
+// For them the split-K partials live in a fixed file-scope device array of
+// SCKV_NOALLOC_SCRATCH_BYTES per GPU, reserved when the library's module is
+// loaded on that GPU and held until the process exits.
+//
+// The array's name is only a host-side stand-in for the device symbol, so the
+// host resolves its device address once per device (with that device
+// current) through cudaGetSymbolAddress and passes the address down; device
+// code could name the array directly. The first call on a device performs
+// that set-up, so make it before capturing any stream into a CUDA graph.
+//
+// Every call reuses the same array and it keeps the last call's contents.
+// Nothing in it needs to start at zero: each split partial a call reads is
+// written earlier in the same call. Calls whose work overlaps on the GPU (two
+// streams, or two host threads) race on the array; serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = SCKV_NOALLOC_SCRATCH_BYTES;
+static_assert(kNoAllocScratchBytes % 256 == 0, "scratch size must keep 256-byte alignment");
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+void* g_noalloc_scratch_addr[64] = {};
+
+}  // namespace
+
+extern "C" int sckv_decode_attn_noalloc(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                                        const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                                        const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
+                                        int chunk_pages, void* stream) {
+  if (pool == nullptr) return SCKV_ERR_INVALID_ARG;
+  if (n_seqs <= 0 || num_q_heads <= 0 || max_blocks <= 0) return SCKV_ERR_INVALID_ARG;
+  const int dev = pool->device;
+  if (dev < 0 || dev >= 64) return SCKV_ERR_INVALID_ARG;
+  int chunk = chunk_pages;
+  if (chunk <= 0) {
+    // Default split, widened until the partials fit the fixed buffer.
+    chunk = pick_chunk(pool, n_seqs, max_blocks);
+    while (chunk < max_blocks &&
+           sckv_decode_workspace_bytes(pool, n_seqs, num_q_heads, max_blocks, chunk) > kNoAllocScratchBytes)
+      chunk = chunk * 2 < max_blocks ? chunk * 2 : max_blocks;
+  }
+  if (sckv_decode_workspace_bytes(pool, n_seqs, num_q_heads, max_blocks, chunk) > kNoAllocScratchBytes)
+    return SCKV_ERR_SCRATCH_LIMIT;
+  if (g_noalloc_scratch_addr[dev] == nullptr) {
+    SCKV_CUDA_CHECK(cudaSetDevice(dev));
+    void* addr = nullptr;
+    SCKV_CUDA_CHECK(cudaGetSymbolAddress(&addr, g_noalloc_scratch));
+    g_noalloc_scratch_addr[dev] = addr;
+  }
+  return sckv_decode_attn(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens, n_seqs,
+                          scale, out, out_dtype, g_noalloc_scratch_addr[dev], kNoAllocScratchBytes, chunk, stream);
+}

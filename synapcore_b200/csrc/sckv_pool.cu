@@ -178,6 +178,7 @@ extern "C" const char* sckv_status_string(int code) {
     case SCKV_ERR_POOL_EXHAUSTED: return "page pool exhausted";
     case SCKV_ERR_TIMEOUT: return "in-kernel wait timed out";
     case SCKV_ERR_UNSUPPORTED: return "unsupported dtype or shape";
+    case SCKV_ERR_SCRATCH_LIMIT: return "request exceeds the fixed no-allocation scratch";
     default: return "unknown status";
   }
 }
