@@ -52,6 +52,11 @@ WORKLOADS = {
                   batch=64, ctx=4096, pool_pages=18750),
     "qwen3-fp8": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                       qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
+    # profiling-sized variants: same per-launch structure, 2 layers, a few hundred MB
+    "olmoe-small": dict(model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128, kv="fp16",
+                        qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
+    "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
+                            qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
 }
 
 

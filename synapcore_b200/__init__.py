@@ -1,0 +1,23 @@
+"""B200-native paged KV cache: a drop-in for SynapCore's paged KV path.
+
+Host side (Python / PyTorch) mirrors the reference API — PagedKVArena,
+NativeKVPrefixCache, the KV prefix hash table — and drives hand-written
+sm_100a CUDA kernels in libsckv.so through its C ABI (include/sckv.h).
+"""
+from ._native import SCKVBoundsError, SCKVError, SCKVPoolExhausted
+from .arena import PagedKVArena
+from .kv_index import KVPrefixIndex
+from .pool import KVPool
+from .prefix_cache import NativeKVPrefixCache, PagedKVStats, chain_merkle_prefix_hash
+
+__all__ = [
+    "KVPool",
+    "KVPrefixIndex",
+    "NativeKVPrefixCache",
+    "PagedKVArena",
+    "PagedKVStats",
+    "SCKVBoundsError",
+    "SCKVError",
+    "SCKVPoolExhausted",
+    "chain_merkle_prefix_hash",
+]

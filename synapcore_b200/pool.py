@@ -67,9 +67,12 @@ class KVPool:
         if kv_dtype not in DTYPE_CODES:
             raise ValueError(f"kv_dtype must be one of {sorted(DTYPE_CODES)}, got {kv_dtype!r}")
         self.lib = N.lib()
-        self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
-        if self.device.type != "cuda":
+        dev = torch.device(device if device is not None else "cuda")
+        if dev.type != "cuda":
             raise ValueError("KVPool lives in GPU memory; pass a cuda device")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self.num_layers, self.num_kv_heads, self.head_dim = int(num_layers), int(num_kv_heads), int(head_dim)
         self.max_pages = int(max_pages)
         self.kv_dtype = kv_dtype
@@ -79,11 +82,11 @@ class KVPool:
         with torch.cuda.device(self.device):
             self.data = torch.zeros(data_b, dtype=torch.uint8, device=self.device)
             self.scales = torch.zeros(max(scale_b, 16), dtype=torch.uint8, device=self.device) if scale_b else None
-            self.alloc_state = torch.zeros(alloc_b, dtype=torch.uint8, device=self.device)
+            self.alloc_region = torch.zeros(alloc_b, dtype=torch.uint8, device=self.device)
             h = ctypes.c_void_p()
             N.check(self.lib.sckv_pool_wrap(self.num_layers, self.num_kv_heads, self.head_dim, PAGE_TOKENS,
                                             self.max_pages, self.code, self.device.index, self.data.data_ptr(),
-                                            _ptr(self.scales), self.alloc_state.data_ptr(), ctypes.byref(h)),
+                                            _ptr(self.scales), self.alloc_region.data_ptr(), ctypes.byref(h)),
                     "sckv_pool_wrap")
             self.handle = h
             self.alloc_reset()
