@@ -195,9 +195,12 @@ def build_state(w, rank: int):
     if w["kv"] == "fp8_e4m3":
         # random e4m3 codes (no NaN bytes 0x7f / 0xff) and per-page-head scales U[0.5,4]/448*4
         for l in range(L):
-            codes = torch.randint(0, 0x7F, view[l].shape, dtype=torch.uint8, device=dev, generator=g)
-            sign = torch.randint(0, 2, view[l].shape, dtype=torch.uint8, device=dev, generator=g) << 7
-            view[l].copy_(codes | sign)
+            for c0 in range(0, w["pool_pages"], 8192):
+                blk = view[l, c0:c0 + 8192]
+                codes = torch.randint(0, 0x7F, blk.shape, dtype=torch.uint8, device=dev, generator=g)
+                codes |= torch.randint(0, 2, blk.shape, dtype=torch.uint8, device=dev, generator=g) << 7
+                blk.copy_(codes)
+                del codes
         pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
     else:
         for l in range(L):

@@ -25,38 +25,14 @@
 //    returns. Invalid page ids are recorded (SCKV_ERR_BOUNDS) and page 0 is
 //    read in their place so the ring stays consistent.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
-#include "sckv_internal.cuh"
+#include "sckv_decode_common.cuh"
+
+using namespace sckv_detail;
 
 namespace {
-
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kHD = 128;  // head_dim handled by this kernel
-
-struct DecodeParams {
-  const uint8_t* pool;
-  const float* fp8_scales;
-  const void* q;
-  void* out;
-  float* part_acc;  // [n_seqs][Hq][max_splits][HD]
-  float* part_ml;   // [n_seqs][Hq][max_splits][2]
-  const int32_t* block_table;
-  const int32_t* ctx_lens;
-  int32_t* status;
-  int64_t bt_stride;
-  int64_t max_pages;
-  int max_blocks;
-  int n_seqs;
-  int hq;
-  int hkv;
-  int layer;
-  int chunk_pages;
-  int max_splits;
-  int q_dtype;
-  int out_dtype;
-  float scale_log2;
-};
 
 template <int KVDT>
 struct KV;
@@ -102,16 +78,6 @@ struct KV<SCKV_DTYPE_FP8_E4M3> {
     }
   }
 };
-
-__device__ __forceinline__ int clamp_ctx(const DecodeParams& p, int b, bool report) {
-  int ctx = __ldg(p.ctx_lens + b);
-  const int cap = p.max_blocks * SCKV_PAGE_TOKENS;
-  if (ctx < 0 || ctx > cap) {
-    if (report) sckv_report(p.status, SCKV_ERR_BOUNDS, ctx, KID_DECODE);
-    ctx = ctx < 0 ? 0 : cap;
-  }
-  return ctx;
-}
 
 // Reduce-scatter 8 partial sums over the 16 lanes of a half-warp: afterwards
 // lane c holds the full sum of element c >> 1.
@@ -431,6 +397,22 @@ __global__ void combine_kernel(const DecodeParams p) {
   sckv_store_from_float(p.out, out_idx, p.out_dtype, L > 0.f ? O / L : 0.f);
 }
 
+}  // namespace
+
+namespace sckv_detail {
+
+// Merges split partials and writes zeros for empty sequences; runs after
+// either decode kernel.
+int launch_combine(const DecodeParams& prm, cudaStream_t stream) {
+  combine_kernel<<<prm.n_seqs * prm.hq, kHD, 0, stream>>>(prm);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+}  // namespace sckv_detail
+
+namespace {
+
 template <int G, int KVDT, int S>
 int launch_decode(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t stream) {
   using SM = Smem<G, KVDT, S>;
@@ -451,15 +433,7 @@ int launch_decode(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t s
   if (grid < 1) grid = 1;
   kern<<<grid, kThreads, SM::kBytes, stream>>>(prm);
   SCKV_LAUNCH_CHECK();
-  if (prm.max_splits > 1) {
-    combine_kernel<<<prm.n_seqs * prm.hq, kHD, 0, stream>>>(prm);
-    SCKV_LAUNCH_CHECK();
-  } else {
-    // ctx == 0 sequences still need their zero output.
-    combine_kernel<<<prm.n_seqs * prm.hq, kHD, 0, stream>>>(prm);
-    SCKV_LAUNCH_CHECK();
-  }
-  return SCKV_OK;
+  return launch_combine(prm, stream);
 }
 
 template <int KVDT, int S>
@@ -471,6 +445,22 @@ int dispatch_g(const sckv_pool* pool, int G, const DecodeParams& prm, cudaStream
     case 8: return launch_decode<8, KVDT, S>(pool, prm, s);
     default: return SCKV_ERR_UNSUPPORTED;
   }
+}
+
+// Grouped-query heads share each K/V page among G query rows: those go to
+// the tensor-core kernel. A bf16 pool multiplies in bf16, so it needs bf16
+// queries to keep q exact. SCKV_DECODE_KERNEL=simt|mma overrides (for
+// measuring one kernel against the other).
+bool use_tensor_core_path(const sckv_pool* pool, int G, int q_dtype) {
+  static int forced = -2;
+  if (forced == -2) {
+    const char* e = getenv("SCKV_DECODE_KERNEL");
+    forced = (e == nullptr) ? -1 : (strcmp(e, "mma") == 0 ? 1 : (strcmp(e, "simt") == 0 ? 0 : -1));
+  }
+  if (pool->kv_dtype == SCKV_DTYPE_BF16 && q_dtype != SCKV_DTYPE_BF16) return false;
+  if (G > 16) return false;
+  if (forced >= 0) return forced == 1;
+  return G >= 2;
 }
 
 int pick_chunk(const sckv_pool* pool, int n_seqs, int max_blocks) {
@@ -541,6 +531,10 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
   const int G = num_q_heads / pool->num_kv_heads;
   cudaStream_t s = as_stream(stream);
   SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  if (use_tensor_core_path(pool, G, q_dtype)) {
+    const int rc = launch_decode_mma(pool, G, prm, s);
+    if (rc != SCKV_ERR_UNSUPPORTED) return rc;
+  }
   switch (pool->kv_dtype) {
     case SCKV_DTYPE_F16: return dispatch_g<SCKV_DTYPE_F16, 8>(pool, G, prm, s);
     case SCKV_DTYPE_BF16: return dispatch_g<SCKV_DTYPE_BF16, 8>(pool, G, prm, s);

@@ -69,6 +69,10 @@ struct sckv_pool {
   size_t scale_bytes;
   size_t alloc_bytes;
   int num_sms;
+  // TMA tensor map over the page data (a CUtensorMap, encoded on first use
+  // by the tensor-core decode kernel).
+  alignas(64) unsigned char tmap_kv[128];
+  int tmap_ready;
 };
 
 static inline int sckv_elem_bytes(int dtype) {

@@ -50,7 +50,9 @@ extern "C" int sckv_pool_required_bytes(int L, int H, int D, int T, int64_t P, i
   const size_t data = static_cast<size_t>(L) * static_cast<size_t>(P) * slab * sckv_elem_bytes(dtype);
   size_t scales = 0;
   if (dtype == SCKV_DTYPE_INT8) scales = static_cast<size_t>(L) * P * 2ULL * H * T * sizeof(__half);
-  if (dtype == SCKV_DTYPE_FP8_E4M3) scales = static_cast<size_t>(L) * P * 2ULL * H * sizeof(float);
+  // fp8 scales are staged with 16-byte bulk copies of aligned 4-float blocks:
+  // pad so the last block stays inside the region.
+  if (dtype == SCKV_DTYPE_FP8_E4M3) scales = (static_cast<size_t>(L) * P * 2ULL * H * sizeof(float) + 63) / 64 * 64;
   if (data_bytes) *data_bytes = data;
   if (scale_bytes) *scale_bytes = scales;
   if (alloc_bytes) *alloc_bytes = alloc_layout(P).total;

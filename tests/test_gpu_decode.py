@@ -58,6 +58,9 @@ def _make_case(cuda_device, kv_dtype, hq, hkv, ctx_lens, pool_pages, seed, layer
     ("fp8_e4m3", 32, 8, torch.bfloat16),
     ("fp8_e4m3", 16, 16, torch.float16),
     ("fp16", 16, 2, torch.float16),
+    ("bf16", 16, 8, torch.bfloat16),
+    ("fp8_e4m3", 32, 2, torch.bfloat16),
+    ("fp8_e4m3", 8, 4, torch.float32),
 ])
 @pytest.mark.parametrize("chunk_pages", [0, 3])
 def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages):
