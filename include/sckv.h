@@ -169,7 +169,11 @@ SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
  *
  * q   : [n_seqs][num_q_heads][head_dim] of q_dtype (F16 / BF16 / F32)
  * out : [n_seqs][num_q_heads][head_dim] of out_dtype (F16 / BF16 / F32)
- * chunk_pages : pages per split (split-K unit); <= 0 picks one.
+ * block_table : int32 [n_seqs][bt_stride]; bt_stride 0 makes every sequence
+ *               read row 0 (prefill: query token t of one sequence is a
+ *               "sequence" of length start+t+1 over the same pages).
+ * chunk_pages : pages per split (split-K unit); <= 0 picks one. A fixed
+ *               value makes each sequence's result independent of the batch.
  * workspace   : device scratch of sckv_decode_workspace_bytes bytes.
  * Pool dtypes F16, BF16, FP8_E4M3; accumulation is fp32. */
 SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype,
@@ -232,6 +236,15 @@ SCKV_API int sckv_touch_pages(sckv_pool* pool, const int32_t* ids, int n, void* 
 /* Add `delta` to the pin counts of pages (copy-on-write sharing). */
 SCKV_API int sckv_pin_pages(sckv_pool* pool, const int32_t* ids, int n, int delta,
                    void* stream);
+
+/* Drop one pin from each page (a sequence letting go of its pages). A page
+ * whose pin count reaches zero returns to the ring tail in list order, or,
+ * with keep_cached != 0, stays allocated as an LRU eviction candidate (a
+ * cached prefix page). Ids in one call must be distinct. The device side of
+ * freeing a request's KV (the reference drops its per-request arrays,
+ * engine/scheduler.py:369-371). */
+SCKV_API int sckv_release_pages(sckv_pool* pool, const int32_t* ids, int n,
+                       int keep_cached, void* stream);
 
 /* Evict the n least recently used unpinned allocated pages to the ring
  * tail, oldest first; out_ids (may be NULL) receives them, -1 padded. */

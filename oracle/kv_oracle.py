@@ -301,6 +301,18 @@ class AllocatorOracle:
         for pid in ids:
             self.pin[int(pid)] += delta
 
+    def release(self, ids: Sequence[int], keep_cached: bool = False) -> None:
+        """Drop one pin per page; pin 0 -> ring tail (or stay cached)."""
+        for pid in ids:
+            pid = int(pid)
+            if pid < 0 or pid >= self.P or not self.allocated[pid]:
+                continue
+            self.pin[pid] -= 1
+            if self.pin[pid] == 0 and not keep_cached:
+                self.allocated[pid] = False
+                self.last_used[pid] = 0
+                self.ring.append(pid)
+
     def evict_lru(self, n: int) -> List[int]:
         out = []
         for _ in range(n):

@@ -81,6 +81,7 @@ _SIGNATURES = [
     ("sckv_free_pages", c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_touch_pages", c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_pin_pages", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    ("sckv_release_pages", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     ("sckv_evict_lru", c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     ("sckv_reserve_decode", c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p]),
     ("sckv_alloc_state", c_int, [c_void_p, POINTER(c_int64), c_void_p]),

@@ -355,6 +355,47 @@ __global__ void __launch_bounds__(kT) free_kernel(AllocView a, const int32_t* id
   }
 }
 
+// Drop one pin from each listed page, in list order; a page whose pin count
+// reaches zero goes to the ring tail (FIFO) — or, with keep_cached, stays
+// allocated as an LRU eviction candidate. Ids in one call must be distinct.
+__global__ void __launch_bounds__(kT) release_kernel(AllocView a, const int32_t* ids, int n, int keep_cached) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& s = *reinterpret_cast<SelectSmem*>(smem_raw);
+  for (int base = 0; base < n; base += kT) {
+    const int i = base + threadIdx.x;
+    int freed = 0;
+    int32_t id = -1;
+    if (i < n) {
+      id = ids[i];
+      if (id >= 0 && id < a.P && a.state[id] == PAGE_ALLOCATED) {
+        const int old = atomicSub(&a.pin[id], 1);
+        if (old <= 0) {
+          atomicAdd(&a.pin[id], 1);
+          sckv_report(a.status, SCKV_ERR_INVALID_ARG, id, KID_PIN);
+        } else if (old == 1 && !keep_cached) {
+          freed = 1;
+        }
+      } else if (id != -1) {
+        sckv_report(a.status, SCKV_ERR_BOUNDS, id, KID_PIN);
+      }
+    }
+    int total = 0;
+    const int pos = block_exclusive_scan(freed, &total, s);
+    const int64_t tail = a.ctl[CTL_TAIL];
+    if (freed) {
+      a.ring[(tail + pos) % a.P] = id;
+      a.state[id] = PAGE_FREE;
+      a.last_used[id] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      a.ctl[CTL_TAIL] = tail + total;
+      a.ctl[CTL_ALLOCATED] -= total;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void touch_kernel(AllocView a, const int32_t* ids, int n) {
   const int64_t clock0 = a.ctl[CTL_CLOCK];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -478,6 +519,7 @@ int ensure_configured(int device) {
   if (rc == SCKV_OK) rc = configure(reinterpret_cast<const void*>(free_kernel));
   if (rc == SCKV_OK) rc = configure(reinterpret_cast<const void*>(evict_kernel));
   if (rc == SCKV_OK) rc = configure(reinterpret_cast<const void*>(reserve_kernel));
+  if (rc == SCKV_OK) rc = configure(reinterpret_cast<const void*>(release_kernel));
   if (rc == SCKV_OK) done[device] = true;
   return rc;
 }
@@ -540,6 +582,17 @@ extern "C" int sckv_pin_pages(sckv_pool* p, const int32_t* ids, int n, int delta
   int blocks = (n + 255) / 256;
   if (blocks > p->num_sms * 4) blocks = p->num_sms * 4;
   pin_kernel<<<blocks, 256, 0, as_stream(stream)>>>(view_of(p), ids, n, delta);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+extern "C" int sckv_release_pages(sckv_pool* p, const int32_t* ids, int n, int keep_cached, void* stream) {
+  if (p == nullptr || n < 0 || (n > 0 && ids == nullptr)) return SCKV_ERR_INVALID_ARG;
+  if (n == 0) return SCKV_OK;
+  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  int rc = ensure_configured(p->device);
+  if (rc != SCKV_OK) return rc;
+  release_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), ids, n, keep_cached ? 1 : 0);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }

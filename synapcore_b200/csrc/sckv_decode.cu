@@ -494,7 +494,8 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
   if (pool == nullptr) return SCKV_ERR_INVALID_ARG;
   if (pool->head_dim != kHD) return SCKV_ERR_UNSUPPORTED;
   if (layer < 0 || layer >= pool->num_layers) return SCKV_ERR_INVALID_ARG;
-  if (n_seqs <= 0 || num_q_heads <= 0 || max_blocks <= 0 || bt_stride < max_blocks) return SCKV_ERR_INVALID_ARG;
+  if (n_seqs <= 0 || num_q_heads <= 0 || max_blocks <= 0 || (bt_stride != 0 && bt_stride < max_blocks))
+    return SCKV_ERR_INVALID_ARG;
   if (num_q_heads % pool->num_kv_heads != 0) return SCKV_ERR_INVALID_ARG;
   if (!q || !out || !block_table || !ctx_lens) return SCKV_ERR_INVALID_ARG;
   if (q_dtype != SCKV_DTYPE_F16 && q_dtype != SCKV_DTYPE_BF16 && q_dtype != SCKV_DTYPE_F32) return SCKV_ERR_INVALID_ARG;

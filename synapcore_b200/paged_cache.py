@@ -1,0 +1,219 @@
+"""Per-sequence paged KV cache on one GPU: block tables over a KVPool.
+
+This is the B200 form of the scheduler's per-request KV state. The reference
+keeps one contiguous `[1, Hkv, T, D]` array per request and layer, grown by
+`np.concatenate` on every token (models/adapters.py:1194-1207), and gives a
+forked request an eager copy of a matched prefix (engine/scheduler.py:150-152).
+Here every sequence owns a row of a device block table; pages come from the
+pool's on-device allocator; a decode step reserves its new pages on the GPU
+(`sckv_reserve_decode`) without a host round trip; a prefix shared by several
+sequences is the same physical pages (pin count = number of holders), and a
+fork copies only the partially filled last page (copy-on-write).
+
+Rows are kept compact: live sequences occupy rows 0..n_live-1, so a decode
+batch is a contiguous slice. Removing a sequence moves the last row into its
+place. Host state is only the per-row token counts (deterministic, no device
+reads on the decode path).
+"""
+from __future__ import annotations
+
+from typing import Dict, Hashable, List, Optional, Sequence, Tuple
+
+import torch
+
+from .pool import KVPool, PAGE_TOKENS
+
+
+def _ceil_div(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+class PagedKVCache:
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_pages: int, max_seqs: int,
+                 max_blocks_per_seq: int, kv_dtype: str = "fp16", device: Optional[torch.device] = None,
+                 chunk_pages: int = 32):
+        self.pool = KVPool(num_layers, num_kv_heads, head_dim, max_pages, kv_dtype, device=device)
+        self.device = self.pool.device
+        self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
+        self.max_seqs, self.max_blocks = int(max_seqs), int(max_blocks_per_seq)
+        # A fixed split size keeps every sequence's attention result independent
+        # of which other sequences share the batch.
+        self.chunk_pages = int(chunk_pages)
+        self.block_table = torch.full((self.max_seqs, self.max_blocks), -1, dtype=torch.int32, device=self.device)
+        self.ctx_lens = torch.zeros(self.max_seqs, dtype=torch.int32, device=self.device)
+        self.lengths: List[int] = []           # tokens per live row
+        self.row_of: Dict[Hashable, int] = {}  # sequence id -> row
+        self.seq_at: List[Hashable] = []       # row -> sequence id
+        self._arange = torch.arange(self.max_seqs + 1, dtype=torch.int32, device=self.device)
+
+    # ------------------------------------------------------------------ rows
+    @property
+    def n_live(self) -> int:
+        return len(self.seq_at)
+
+    def add_sequence(self, seq_id: Hashable) -> int:
+        if seq_id in self.row_of:
+            raise KeyError(f"sequence {seq_id!r} already exists")
+        if self.n_live >= self.max_seqs:
+            raise RuntimeError("PagedKVCache: all sequence rows are in use")
+        r = self.n_live
+        self.row_of[seq_id] = r
+        self.seq_at.append(seq_id)
+        self.lengths.append(0)
+        self.block_table[r].fill_(-1)
+        self.ctx_lens[r] = 0
+        return r
+
+    def length(self, seq_id: Hashable) -> int:
+        return self.lengths[self.row_of[seq_id]]
+
+    def _pages_of(self, r: int) -> int:
+        return _ceil_div(self.lengths[r], PAGE_TOKENS)
+
+    def remove_sequence(self, seq_id: Hashable, keep_cached: bool = False) -> None:
+        """Drop the sequence's pins on its pages (shared pages survive for their
+        other holders) and compact the rows."""
+        r = self.row_of.pop(seq_id)
+        n = self._pages_of(r)
+        if n:
+            self.pool.release_pages(self.block_table[r, :n], keep_cached=keep_cached)
+        last = self.n_live - 1
+        if r != last:
+            self.block_table[r].copy_(self.block_table[last])
+            self.ctx_lens[r] = self.ctx_lens[last]
+            moved = self.seq_at[last]
+            self.seq_at[r] = moved
+            self.lengths[r] = self.lengths[last]
+            self.row_of[moved] = r
+        self.seq_at.pop()
+        self.lengths.pop()
+        self.block_table[last].fill_(-1)
+        self.ctx_lens[last] = 0
+
+    def move_to_row(self, seq_id: Hashable, row: int) -> None:
+        """Swap two live rows (used to keep decode-phase sequences first)."""
+        r = self.row_of[seq_id]
+        if r == row:
+            return
+        other = self.seq_at[row]
+        tmp_bt = self.block_table[row].clone()
+        self.block_table[row].copy_(self.block_table[r])
+        self.block_table[r].copy_(tmp_bt)
+        tmp_len = self.ctx_lens[row].clone()
+        self.ctx_lens[row] = self.ctx_lens[r]
+        self.ctx_lens[r] = tmp_len
+        self.seq_at[row], self.seq_at[r] = seq_id, other
+        self.lengths[row], self.lengths[r] = self.lengths[r], self.lengths[row]
+        self.row_of[seq_id], self.row_of[other] = row, r
+
+    # -------------------------------------------------------------- prefill
+    def _grow(self, r: int, n_new: int) -> None:
+        """Allocate (pinned) pages so row r can hold n_new more tokens."""
+        have = self._pages_of(r)
+        need = _ceil_div(self.lengths[r] + n_new, PAGE_TOKENS)
+        if need > self.max_blocks:
+            raise ValueError(f"sequence would need {need} blocks > max_blocks_per_seq={self.max_blocks}")
+        if need > have:
+            ids, _ = self.pool.alloc_pages(need - have, pin=True)
+            self.block_table[r, have:need].copy_(ids)
+
+    def append_prefill(self, seq_id: Hashable, k: torch.Tensor, v: torch.Tensor, layer0: int = 0) -> None:
+        """Append T tokens of one sequence: k, v [n_layers, T, Hkv, D] (or
+        [T, Hkv, D] for one layer, layer0). Pages are reserved on the first
+        layer written (layer0 == 0 or n_layers == all) and the length advances
+        once the last layer is written."""
+        if k.dim() == 3:
+            k, v = k.unsqueeze(0), v.unsqueeze(0)
+        r = self.row_of[seq_id]
+        nl, T = k.shape[0], k.shape[1]
+        if layer0 == 0:
+            self._grow(r, T)
+        cu = self._arange[:2].clone()
+        cu[1] = T
+        start = torch.full((1,), self.lengths[r], dtype=torch.int32, device=self.device)
+        self.pool.append(k, v, cu, start, self.block_table[r:r + 1], layer0=layer0)
+        if layer0 + nl == self.num_layers:
+            self.lengths[r] += T
+            self.ctx_lens[r] = self.lengths[r]
+
+    def prefill_attention(self, layer: int, seq_id: Hashable, q: torch.Tensor, start: int,
+                          scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """Causal attention of T new query tokens at positions start..start+T-1
+        (already appended) over the sequence's pages: token t sees positions
+        <= start+t. q [T, Hq, D] -> [T, Hq, D]."""
+        r = self.row_of[seq_id]
+        T = q.shape[0]
+        bt = self.block_table[r:r + 1].expand(T, self.max_blocks)  # stride 0: every token reads row r
+        ctx = torch.arange(start + 1, start + T + 1, dtype=torch.int32, device=self.device)
+        return self.pool.decode_attn(layer, q, bt, ctx, scale=scale, out_dtype=out_dtype,
+                                     max_blocks=self.max_blocks, chunk_pages=self.chunk_pages)
+
+    # --------------------------------------------------------------- decode
+    def decode_reserve(self, n_rows: int) -> None:
+        """One new token for rows 0..n_rows-1: pages for those crossing a page
+        boundary are allocated on the device, lengths advance by one."""
+        self.pool.reserve_decode(self.block_table, self.ctx_lens, n_seqs=n_rows, max_blocks=self.max_blocks)
+        for r in range(n_rows):
+            self.lengths[r] += 1
+
+    def decode_append(self, layer: int, k: torch.Tensor, v: torch.Tensor, n_rows: int) -> None:
+        """k, v [n_rows, Hkv, D]: the token reserved by decode_reserve."""
+        start = self.ctx_lens[:n_rows] - 1
+        self.pool.append(k, v, self._arange[:n_rows + 1], start, self.block_table[:n_rows], layer0=layer,
+                         max_blocks=self.max_blocks)
+
+    def decode_attention(self, layer: int, q: torch.Tensor, n_rows: int, scale: Optional[float] = None,
+                         out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None
+                         ) -> torch.Tensor:
+        return self.pool.decode_attn(layer, q, self.block_table[:n_rows], self.ctx_lens[:n_rows], scale=scale,
+                                     out=out, out_dtype=out_dtype, max_blocks=self.max_blocks,
+                                     chunk_pages=self.chunk_pages)
+
+    # ------------------------------------------------------ sharing / fork
+    def share_prefix(self, seq_id: Hashable, page_ids: Sequence[int]) -> None:
+        """Start an empty sequence with full prefix pages held elsewhere (a
+        prefix-cache hit): its block table points at them and pins them."""
+        r = self.row_of[seq_id]
+        if self.lengths[r] != 0:
+            raise ValueError("share_prefix needs an empty sequence")
+        n = len(page_ids)
+        if n == 0:
+            return
+        ids = torch.as_tensor(list(page_ids), dtype=torch.int32).to(self.device)
+        self.block_table[r, :n].copy_(ids)
+        self.pool.pin_pages(ids, +1)
+        self.lengths[r] = n * PAGE_TOKENS
+        self.ctx_lens[r] = self.lengths[r]
+
+    def fork(self, src_id: Hashable, dst_id: Hashable) -> int:
+        """Copy-on-write fork: full pages are shared (pinned once more), the
+        partially filled last page is copied to a fresh page."""
+        rs = self.row_of[src_id]
+        rd = self.add_sequence(dst_id)
+        n_tok = self.lengths[rs]
+        n_full = n_tok // PAGE_TOKENS
+        if n_full:
+            self.block_table[rd, :n_full].copy_(self.block_table[rs, :n_full])
+            self.pool.pin_pages(self.block_table[rd, :n_full], +1)
+        if n_tok % PAGE_TOKENS:
+            ids, _ = self.pool.alloc_pages(1, pin=True)
+            self.pool.copy_pages(self.block_table[rs, n_full:n_full + 1], ids)
+            self.block_table[rd, n_full:n_full + 1].copy_(ids)
+        self.lengths[rd] = n_tok
+        self.ctx_lens[rd] = n_tok
+        return rd
+
+    def page_ids(self, seq_id: Hashable) -> List[int]:
+        r = self.row_of[seq_id]
+        return self.block_table[r, :self._pages_of(r)].tolist()
+
+    # --------------------------------------------------------------- gather
+    def gather(self, seq_id: Hashable, out_dtype: torch.dtype = torch.float16) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Contiguous [L, Hkv, T, D] K and V of one sequence (all layers)."""
+        r = self.row_of[seq_id]
+        n = self._pages_of(r)
+        return self.pool.gather(self.block_table[r, :n], self.lengths[r], out_dtype=out_dtype)
+
+    def check(self) -> None:
+        """Raise if any kernel recorded an error in the device status word."""
+        self.pool.raise_on_status()

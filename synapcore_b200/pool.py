@@ -51,6 +51,21 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _need(t: torch.Tensor, name: str, device: torch.device, dtype: Optional[torch.dtype] = None,
+          min_numel: int = 0, contiguous: bool = True) -> None:
+    """Reject tensors the kernels would read out of bounds or misinterpret."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, the pool is on {device}")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if t.numel() < min_numel:
+        raise ValueError(f"{name} has {t.numel()} elements, needs at least {min_numel}")
+
+
 def _dev_i32(x, device) -> torch.Tensor:
     if isinstance(x, torch.Tensor):
         t = x.to(device=device, dtype=torch.int32)
@@ -132,6 +147,17 @@ class KVPool:
         n_seqs = cu_tokens.numel() - 1
         bt = block_table if block_table.dim() == 2 else block_table.view(1, -1)
         mb = bt.shape[1] if max_blocks is None else int(max_blocks)
+        if tuple(k_new.shape[2:]) != (self.num_kv_heads, self.head_dim) or k_new.shape != v_new.shape:
+            raise ValueError(f"k_new/v_new must be [n_layers, n_tokens, {self.num_kv_heads}, {self.head_dim}]")
+        if layer0 < 0 or layer0 + nl > self.num_layers:
+            raise ValueError("append layers out of range")
+        _need(k_new, "k_new", self.device)
+        _need(v_new, "v_new", self.device)
+        _need(cu_tokens, "cu_tokens", self.device, torch.int32, 1)
+        _need(start_pos, "start_pos", self.device, torch.int32, n_seqs)
+        _need(bt, "block_table", self.device, torch.int32, contiguous=False)
+        if bt.dim() != 2 or bt.shape[0] < n_seqs or mb > bt.shape[1] or bt.stride(1) != 1:
+            raise ValueError("block_table must be [>= n_seqs, >= max_blocks] with unit column stride")
         N.check(self.lib.sckv_append(self.handle, layer0, nl, k_new.data_ptr(), v_new.data_ptr(),
                                      torch_dtype_code(k_new.dtype), n_seqs, nt, cu_tokens.data_ptr(),
                                      start_pos.data_ptr(), bt.data_ptr(), bt.stride(0), mb, _stream_ptr(stream)),
@@ -141,6 +167,13 @@ class KVPool:
                     stream: Optional[torch.cuda.Stream] = None) -> None:
         """k_src, v_src: [n, L, H, 16, D] float16 / bfloat16 / float32."""
         k_src, v_src = k_src.contiguous(), v_src.contiguous()
+        n = page_ids.numel()
+        shape = (n, self.num_layers, self.num_kv_heads, PAGE_TOKENS, self.head_dim)
+        if tuple(k_src.shape) != shape or tuple(v_src.shape) != shape:
+            raise ValueError(f"k_src/v_src must be {list(shape)}")
+        _need(page_ids, "page_ids", self.device, torch.int32)
+        _need(k_src, "k_src", self.device)
+        _need(v_src, "v_src", self.device)
         N.check(self.lib.sckv_write_pages(self.handle, page_ids.data_ptr(), page_ids.numel(), k_src.data_ptr(),
                                           v_src.data_ptr(), torch_dtype_code(k_src.dtype), _stream_ptr(stream)),
                 "sckv_write_pages")
@@ -149,6 +182,14 @@ class KVPool:
                               vs: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> None:
         """kq/vq int8 [n, L, H, 16, D]; ks/vs float16 [n, L, H, 16]."""
         kq, ks, vq, vs = (t.contiguous() for t in (kq, ks, vq, vs))
+        n = page_ids.numel()
+        qs = (n, self.num_layers, self.num_kv_heads, PAGE_TOKENS, self.head_dim)
+        if tuple(kq.shape) != qs or tuple(vq.shape) != qs or tuple(ks.shape) != qs[:-1] or tuple(vs.shape) != qs[:-1]:
+            raise ValueError("quantized page shapes do not match the pool")
+        _need(page_ids, "page_ids", self.device, torch.int32)
+        for t, name, dt in ((kq, "kq", torch.int8), (vq, "vq", torch.int8), (ks, "ks", torch.float16),
+                            (vs, "vs", torch.float16)):
+            _need(t, name, self.device, dt)
         N.check(self.lib.sckv_write_pages_quantized(self.handle, page_ids.data_ptr(), page_ids.numel(),
                                                     kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
                                                     _stream_ptr(stream)),
@@ -164,6 +205,14 @@ class KVPool:
         nt = n_pages * PAGE_TOKENS if n_tokens is None else int(n_tokens)
         nl = self.num_layers - layer0 if n_layers is None else int(n_layers)
         shape = (nl, self.num_kv_heads, nt, self.head_dim)
+        _need(page_ids, "page_ids", self.device, torch.int32)
+        if nt > n_pages * PAGE_TOKENS or layer0 < 0 or layer0 + nl > self.num_layers:
+            raise ValueError("gather range out of bounds")
+        if out is not None:
+            for t in out:
+                _need(t, "out", self.device)
+                if tuple(t.shape) != shape:
+                    raise ValueError(f"gather outputs must be {list(shape)}")
         if out is None:
             ok = torch.empty(shape, dtype=out_dtype, device=self.device)
             ov = torch.empty(shape, dtype=out_dtype, device=self.device)
@@ -176,6 +225,8 @@ class KVPool:
 
     def copy_pages(self, src_ids: torch.Tensor, dst_ids: torch.Tensor,
                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        _need(src_ids, "src_ids", self.device, torch.int32)
+        _need(dst_ids, "dst_ids", self.device, torch.int32, src_ids.numel())
         N.check(self.lib.sckv_copy_pages(self.handle, src_ids.data_ptr(), dst_ids.data_ptr(), src_ids.numel(),
                                          _stream_ptr(stream)), "sckv_copy_pages")
 
@@ -193,11 +244,28 @@ class KVPool:
         q = q.contiguous()
         B, hq, d = q.shape
         mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
+        if d != self.head_dim or hq % self.num_kv_heads != 0:
+            raise ValueError(f"q must be [B, k*{self.num_kv_heads}, {self.head_dim}]")
+        if not 0 <= layer < self.num_layers:
+            raise ValueError("layer out of range")
+        _need(q, "q", self.device)
+        _need(ctx_lens, "ctx_lens", self.device, torch.int32, B)
+        _need(block_table, "block_table", self.device, torch.int32, contiguous=False)
+        if block_table.dim() != 2 or block_table.stride(1) != 1 or mb > block_table.shape[1]:
+            raise ValueError("block_table must be 2-D with unit column stride and >= max_blocks columns")
+        if block_table.stride(0) != 0 and block_table.shape[0] < B:
+            raise ValueError("block_table has fewer rows than sequences")
         if scale is None:
             scale = float(d) ** -0.5
         if out is None:
             out = torch.empty((B, hq, d), dtype=out_dtype or q.dtype, device=self.device)
+        else:
+            _need(out, "out", self.device, min_numel=B * hq * d)
+            if tuple(out.shape) != (B, hq, d):
+                raise ValueError("out must have q's shape")
         need = self.decode_workspace_bytes(B, hq, mb, chunk_pages)
+        if workspace is not None:
+            _need(workspace, "workspace", self.device, min_numel=need)
         if workspace is None:
             if self._workspace is None or self._workspace.numel() < need:
                 self._workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=self.device)
@@ -236,6 +304,12 @@ class KVPool:
         N.check(self.lib.sckv_pin_pages(self.handle, ids.data_ptr(), ids.numel(), int(delta), _stream_ptr(stream)),
                 "sckv_pin_pages")
 
+    def release_pages(self, ids: torch.Tensor, keep_cached: bool = False,
+                      stream: Optional[torch.cuda.Stream] = None) -> None:
+        ids = _dev_i32(ids, self.device)
+        N.check(self.lib.sckv_release_pages(self.handle, ids.data_ptr(), ids.numel(), 1 if keep_cached else 0,
+                                            _stream_ptr(stream)), "sckv_release_pages")
+
     def evict_lru(self, n: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         out = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
         N.check(self.lib.sckv_evict_lru(self.handle, n, out.data_ptr(), _stream_ptr(stream)), "sckv_evict_lru")
@@ -245,6 +319,11 @@ class KVPool:
                        max_blocks: Optional[int] = None, stream: Optional[torch.cuda.Stream] = None) -> None:
         n = ctx_lens.numel() if n_seqs is None else int(n_seqs)
         mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
+        _need(ctx_lens, "ctx_lens", self.device, torch.int32, n)
+        _need(block_table, "block_table", self.device, torch.int32, contiguous=False)
+        if block_table.dim() != 2 or block_table.stride(1) != 1 or block_table.shape[0] < n or \
+                mb > block_table.shape[1]:
+            raise ValueError("block_table must be [>= n_seqs, >= max_blocks] with unit column stride")
         N.check(self.lib.sckv_reserve_decode(self.handle, block_table.data_ptr(), block_table.stride(0), mb,
                                              ctx_lens.data_ptr(), n, _stream_ptr(stream)), "sckv_reserve_decode")
 

@@ -261,6 +261,81 @@ def sdpa_cases(ad, arrays):
     return out
 
 
+def scheduler_runs(ne, ad, arrays):
+    """The reference ContinuousBatchScheduler (engine/scheduler.py) over a
+    stub of the reference engine carrying the seeded weights of
+    tests/stub_model.py: real ModularAttentionEngine attention, real
+    NativeKVPrefixCache (stand-in bridge, fixed clock), one routed expert.
+    Runs the six requests batched (max_batch_size 4) and isolated."""
+    import types
+    import time as _time
+
+    sys.path.insert(0, str(OUT.parent))
+    from stub_model import CFG, make_weights, prompts  # noqa: E402
+    from engine import scheduler as sch  # noqa: E402
+
+    w = make_weights()
+    c = CFG
+    cfg = {"model_type": "olmoe", "num_hidden_layers": c["num_layers"], "num_experts": 1, "num_experts_per_tok": 1,
+           "hidden_size": c["hidden"], "intermediate_size": c["inter"], "num_attention_heads": c["hq"],
+           "num_key_value_heads": c["hkv"], "vocab_size": c["vocab"], "rms_norm_eps": c["rms_eps"],
+           "rope_theta": c["rope_theta"], "eos_token_id": 50279}
+    ne.time = types.SimpleNamespace(time=lambda: 0.0, perf_counter=_time.perf_counter)
+
+    def make_engine(tmp):
+        eng = types.SimpleNamespace()
+        eng.config = cfg
+        eng.num_layers = c["num_layers"]
+        eng.hidden_size = c["hidden"]
+        eng.rms_eps = c["rms_eps"]
+        eng.top_k = 1
+        eng.enable_merkle_kv = True
+        eng.active_merkle_root = GOLDEN_SEED_ROOT
+        eng.adapter = ad.OLMoEAdapter(cfg)
+        eng.attention_engine = ad.ModularAttentionEngine(eng.adapter.spec)
+        eng.kv_prefix_cache = ne.NativeKVPrefixCache(tmp, stand_in_bridge(ne), device="cpu",
+                                                     num_layers=c["num_layers"], num_kv_heads=c["hkv"],
+                                                     head_dim=c["head_dim"], max_pages=64, quant_mode="fp16")
+        eng.emb_np_view = w["emb"]
+        eng.lm_head_w_int8_view = w["lm_w_int8"]
+        eng.lm_head_s_fp16_view = w["lm_s_fp16"]
+        eng.core_np_views = {k: v for k, v in w.items() if k.startswith("model.")}
+        eng.live_routing_buffer = types.SimpleNamespace(record_numpy_layer=lambda l, idx: None)
+        eng._rmsnorm_numpy = types.MethodType(ne.NativeMerkleMoEEngine._rmsnorm_numpy, eng)
+        eng.forward_attention_layer_numpy = types.MethodType(ne.NativeMerkleMoEEngine.forward_attention_layer_numpy,
+                                                             eng)
+        eng.load_or_get_expert_entry = lambda l, e, is_prefetch=False: types.SimpleNamespace(
+            gate_w=w[f"model.layers.{l}.expert.gate"], up_w=w[f"model.layers.{l}.expert.up"],
+            down_w=w[f"model.layers.{l}.expert.down"])
+        return eng
+
+    ps = prompts()
+    out = {"prompts": ps}
+    try:
+        for mode, mbs in (("batched", 4), ("isolated", 1)):
+            tmp = Path(tempfile.mkdtemp(prefix="sckv_sched_"))
+            eng = make_engine(tmp)
+            s_ = sch.ContinuousBatchScheduler(eng, max_batch_size=mbs)
+            for i, pr in enumerate(ps):
+                s_.submit_request(f"req_{i}", pr, max_new_tokens=5, stop_token_ids=set())
+            steps = s_.run_until_complete_numpy()
+            done = s_.completed_requests
+            out[mode] = {
+                "generated": {k: list(map(int, v.generated_ids)) for k, v in done.items()},
+                "prefix_skipped": {k: int(v.kv_prefix_skipped) for k, v in done.items()},
+                "tokens_skipped": int(eng.kv_prefix_cache.tokens_skipped),
+                "blocks_loaded_from_arena": int(eng.kv_prefix_cache.blocks_loaded_from_arena),
+                "steps": len(steps),
+                "batch_sizes": [int(st["batch_size"]) for st in steps],
+            }
+            for k, v in done.items():
+                arrays[f"sched_{mode}_{k}_logits"] = v.last_logits.astype(np.float32)
+            shutil.rmtree(tmp, ignore_errors=True)
+    finally:
+        ne.time = _time
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -278,6 +353,7 @@ def main():
         "kv_table_kat": kv_table_kat(ne),
         "kv_table_long_context": kv_table_long_context(ne),
         "sdpa": sdpa_cases(ad, arrays),
+        "scheduler": scheduler_runs(ne, ad, arrays),
         "chain_hash": [ne.chain_merkle_prefix_hash(GOLDEN_SEED_ROOT, list(range(16))),
                        ne.chain_merkle_prefix_hash("00" * 32, [0] * 16),
                        ne.chain_merkle_prefix_hash("ff" * 32, [4294967295] * 16)],
