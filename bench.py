@@ -183,6 +183,20 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- our arm
+def local_workload(w, world: int, layout: str):
+    """Per-rank slice of the workload: the same sequences with Hkv/N kv heads
+    (and their query heads) under KV-head sharding; the full workload under
+    sequence sharding (each rank its own sequences)."""
+    if layout != "heads" or world == 1:
+        return dict(w)
+    if w["hkv"] % world:
+        raise SystemExit(f"--layout heads needs {w['hkv']} kv heads divisible by {world}")
+    lw = dict(w)
+    lw["hkv"] = w["hkv"] // world
+    lw["hq"] = w["hq"] // world
+    return lw
+
+
 def build_state(w, rank: int):
     from synapcore_b200.pool import KVPool
 
@@ -224,6 +238,7 @@ def build_state(w, rank: int):
 
 def run_step(w, s, attn_events=None):
     pool = s["pool"]
+    gather = s.get("gather")
     for l in range(w["layers"]):
         pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=l)
         if attn_events is not None:
@@ -233,11 +248,19 @@ def run_step(w, s, attn_events=None):
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
+        if gather is not None:
+            s["full"][l].copy_(gather.gather(s["out"][l]))
 
 
-def bench_ours(args, w, world, rank, local):
+def bench_ours(args, w_full, world, rank, local):
+    w = local_workload(w_full, world, args.layout)
     s = build_state(w, rank)
     pool = s["pool"]
+    if args.layout == "heads" and world > 1:
+        from synapcore_b200.distributed import HeadShardedOutput
+
+        s["gather"] = HeadShardedOutput(world)
+        s["full"] = torch.empty((w["layers"], w["batch"], w_full["hq"], w["d"]), dtype=w["qdt"], device="cuda")
     for _ in range(args.warmup):
         run_step(w, s)
     torch.cuda.synchronize()
@@ -268,7 +291,7 @@ def bench_ours(args, w, world, rank, local):
     h_q = s["q"].cpu().pin_memory()
     h_k = s["kn"].cpu().pin_memory()
     h_v = s["vn"].cpu().pin_memory()
-    h_out = torch.empty(s["out"].shape, dtype=s["out"].dtype).pin_memory()
+    h_out = torch.empty((s["full"] if "gather" in s else s["out"]).shape, dtype=s["out"].dtype).pin_memory()
     d_q, d_k, d_v = torch.empty_like(s["q"]), torch.empty_like(s["kn"]), torch.empty_like(s["vn"])
 
     def e2e_step():
@@ -278,7 +301,9 @@ def bench_ours(args, w, world, rank, local):
         for l in range(L):
             pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=l)
             pool.decode_attn(l, d_q[l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
-        h_out.copy_(s["out"], non_blocking=True)
+            if "gather" in s:
+                s["full"][l].copy_(s["gather"].gather(s["out"][l]))
+        h_out.copy_(s["full"] if "gather" in s else s["out"], non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -312,19 +337,23 @@ def bench_ours(args, w, world, rank, local):
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if (args.layout == "heads" and world > 1) else "weak",
         "vs_baseline": None,
         "dtype": w["kv"],
         "data": "synthetic (seeded N(0,1) KV pages, random block-table permutation)",
-        "tok_per_s": round(world * w["batch"] / (ms_step * 1e-3), 1),
+        "tok_per_s": round((w["batch"] if (args.layout == "heads" and world > 1) else world * w["batch"])
+                           / (ms_step * 1e-3), 1),
         "pct_hbm_peak": round(100.0 * value / world / peak, 2),
         "config": {
-            "workload": f"{args.workload}: paged decode attention, {w['model']} shape {w['layers']}L x "
-                        f"{w['hq']}q/{w['hkv']}kv heads x d{w['d']}, {w['kv']} KV, page 16, batch {w['batch']}/GPU, "
-                        f"context {w['ctx']}, pool {w['pool_pages']} all-layer pages",
-            "global_batch": world * w["batch"],
+            "workload": f"{args.workload}: paged decode attention, {w_full['model']} shape {w_full['layers']}L x "
+                        f"{w_full['hq']}q/{w_full['hkv']}kv heads x d{w_full['d']}, {w_full['kv']} KV, page 16, "
+                        f"batch {w_full['batch']}" + ("" if (args.layout == "heads" and world > 1) else "/GPU")
+                        + f", context {w_full['ctx']}, pool {w_full['pool_pages']} all-layer pages",
+            "global_batch": w["batch"] if (args.layout == "heads" and world > 1) else world * w["batch"],
             "seq_len": w["ctx"],
-            "parallelism": f"sequence-sharded x{world} (independent pools)",
+            "parallelism": (f"kv-head-sharded x{world} (NCCL all-gather of outputs per layer)"
+                            if (args.layout == "heads" and world > 1)
+                            else f"sequence-sharded x{world} (independent pools)"),
             "l2": "inputs larger than L2 (KV per layer launch >> 126 MB)",
         },
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
@@ -427,6 +456,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="olmoe")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layout", choices=["seq", "heads"], default="seq",
+                    help="multi-GPU layout: sequence sharding (default) or KV-head sharding")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     world, rank, local = dist_setup(args.gpus)

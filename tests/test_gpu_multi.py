@@ -1,0 +1,91 @@
+"""Two-GPU runs (skipped with fewer than 2 GPUs): KV-head-sharded decode
+attention with the NCCL all-gather equals the single-GPU result, and
+sequence-sharded pools run independently on each GPU."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(seed=0):
+    rng = np.random.default_rng(seed)
+    L, hq, hkv, D, P = 2, 16, 4, 128, 96
+    ctx = [37, 200, 513, 16]
+    k = rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)
+    v = rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)
+    mb = max((c + 15) // 16 for c in ctx)
+    bt = np.stack([rng.choice(P, size=mb, replace=False) for _ in ctx]).astype(np.int32)
+    q = rng.standard_normal((len(ctx), hq, D)).astype(np.float16)
+    return L, hq, hkv, D, P, ctx, k, v, bt, q
+
+
+def _worker(rank, world, port, out_path):
+    import torch.distributed as dist
+
+    from synapcore_b200.distributed import HeadShardedOutput, head_range, query_head_range
+    from synapcore_b200.pool import KVPool
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        L, hq, hkv, D, P, ctx, k, v, bt, q = _case()
+        kvr = head_range(hkv, world, rank)
+        qr = query_head_range(hq, hkv, world, rank)
+        pool = KVPool(L, len(kvr), D, P, "fp16", device=dev)
+        ids = torch.arange(P, dtype=torch.int32, device=dev)
+        pool.write_pages(ids, torch.from_numpy(np.ascontiguousarray(k[:, :, kvr.start:kvr.stop])).to(dev),
+                         torch.from_numpy(np.ascontiguousarray(v[:, :, kvr.start:kvr.stop])).to(dev))
+        bt_d = torch.from_numpy(bt).to(dev)
+        ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+        q_d = torch.from_numpy(np.ascontiguousarray(q[:, qr.start:qr.stop])).to(dev)
+        gather = HeadShardedOutput(world)
+        outs = []
+        for layer in range(L):
+            local = pool.decode_attn(layer, q_d, bt_d, ctx_d, out_dtype=torch.float32)
+            outs.append(gather.gather(local))
+        torch.cuda.synchronize()
+        pool.raise_on_status()
+        if rank == 0:
+            np.save(out_path, torch.stack(outs).cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_head_sharded_decode_equals_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from synapcore_b200.pool import KVPool
+
+    out = tmp_path / "sharded.npy"
+    mp.start_processes(_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True, start_method="spawn")
+    sharded = np.load(out)
+    L, hq, hkv, D, P, ctx, k, v, bt, q = _case()
+    dev = torch.device("cuda", 0)
+    pool = KVPool(L, hkv, D, P, "fp16", device=dev)
+    pool.write_pages(torch.arange(P, dtype=torch.int32, device=dev), torch.from_numpy(k).to(dev),
+                     torch.from_numpy(v).to(dev))
+    bt_d = torch.from_numpy(bt).to(dev)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    for layer in range(L):
+        full = pool.decode_attn(layer, torch.from_numpy(q).to(dev), bt_d, ctx_d, out_dtype=torch.float32)
+        ref = full.cpu().numpy()
+        got = sharded[layer]
+        assert np.max(np.abs(got - ref)) <= 2e-3 * np.max(np.abs(ref))
