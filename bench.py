@@ -161,6 +161,9 @@ def dist_setup(n_gpus: int):
     if world > 1:
         import datetime
 
+        # NCCL's own messages (e.g. its version banner) go to stderr so that
+        # stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device(f"cuda:{local}"))
