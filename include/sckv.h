@@ -183,6 +183,25 @@ SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_d
                      void* workspace, size_t workspace_bytes, int chunk_pages,
                      void* stream);
 
+/* Causal prefill attention: for each of n_seqs sequences, the query tokens
+ * cu_q[b] .. cu_q[b+1]-1 sit at positions start_pos[b] + i and attend to
+ * every token of that sequence at positions <= their own (the new tokens'
+ * K/V must already be appended). Replaces the prompt pass of
+ * ModularAttentionEngine.forward_numpy with its causal mask
+ * (models/adapters.py:1209-1229, mask at :1218-1224).
+ * q/out : [n_tokens][num_q_heads][head_dim]; cu_q int32 [n_seqs+1];
+ * start_pos int32 [n_seqs]; block_table [n_seqs][bt_stride] (device).
+ * Tensor cores (mma.m16n8k16, fp32 accumulation) over TMA-staged pages.
+ * Pools F16, BF16 (bf16 queries only) and FP8_E4M3 (even num_kv_heads);
+ * num_q_heads / num_kv_heads must be a power of two <= 16; otherwise
+ * SCKV_ERR_UNSUPPORTED. */
+SCKV_API int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q,
+                      int q_dtype, int num_q_heads, int n_seqs, int n_tokens,
+                      const int32_t* cu_q, const int32_t* start_pos,
+                      const int32_t* block_table, int64_t bt_stride,
+                      int max_blocks, float scale, void* out, int out_dtype,
+                      void* stream);
+
 /* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
 #define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)
 

@@ -134,6 +134,16 @@ def sdpa_decode(q_f32: np.ndarray, k_f16: np.ndarray, v_f16: np.ndarray, scale: 
     return (p @ v)[:, 0, :]
 
 
+def sdpa_prefill(q_f32: np.ndarray, k: np.ndarray, v: np.ndarray, start: int,
+                 scale: Optional[float] = None) -> np.ndarray:
+    """Causal prompt pass (models/adapters.py:1209-1229 with the -1e9 mask of
+    :1218-1224): query t at position start+t sees keys 0..start+t. The -1e9
+    mask makes masked probabilities exactly 0 in fp32, so each row is the
+    decode SDPA over its visible prefix. q [T, Hq, D]; k, v [Hkv, ctx, D]."""
+    return np.stack([sdpa_decode(q_f32[t], k[:, :start + t + 1], v[:, :start + t + 1], scale)
+                     for t in range(q_f32.shape[0])])
+
+
 # --------------------------------------------------------------------------
 # PagedKVArena restatement — native/native_engine.py:224-432
 # --------------------------------------------------------------------------
@@ -454,6 +464,22 @@ class PagedPoolOracle:
                 self.scales[:, d] = self.scales[:, s]
 
     # ---- paged decode attention over block tables (kernels 3+4)
+    def prefill(self, layer: int, q: np.ndarray, cu_q: Sequence[int], start_pos: Sequence[int],
+                block_table: np.ndarray, scale: Optional[float] = None) -> np.ndarray:
+        """q [n_tokens][Hq][D] float32 values; sequence b owns rows
+        cu_q[b]..cu_q[b+1]-1 at positions start_pos[b]+i -> causal SDPA
+        (sdpa_prefill) over the gathered pages, [n_tokens][Hq][D] float32."""
+        out = np.zeros(q.shape, np.float32)
+        for b in range(len(cu_q) - 1):
+            t0, t1, st = int(cu_q[b]), int(cu_q[b + 1]), int(start_pos[b])
+            if t1 == t0:
+                continue
+            ctx = st + t1 - t0
+            n_pages = (ctx + PAGE_TOKENS - 1) // PAGE_TOKENS
+            k, v = self.gather(layer, 1, block_table[b, :n_pages], ctx)
+            out[t0:t1] = sdpa_prefill(q[t0:t1].astype(np.float32), k[0], v[0], st, scale)
+        return out
+
     def decode(self, layer: int, q: np.ndarray, block_table: np.ndarray, ctx_lens: np.ndarray,
                scale: Optional[float] = None) -> np.ndarray:
         """q [B][Hq][D] float32 values -> [B][Hq][D] float32 via sdpa_decode

@@ -26,27 +26,12 @@
 #include <math.h>
 
 #include "sckv_decode_common.cuh"
+#include "sckv_mma_common.cuh"
 
 using namespace sckv_detail;
+using namespace sckv_mma;
 
 namespace {
-
-constexpr int kBoxBytes = 16 * 128;  // one TMA box: 16 rows x 128 bytes (swizzled)
-
-template <int KVDT>
-struct MmaKV;
-template <>
-struct MmaKV<SCKV_DTYPE_F16> {
-  static constexpr int kEB = 2;
-};
-template <>
-struct MmaKV<SCKV_DTYPE_BF16> {
-  static constexpr int kEB = 2;
-};
-template <>
-struct MmaKV<SCKV_DTYPE_FP8_E4M3> {
-  static constexpr int kEB = 1;
-};
 
 // One stage = one page of HG kv heads: for each 128-byte column block of the
 // head dim (1 for FP8, 2 for 16-bit), a TMA box [K|V][HG heads][16 tok][128 B]
@@ -63,96 +48,6 @@ struct MmaSmem {
   static constexpr int kScaleBytes = (KVDT == SCKV_DTYPE_FP8_E4M3) ? S * kScaleSlot * 4 : 0;
   static constexpr int kBytes = 1024 + kRingBytes + kScaleBytes + 2 * S * 8 + kRedFloats * 4 + 16;
 };
-
-// Byte address of (row, byte) inside a 128-byte-swizzled 16 x 128 B box.
-__device__ __forceinline__ uint32_t swz(uint32_t box, int row, int byte) {
-  return box + row * 128 + ((((byte >> 4) ^ (row & 7))) << 4) + (byte & 15);
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
-  uint32_t d;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
-  return d;
-}
-
-template <bool BF16>
-__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  if (BF16) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  }
-}
-
-__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two_bytes) {
-  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_bytes & 0xffffu), __NV_E4M3);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Four e4m3 bytes -> two f16x2: bytes (0,1) -> lo, bytes (2,3) -> hi (exact).
-__device__ __forceinline__ void cvt_fp8x4(uint32_t x, uint32_t& lo, uint32_t& hi) {
-  asm("{\n\t.reg .b16 l16, h16;\n\tmov.b32 {l16, h16}, %2;\n\t"
-      "cvt.rn.f16x2.e4m3x2 %0, l16;\n\tcvt.rn.f16x2.e4m3x2 %1, h16;\n\t}"
-      : "=r"(lo), "=r"(hi)
-      : "r"(x));
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  if (BF16) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-  __half2 v = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-template <bool BF16>
-__device__ __forceinline__ float round16(float x) {
-  return BF16 ? __bfloat162float(__float2bfloat16_rn(x)) : __half2float(__float2half_rn(x));
-}
-
-// Keep the f16/bf16 halves of `r` whose tokens are < nv.
-__device__ __forceinline__ uint32_t mask_pair(uint32_t r, int tok_lo, int tok_hi, int nv) {
-  const uint32_t m = (tok_lo < nv ? 0x0000ffffu : 0u) | (tok_hi < nv ? 0xffff0000u : 0u);
-  return r & m;
-}
-
-// 5-D tiled TMA load; coordinates (dim, token, head, K|V, slab).
-__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int x, int tok, int head, int kv,
-                                            int slab, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
-      "%6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(tok), "r"(head), "r"(kv), "r"(slab), "r"(smem_u32(bar))
-      : "memory");
-}
 
 template <int KVDT, int NQT, int HG, int S>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -568,38 +463,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// Encode the pool's tensor map once: a 5-D view (dim, token, head, K|V,
-// layer*page slab) with boxes of 128 bytes x 16 tokens x HG heads x K and V,
-// 128-byte swizzle.
-int ensure_tmap(const sckv_pool* cpool, int HG) {
-  sckv_pool* pool = const_cast<sckv_pool*>(cpool);
-  if (pool->tmap_ready == HG) return SCKV_OK;
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  if (encode == nullptr) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || fn == nullptr)
-      return SCKV_ERR_CUDA;
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
-  const cuuint64_t eb = (cuuint64_t)sckv_elem_bytes(pool->kv_dtype);
-  const cuuint64_t D = (cuuint64_t)pool->head_dim, H = (cuuint64_t)pool->num_kv_heads;
-  const cuuint64_t dims[5] = {D, (cuuint64_t)SCKV_PAGE_TOKENS, H, 2,
-                              (cuuint64_t)pool->num_layers * (cuuint64_t)pool->max_pages};
-  const cuuint64_t strides[4] = {D * eb, SCKV_PAGE_TOKENS * D * eb, H * SCKV_PAGE_TOKENS * D * eb,
-                                 2 * H * SCKV_PAGE_TOKENS * D * eb};
-  const cuuint32_t box[5] = {(cuuint32_t)(128 / eb), (cuuint32_t)SCKV_PAGE_TOKENS, (cuuint32_t)HG, 2, 1};
-  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  const CUtensorMapDataType dt = (eb == 2) ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUresult r = encode(reinterpret_cast<CUtensorMap*>(pool->tmap_kv), dt, 5, pool->data, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return SCKV_ERR_CUDA;
-  pool->tmap_ready = HG;
-  return SCKV_OK;
-}
-
 template <int KVDT, int NQT, int HG, int S>
 int launch_mma(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t stream) {
   using SM = MmaSmem<KVDT, NQT, HG, S>;
@@ -607,7 +470,8 @@ int launch_mma(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t stre
   static bool configured[64] = {};
   const int dev = pool->device;
   if (dev < 0 || dev >= 64) return SCKV_ERR_INVALID_ARG;
-  const int rc = ensure_tmap(pool, HG);
+  sckv_pool* mp = const_cast<sckv_pool*>(pool);  // the map is a cache inside the handle
+  const int rc = ensure_tmap(pool, HG, mp->tmap_kv, &mp->tmap_ready);
   if (rc != SCKV_OK) return rc;
   if (!configured[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes) != cudaSuccess)

@@ -72,7 +72,10 @@ struct sckv_pool {
   // TMA tensor map over the page data (a CUtensorMap, encoded on first use
   // by the tensor-core decode kernel).
   alignas(64) unsigned char tmap_kv[128];
-  int tmap_ready;
+  int tmap_ready;  // head-group size the map was encoded for (0 = not yet)
+  // A second map with one-head boxes (prefill attention).
+  alignas(64) unsigned char tmap_kv1[128];
+  int tmap1_ready;
 };
 
 static inline int sckv_elem_bytes(int dtype) {

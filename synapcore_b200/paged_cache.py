@@ -21,6 +21,7 @@ from typing import Dict, Hashable, List, Optional, Sequence, Tuple
 
 import torch
 
+from . import _native as N
 from .pool import KVPool, PAGE_TOKENS
 
 
@@ -143,7 +144,18 @@ class PagedKVCache:
         <= start+t. q [T, Hq, D] -> [T, Hq, D]."""
         r = self.row_of[seq_id]
         T = q.shape[0]
-        bt = self.block_table[r:r + 1].expand(T, self.max_blocks)  # stride 0: every token reads row r
+        cu = torch.tensor([0, T], dtype=torch.int32, device=self.device)
+        st = torch.tensor([start], dtype=torch.int32, device=self.device)
+        try:
+            return self.pool.prefill_attn(layer, q, cu, st, self.block_table[r:r + 1], scale=scale,
+                                          out_dtype=out_dtype, max_blocks=self.max_blocks)
+        except N.SCKVError as e:
+            if e.code != N.SCKV_ERR_UNSUPPORTED:
+                raise
+        # combinations the tensor-core prefill kernel does not build (int8
+        # pools, non-power-of-two groups): token t is a decode query of length
+        # start+t+1 over the same row (block-table stride 0)
+        bt = self.block_table[r:r + 1].expand(T, self.max_blocks)
         ctx = torch.arange(start + 1, start + T + 1, dtype=torch.int32, device=self.device)
         return self.pool.decode_attn(layer, q, bt, ctx, scale=scale, out_dtype=out_dtype,
                                      max_blocks=self.max_blocks, chunk_pages=self.chunk_pages)

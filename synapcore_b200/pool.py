@@ -277,6 +277,44 @@ class KVPool:
                 "sckv_decode_attn")
         return out
 
+    def prefill_attn(self, layer: int, q: torch.Tensor, cu_q: torch.Tensor, start_pos: torch.Tensor,
+                     block_table: torch.Tensor, scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                     out_dtype: Optional[torch.dtype] = None, max_blocks: Optional[int] = None,
+                     stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Causal attention of new query tokens q [n_tokens, Hq, D] (sequence b
+        owns rows cu_q[b]..cu_q[b+1]-1 at positions start_pos[b]+i) over their
+        sequences' pages. Raises SCKVError(SCKV_ERR_UNSUPPORTED) for pool /
+        head combinations the tensor-core kernel does not build."""
+        q = q.contiguous()
+        n_tok, hq, d = q.shape
+        n_seqs = cu_q.numel() - 1
+        mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
+        if d != self.head_dim or hq % self.num_kv_heads != 0:
+            raise ValueError(f"q must be [n_tokens, k*{self.num_kv_heads}, {self.head_dim}]")
+        if not 0 <= layer < self.num_layers:
+            raise ValueError("layer out of range")
+        _need(q, "q", self.device)
+        _need(cu_q, "cu_q", self.device, torch.int32, 2)
+        _need(start_pos, "start_pos", self.device, torch.int32, n_seqs)
+        _need(block_table, "block_table", self.device, torch.int32, contiguous=False)
+        if block_table.dim() != 2 or block_table.stride(1) != 1 or block_table.shape[0] < n_seqs or \
+                mb > block_table.shape[1] or block_table.stride(0) < mb:
+            raise ValueError("block_table must be [>= n_seqs, >= max_blocks] rows with unit column stride")
+        if scale is None:
+            scale = float(d) ** -0.5
+        if out is None:
+            out = torch.empty((n_tok, hq, d), dtype=out_dtype or q.dtype, device=self.device)
+        else:
+            _need(out, "out", self.device)
+            if tuple(out.shape) != (n_tok, hq, d):
+                raise ValueError("out must have q's shape")
+        N.check(self.lib.sckv_prefill_attn(self.handle, layer, q.data_ptr(), torch_dtype_code(q.dtype), hq, n_seqs,
+                                           n_tok, cu_q.data_ptr(), start_pos.data_ptr(), block_table.data_ptr(),
+                                           block_table.stride(0), mb, float(scale), out.data_ptr(),
+                                           torch_dtype_code(out.dtype), _stream_ptr(stream)),
+                "sckv_prefill_attn")
+        return out
+
     # ---------------------------------------------------------------- kernel 5
     def alloc_reset(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         N.check(self.lib.sckv_alloc_reset(self.handle, _stream_ptr(stream)), "sckv_alloc_reset")
