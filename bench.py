@@ -1,19 +1,26 @@
 #!/usr/bin/env python3
 """Paged decode-attention benchmark (B200).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload olmoe|qwen3-fp8]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads (synthetic, seeded):
-  olmoe      16 layers x 16 KV heads (MHA), head_dim 128, fp16, 16-token pages,
-             64 sequences x context 4096 per GPU, one query token per
-             sequence, block tables a random permutation of a pool of 18,750
-             all-layer pages (= 300,000 layer-pages of 128 KiB).
-  qwen3-fp8  36 layers, 32 query / 8 KV heads, head_dim 128, FP8-e4m3 KV with
-             per-page fp32 scales, bf16 queries, 128 sequences x context 16384.
+  olmoe       16 layers x 16 KV heads (MHA), head_dim 128, fp16, 16-token pages,
+              64 sequences x context 4096 per GPU, one query token per
+              sequence, block tables a random permutation of a pool of 18,750
+              all-layer pages (= 300,000 layer-pages of 128 KiB).
+  qwen3-fp8   36 layers, 32 query / 8 KV heads, head_dim 128, FP8-e4m3 KV with
+              per-page fp32 scales, bf16 queries, 128 sequences x context 16384.
+  qwen3-long  36 layers, 32 / 8 heads, bf16 KV and queries, 64 sequences per
+              GPU with contexts ~U[8192, 32768] that grow by one token per
+              step; 100 GB of physical layers per GPU, logical layer l reads
+              physical layer l mod Lp (the full KV of 512 such sequences,
+              ~1.55 TB, exceeds the box).
+  *-small     profiling-sized variants (2 layers, a few hundred MB).
 
 A step = for every layer: append one new K/V token per sequence (scatter
 through the block table), then paged decode attention for every sequence.
-The step keeps the context fixed (the new token rewrites slot ctx-1).
+Fixed-context workloads keep the context (the new token rewrites slot
+ctx-1); growing ones append at slot ctx and attend over ctx+1 tokens.
 
 One JSON line on rank 0. `value` = KV GB/s over all ranks (algorithmic bytes
 of attention + append per step / step time, inputs resident in HBM). `e2e`
@@ -57,6 +64,15 @@ WORKLOADS = {
                         qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
     "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                             qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
+    # long-context scale-out: 64 sequences per GPU, context ~U[8192, 32768],
+    # every step appends one token per sequence (contexts grow). bf16 KV of
+    # 512 such sequences is ~1.55 TB, above one 8-GPU box, so each GPU keeps
+    # `pool_gb` of physical layers and logical layer l reads layer l mod Lp
+    # (every launch still streams its own >> L2 bytes from HBM).
+    "qwen3-long": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="bf16", qdt=torch.bfloat16,
+                       batch=64, ctx=(8192, 32768), grow=True, pool_gb=100.0),
+    "qwen3-long-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="bf16",
+                             qdt=torch.bfloat16, batch=8, ctx=(8192, 32768), grow=True, pool_gb=4.0),
 }
 
 
@@ -64,14 +80,19 @@ def kv_bytes_per_elem(kv: str) -> int:
     return 2 if kv in ("fp16", "bf16") else 1
 
 
-def attn_bytes_per_launch(w) -> int:
-    """Algorithmic bytes one decode-attention launch must move."""
-    B, T, hkv, hq, d = w["batch"], w["ctx"], w["hkv"], w["hq"], w["d"]
+def attn_bytes_per_launch(w, ctx=None) -> int:
+    """Algorithmic bytes one decode-attention launch must move: every
+    sequence's K and V (plus FP8 page scales and block-table entries) once,
+    its query row in and its output row out. `ctx` = per-sequence context
+    lengths (default: the workload's uniform context)."""
+    hkv, hq, d = w["hkv"], w["hq"], w["d"]
+    c = np.full(w["batch"], w["ctx"], np.int64) if ctx is None else np.asarray(ctx, np.int64)
+    pages = (c + PAGE - 1) // PAGE
     b = kv_bytes_per_elem(w["kv"])
-    kv = B * T * hkv * d * 2 * b
-    scales = B * (T // PAGE) * hkv * 2 * 4 if w["kv"] == "fp8_e4m3" else 0
-    bt = B * (T // PAGE) * 4
-    qo = B * hq * d * 2 * 2
+    kv = int(c.sum()) * hkv * d * 2 * b
+    scales = int(pages.sum()) * hkv * 2 * 4 if w["kv"] == "fp8_e4m3" else 0
+    bt = int(pages.sum()) * 4
+    qo = len(c) * hq * d * 2 * 2
     return kv + scales + bt + qo
 
 
@@ -200,19 +221,56 @@ def local_workload(w, world: int, layout: str):
     return lw
 
 
-def build_state(w, rank: int):
+def ctx_desc(w) -> str:
+    if isinstance(w["ctx"], tuple):
+        g = " growing 1/step" if w.get("grow") else ""
+        return f"~U[{w['ctx'][0]},{w['ctx'][1]}]{g}"
+    return str(w["ctx"])
+
+
+def mean_ctx(w) -> int:
+    return int(np.mean(w["ctx"])) if isinstance(w["ctx"], tuple) else int(w["ctx"])
+
+
+def seq_contexts(w, rank: int) -> np.ndarray:
+    """Per-sequence starting context lengths (uniform or ~U[lo, hi], seeded per rank)."""
+    if isinstance(w["ctx"], tuple):
+        lo, hi = w["ctx"]
+        return np.random.default_rng(100 + rank).integers(lo, hi + 1, size=w["batch"]).astype(np.int64)
+    return np.full(w["batch"], w["ctx"], np.int64)
+
+
+def build_state(w, rank: int, grow_steps: int = 0):
+    """Pool, block tables and per-layer inputs of one rank.
+
+    Fixed-context workloads: the step's new token rewrites slot ctx-1, so
+    every step moves the same bytes. Growing workloads (`grow`): the new
+    token goes to slot ctx and contexts advance by one per step; block tables
+    have room for `grow_steps` more tokens and `reset()` rewinds them."""
     from synapcore_b200.pool import KVPool
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    L, hq, hkv, d, B, T = w["layers"], w["hq"], w["hkv"], w["d"], w["batch"], w["ctx"]
-    pool = KVPool(L, hkv, d, w["pool_pages"], w["kv"], device=dev)
+    L, hq, hkv, d, B = w["layers"], w["hq"], w["hkv"], w["d"], w["batch"]
+    grow = bool(w.get("grow"))
+    ctx0 = seq_contexts(w, rank)
+    cap = ctx0 + (grow_steps + 1 if grow else 0)
+    n_blocks = (cap + PAGE - 1) // PAGE
+    max_blocks = int(n_blocks.max())
+    if "pool_pages" in w:
+        pool_pages = int(w["pool_pages"])
+        n_phys = L
+    else:
+        pool_pages = int(n_blocks.sum()) + 64
+        layer_bytes = pool_pages * 2 * hkv * PAGE * d * kv_bytes_per_elem(w["kv"])
+        n_phys = max(1, min(L, int(w["pool_gb"] * 1e9 // layer_bytes)))
+    pool = KVPool(n_phys, hkv, d, pool_pages, w["kv"], device=dev)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     view = pool.pool_view()
     if w["kv"] == "fp8_e4m3":
         # random e4m3 codes (no NaN bytes 0x7f / 0xff) and per-page-head scales U[0.5,4]/448*4
-        for l in range(L):
-            for c0 in range(0, w["pool_pages"], 8192):
+        for l in range(n_phys):
+            for c0 in range(0, pool_pages, 8192):
                 blk = view[l, c0:c0 + 8192]
                 codes = torch.randint(0, 0x7F, blk.shape, dtype=torch.uint8, device=dev, generator=g)
                 codes |= torch.randint(0, 2, blk.shape, dtype=torch.uint8, device=dev, generator=g) << 7
@@ -220,44 +278,76 @@ def build_state(w, rank: int):
                 del codes
         pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
     else:
-        for l in range(L):
-            view[l].normal_(generator=g)
-    n_blocks = T // PAGE
+        for l in range(n_phys):
+            for c0 in range(0, pool_pages, 8192):
+                view[l, c0:c0 + 8192].normal_(generator=g)
     rng = np.random.default_rng(rank)
-    perm = rng.permutation(w["pool_pages"])[: B * n_blocks].astype(np.int32)
-    bt = torch.from_numpy(perm.reshape(B, n_blocks)).to(dev)
-    ctx = torch.full((B,), T, dtype=torch.int32, device=dev)
+    perm = rng.permutation(pool_pages)[: int(n_blocks.sum())].astype(np.int32)
+    bt_h = np.zeros((B, max_blocks), np.int32)
+    off = 0
+    for b in range(B):
+        bt_h[b, : n_blocks[b]] = perm[off: off + n_blocks[b]]
+        off += n_blocks[b]
+    bt = torch.from_numpy(bt_h).to(dev)
+    # attention context after the step's append, and the append slot
+    ctx_attn0 = ctx0 + 1 if grow else ctx0
+    ctx = torch.from_numpy(ctx_attn0.astype(np.int32)).to(dev)
+    start = torch.from_numpy((ctx_attn0 - 1).astype(np.int32)).to(dev)
     cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
-    start = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
     q = torch.randn((L, B, hq, d), generator=g, device=dev).to(w["qdt"])
     src_dt = torch.float16 if w["kv"] == "fp16" else torch.bfloat16
     kn = torch.randn((L, B, hkv, d), generator=g, device=dev).to(src_dt)
     vn = torch.randn((L, B, hkv, d), generator=g, device=dev).to(src_dt)
     out = torch.empty((L, B, hq, d), dtype=w["qdt"], device=dev)
-    ws = torch.empty(pool.decode_workspace_bytes(B, hq, n_blocks), dtype=torch.uint8, device=dev)
+    ws = torch.empty(pool.decode_workspace_bytes(B, hq, max_blocks), dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
-    return dict(pool=pool, bt=bt, ctx=ctx, cu=cu, start=start, q=q, kn=kn, vn=vn, out=out, ws=ws)
+    st = dict(pool=pool, bt=bt, ctx=ctx, cu=cu, start=start, q=q, kn=kn, vn=vn, out=out, ws=ws,
+              n_phys=n_phys, grow=grow, ctx0=ctx0, ctx_host=ctx_attn0.copy(), max_blocks=max_blocks,
+              pool_pages=pool_pages)
+    return st
+
+
+def reset_contexts(s):
+    """Rewind growing contexts to their starting lengths."""
+    if s["grow"]:
+        s["ctx"].copy_(torch.from_numpy((s["ctx0"] + 1).astype(np.int32)))
+        s["start"].copy_(torch.from_numpy(s["ctx0"].astype(np.int32)))
+        s["ctx_host"] = s["ctx0"] + 1
+
+
+def step_bytes(w, s) -> int:
+    """Algorithmic bytes of the next step (attention at the current contexts + appends)."""
+    return w["layers"] * (attn_bytes_per_launch(w, s["ctx_host"]) + append_bytes_per_launch(w))
+
+
+def advance(s):
+    if s["grow"]:
+        s["ctx"] += 1
+        s["start"] += 1
+        s["ctx_host"] = s["ctx_host"] + 1
 
 
 def run_step(w, s, attn_events=None):
     pool = s["pool"]
     gather = s.get("gather")
     for l in range(w["layers"]):
-        pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=l)
+        pl = l % s["n_phys"]
+        pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
-        pool.decode_attn(l, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
+        pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
         if gather is not None:
             s["full"][l].copy_(gather.gather(s["out"][l]))
+    advance(s)
 
 
 def bench_ours(args, w_full, world, rank, local):
     w = local_workload(w_full, world, args.layout)
-    s = build_state(w, rank)
+    s = build_state(w, rank, grow_steps=max(args.steps, args.warmup))
     pool = s["pool"]
     if args.layout == "heads" and world > 1:
         from synapcore_b200.distributed import HeadShardedOutput
@@ -268,6 +358,9 @@ def bench_ours(args, w_full, world, rank, local):
         run_step(w, s)
     torch.cuda.synchronize()
     pool.raise_on_status()
+    reset_contexts(s)
+    total_bytes = 0
+    launch_bytes = []
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
@@ -279,6 +372,8 @@ def bench_ours(args, w_full, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
+        total_bytes += step_bytes(w, s)
+        launch_bytes.append(attn_bytes_per_launch(w, s["ctx_host"]))
         run_step(w, s, attn_ev)
     e1.record()
     torch.cuda.synchronize()
@@ -302,15 +397,19 @@ def bench_ours(args, w_full, world, rank, local):
         d_k.copy_(h_k, non_blocking=True)
         d_v.copy_(h_v, non_blocking=True)
         for l in range(L):
-            pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=l)
-            pool.decode_attn(l, d_q[l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
+            pl = l % s["n_phys"]
+            pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=pl)
+            pool.decode_attn(pl, d_q[l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
             if "gather" in s:
                 s["full"][l].copy_(s["gather"].gather(s["out"][l]))
         h_out.copy_(s["full"] if "gather" in s else s["out"], non_blocking=True)
+        advance(s)
 
+    reset_contexts(s)
     for _ in range(max(1, args.warmup)):
         e2e_step()
     torch.cuda.synchronize()
+    reset_contexts(s)
     barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
@@ -324,12 +423,13 @@ def bench_ours(args, w_full, world, rank, local):
     d2h = h_out.numel() * h_out.element_size()
     pool.raise_on_status()
 
-    step_bytes = L * (attn_bytes_per_launch(w) + append_bytes_per_launch(w))
     ms_step = ms_total / args.steps
-    value = world * step_bytes / (ms_step * 1e-3) / 1e9
-    e2e_value = world * step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+    # the e2e pass replays the same context sequence, so it moves the same bytes
+    value = world * total_bytes / (ms_total * 1e-3) / 1e9
+    e2e_value = world * total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak_gbs()
-    achieved = attn_bytes_per_launch(w) / (attn_avg_ms * 1e-3) / 1e9
+    avg_launch_bytes = float(np.mean(launch_bytes))
+    achieved = avg_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
     traffic = profiled_traffic(args.workload)
     res = {
         "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
@@ -351,9 +451,11 @@ def bench_ours(args, w_full, world, rank, local):
             "workload": f"{args.workload}: paged decode attention, {w_full['model']} shape {w_full['layers']}L x "
                         f"{w_full['hq']}q/{w_full['hkv']}kv heads x d{w_full['d']}, {w_full['kv']} KV, page 16, "
                         f"batch {w_full['batch']}" + ("" if (args.layout == "heads" and world > 1) else "/GPU")
-                        + f", context {w_full['ctx']}, pool {w_full['pool_pages']} all-layer pages",
+                        + f", context {ctx_desc(w_full)}, pool {s['pool_pages']} pages x {s['n_phys']} layers"
+                        + (f" (logical layer l reads physical layer l mod {s['n_phys']})"
+                           if s["n_phys"] < w["layers"] else ""),
             "global_batch": w["batch"] if (args.layout == "heads" and world > 1) else world * w["batch"],
-            "seq_len": w["ctx"],
+            "seq_len": ctx_desc(w_full),
             "parallelism": (f"kv-head-sharded x{world} (NCCL all-gather of outputs per layer)"
                             if (args.layout == "heads" and world > 1)
                             else f"sequence-sharded x{world} (independent pools)"),
@@ -364,8 +466,9 @@ def bench_ours(args, w_full, world, rank, local):
         "gpu_launches": int(args.steps * L * 3),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "decode_kernel (+combine) per layer launch",
-                     "bytes_per_launch": attn_bytes_per_launch(w), "avg_launch_ms": round(attn_avg_ms, 4)},
+                     "kernel": ("decode_mma_kernel" if w["hq"] // w["hkv"] >= 2 else "decode_kernel")
+                               + " (+combine) per layer launch",
+                     "bytes_per_launch": int(avg_launch_bytes), "avg_launch_ms": round(attn_avg_ms, 4)},
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -391,14 +494,15 @@ def cpu_baseline(w, budget_s: float = 15.0):
     from oracle.kv_oracle import sdpa_decode
 
     n_seqs = 8
-    q, k, v = cpu_sample(w, n_seqs, w["ctx"])
+    T = mean_ctx(w)
+    q, k, v = cpu_sample(w, n_seqs, T)
     if w["kv"] == "fp8_e4m3":
         from oracle.kv_oracle import fp8_decode, fp8_encode
 
         s = (np.abs(k.astype(np.float32)).max(axis=(2, 3), keepdims=True) / 448).astype(np.float32)
         kc = fp8_encode(k.astype(np.float32) / s)
         vc = fp8_encode(v.astype(np.float32) / s)
-    per_call_bytes = n_seqs * w["ctx"] * w["hkv"] * w["d"] * 2 * kv_bytes_per_elem(w["kv"])
+    per_call_bytes = n_seqs * T * w["hkv"] * w["d"] * 2 * kv_bytes_per_elem(w["kv"])
     reps, t0 = 0, time.perf_counter()
     while True:
         for b in range(n_seqs):
@@ -415,8 +519,9 @@ def cpu_baseline(w, budget_s: float = 15.0):
     gbs = reps * per_call_bytes / el / 1e9
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
             or (os.cpu_count() or 1), "kind": "port",
-            "sample": f"1 layer x {n_seqs} seqs x ctx {w['ctx']} ({w['kv']} KV), {reps} reps in {el:.1f}s; "
-                      f"tok/s extrapolated to the full step = {w['batch'] * gbs * 1e9 / (w['layers'] * attn_bytes_per_launch(w)):.3f}"}
+            "sample": f"1 layer x {n_seqs} seqs x ctx {T} ({w['kv']} KV), {reps} reps in {el:.1f}s; "
+                      f"tok/s extrapolated to the full step = "
+                      f"{w['batch'] * gbs * 1e9 / (w['layers'] * attn_bytes_per_launch(w, [T] * w['batch'])):.3f}"}
 
 
 def bench_reference(args, w, world, rank):
@@ -443,9 +548,9 @@ def bench_reference(args, w, world, rank):
         "dtype": w["kv"],
         "data": "synthetic (seeded)",
         "config": {"workload": f"{args.workload}: reference NumPy decode SDPA on a bounded host sample",
-                   "global_batch": w["batch"], "seq_len": w["ctx"], "parallelism": "host cores"},
+                   "global_batch": w["batch"], "seq_len": ctx_desc(w), "parallelism": "host cores"},
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"per step: 1 layer x 8 seqs x ctx {w['ctx']}, ~{args.cpu_seconds / max(1, args.steps):.1f}s"},
+                         "sample": f"per step: 1 layer x 8 seqs x ctx {mean_ctx(w)}, ~{args.cpu_seconds / max(1, args.steps):.1f}s"},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

@@ -175,7 +175,9 @@ SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
  * chunk_pages : pages per split (split-K unit); <= 0 picks one. A fixed
  *               value makes each sequence's result independent of the batch.
  * workspace   : device scratch of sckv_decode_workspace_bytes bytes.
- * Pool dtypes F16, BF16, FP8_E4M3; accumulation is fp32. */
+ * Pool dtypes F16, BF16, FP8_E4M3 (per-page-head scale) and INT8
+ * (per-token fp16 scales, num_q_heads / num_kv_heads in {1, 2, 4, 8});
+ * accumulation is fp32. */
 SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype,
                      int num_q_heads, const int32_t* block_table,
                      int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
@@ -319,6 +321,10 @@ SCKV_API int sckv_kv_insert(uint8_t* table, const uint8_t* prefix_hash32,
 /* Misc                                                                        */
 /* ========================================================================== */
 SCKV_API const char* sckv_version(void);
+/* Where the calling thread's last SCKV_ERR_CUDA came from
+ * ("file:line call: CUDA error name"); "" if none. No reference counterpart
+ * (the reference's native calls report only status codes). */
+SCKV_API const char* sckv_last_error(void);
 SCKV_API const char* sckv_status_string(int code);
 
 #ifdef __cplusplus

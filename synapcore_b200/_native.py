@@ -93,6 +93,7 @@ _SIGNATURES = [
     ("sckv_kv_lookup", c_int, [c_void_p, c_void_p, POINTER(c_uint32)]),
     ("sckv_kv_insert", c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_double, c_void_p, POINTER(c_uint64)]),
     ("sckv_version", ctypes.c_char_p, []),
+    ("sckv_last_error", ctypes.c_char_p, []),
     ("sckv_status_string", ctypes.c_char_p, [c_int]),
 ]
 
@@ -138,6 +139,10 @@ def check(rc: int, where: str) -> None:
         raise SCKVPoolExhausted(rc, where)
     if rc == SCKV_ERR_BOUNDS:
         raise SCKVBoundsError(rc, where)
+    if rc == SCKV_ERR_CUDA and _lib is not None:
+        detail = (_lib.sckv_last_error() or b"").decode(errors="replace")
+        if detail:
+            where = f"{where} [{detail}]"
     raise SCKVError(rc, where)
 
 

@@ -506,8 +506,7 @@ __global__ void __launch_bounds__(kT) reserve_kernel(AllocView a, int32_t* bt, i
 constexpr size_t kSelectSmemBytes = sizeof(SelectSmem);
 
 int configure(const void* fn) {
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSelectSmemBytes) != cudaSuccess)
-    return SCKV_ERR_CUDA;
+  SCKV_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSelectSmemBytes));
   return SCKV_OK;
 }
 

@@ -79,6 +79,21 @@ struct KV<SCKV_DTYPE_FP8_E4M3> {
   }
 };
 
+// int8 codes of the arena's quant mode; the per-token fp16 scales are applied
+// to the score (K) and the probability (V), not to each element.
+template <>
+struct KV<SCKV_DTYPE_INT8> {
+  static constexpr int kBytes = 1;
+  __device__ static __forceinline__ void load8(const uint8_t* p, float f[8]) {
+    uint2 r = *reinterpret_cast<const uint2*>(p);
+    const uint32_t w[2] = {r.x, r.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) f[4 * i + b] = (float)(int8_t)((w[i] >> (8 * b)) & 0xffu);
+  }
+};
+
 // Reduce-scatter 8 partial sums over the 16 lanes of a half-warp: afterwards
 // lane c holds the full sum of element c >> 1.
 __device__ __forceinline__ float reduce_scatter8(const float v[8], int c) {
@@ -107,8 +122,14 @@ __device__ __forceinline__ float reduce_scatter8(const float v[8], int c) {
 
 template <int G, int KVDT, int S>
 struct Smem {
+  // page i -> warp i % kConsumerWarps and ring slot i % S: S a multiple of the
+  // warp count keeps every use of a slot with one warp (see the phase-parity
+  // wait in the consumer loop)
+  static_assert(S % kConsumerWarps == 0, "ring depth must be a multiple of the consumer warps");
   static constexpr int kPH = SCKV_PAGE_TOKENS * kHD * KV<KVDT>::kBytes;  // bytes of one page-head
-  static constexpr int kStageBytes = 2 * kPH;
+  // int8 stages also carry the page-head's 16 K and 16 V token scales (fp16)
+  static constexpr int kTokScaleBytes = (KVDT == SCKV_DTYPE_INT8) ? SCKV_PAGE_TOKENS * 2 : 0;
+  static constexpr int kStageBytes = 2 * kPH + 2 * kTokScaleBytes;
   static constexpr int kRingBytes = S * kStageBytes;
   static constexpr int kRedFloats = kConsumerWarps * G * (kHD + 2);
   static constexpr int kBytes = kRingBytes + 2 * S * 8 + kRedFloats * 4 + 16;
@@ -175,9 +196,17 @@ __global__ void __launch_bounds__(kThreads, (G <= 2 ? 3 : (G == 4 ? 2 : 1)))
         }
         const uint8_t* src = p.pool + (layer_base + page) * slab_bytes + (int64_t)h * SM::kPH;
         uint8_t* dst = ring + st * SM::kStageBytes;
-        mbar_arrive_expect_tx(&full[st], 2 * SM::kPH);
+        mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
         bulk_g2s(dst, src, SM::kPH, &full[st]);
         bulk_g2s(dst + SM::kPH, src + (int64_t)p.hkv * SM::kPH, SM::kPH, &full[st]);
+        if (KVDT == SCKV_DTYPE_INT8) {
+          // scales [layer][page][K|V][head][16 tokens] fp16: 32 bytes per page-head
+          const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(p.fp8_scales) +
+                                ((layer_base + page) * 2 * p.hkv + h) * SM::kTokScaleBytes;
+          bulk_g2s(dst + 2 * SM::kPH, ssrc, SM::kTokScaleBytes, &full[st]);
+          bulk_g2s(dst + 2 * SM::kPH + SM::kTokScaleBytes, ssrc + (int64_t)p.hkv * SM::kTokScaleBytes,
+                   SM::kTokScaleBytes, &full[st]);
+        }
         ++gcount;
       }
     }
@@ -242,6 +271,12 @@ __global__ void __launch_bounds__(kThreads, (G <= 2 ? 3 : (G == 4 ? 2 : 1)))
         const uint8_t* sK = ring + st * SM::kStageBytes;
         const uint8_t* sV = sK + SM::kPH;
         const int nv = min(SCKV_PAGE_TOKENS, ctx - (j0 + i) * SCKV_PAGE_TOKENS);
+        if (KVDT == SCKV_DTYPE_INT8) {
+          // this lane's score and probability belong to token tok_mine
+          const __half* ts = reinterpret_cast<const __half*>(sK + 2 * SM::kPH);
+          kscale = __half2float(ts[tok_mine]);
+          vscale = __half2float(ts[SCKV_PAGE_TOKENS + tok_mine]);
+        }
 
         float part[G][8];
 #pragma unroll
@@ -420,12 +455,11 @@ int launch_decode(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t s
   static bool configured[64] = {};
   const int dev = pool->device;
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes) != cudaSuccess)
-      return SCKV_ERR_CUDA;
+    SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes));
     configured[dev] = true;
   }
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, SM::kBytes) != cudaSuccess) return SCKV_ERR_CUDA;
+  SCKV_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, SM::kBytes));
   if (occ < 1) occ = 1;
   const int n_items = prm.n_seqs * prm.hkv * prm.max_splits;
   int grid = pool->num_sms * occ;
@@ -540,6 +574,7 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
     case SCKV_DTYPE_F16: return dispatch_g<SCKV_DTYPE_F16, 8>(pool, G, prm, s);
     case SCKV_DTYPE_BF16: return dispatch_g<SCKV_DTYPE_BF16, 8>(pool, G, prm, s);
     case SCKV_DTYPE_FP8_E4M3: return dispatch_g<SCKV_DTYPE_FP8_E4M3, 16>(pool, G, prm, s);
+    case SCKV_DTYPE_INT8: return dispatch_g<SCKV_DTYPE_INT8, 16>(pool, G, prm, s);
     default: return SCKV_ERR_UNSUPPORTED;
   }
 }

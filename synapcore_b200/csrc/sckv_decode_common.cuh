@@ -11,7 +11,7 @@ constexpr int kHD = 128;  // head_dim handled by this kernel
 
 struct DecodeParams {
   const uint8_t* pool;
-  const float* fp8_scales;
+  const float* fp8_scales;  // the pool's scale region: FP8 float per page-head, or int8 fp16 per token
   const void* q;
   void* out;
   float* part_acc;  // [n_seqs][Hq][max_splits][HD]

@@ -57,6 +57,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr bool kFP8 = (KVDT == SCKV_DTYPE_FP8_E4M3);
   constexpr int kG = SM::kG;
   constexpr int kWPH = kConsumerWarps / HG;  // consumer warps per head
+  // Pages go to the kWPH warps of a head in turn (page i -> warp i % kWPH) and
+  // page i lands in ring slot i % S. With S a multiple of kWPH every use of a
+  // slot belongs to the same warps, so a warp waiting for a slot has consumed
+  // the slot's previous use and the phase-parity wait cannot be satisfied by
+  // an older phase of the same parity.
+  static_assert(S % kWPH == 0, "ring depth must be a multiple of the warps per head");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // swizzled TMA destinations need 1024-byte alignment
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -474,13 +480,11 @@ int launch_mma(const sckv_pool* pool, const DecodeParams& prm, cudaStream_t stre
   const int rc = ensure_tmap(pool, HG, mp->tmap_kv, &mp->tmap_ready);
   if (rc != SCKV_OK) return rc;
   if (!configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes) != cudaSuccess)
-      return SCKV_ERR_CUDA;
+    SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes));
     configured[dev] = true;
   }
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, SM::kBytes) != cudaSuccess)
-    return SCKV_ERR_CUDA;
+  SCKV_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, SM::kBytes));
   if (occ < 1) occ = 1;
   const int n_items = prm.n_seqs * (prm.hkv / HG) * prm.max_splits;
   int grid = pool->num_sms * occ;
@@ -505,14 +509,15 @@ int launch_decode_mma(const sckv_pool* pool, int G, const DecodeParams& prm, cud
   if (pool->head_dim != kHD || G < 1 || G > 16) return SCKV_ERR_UNSUPPORTED;
   if ((int64_t)pool->num_layers * pool->max_pages > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
   const int H = pool->num_kv_heads;
-  // Stages hold one page of HG kv heads (16 KiB for HG=4 FP8 / HG=2 16-bit).
+  // Stages hold one page of HG kv heads (16 KiB for HG=4 FP8 / HG=2 16-bit);
+  // ring depths are multiples of the warps per head (4 / HG).
   switch (pool->kv_dtype) {
     case SCKV_DTYPE_F16:
-      return (H % 2 == 0) ? launch_mma_nq<SCKV_DTYPE_F16, 2, 5>(pool, G, prm, stream)
-                          : launch_mma_nq<SCKV_DTYPE_F16, 1, 10>(pool, G, prm, stream);
+      return (H % 2 == 0) ? launch_mma_nq<SCKV_DTYPE_F16, 2, 4>(pool, G, prm, stream)
+                          : launch_mma_nq<SCKV_DTYPE_F16, 1, 8>(pool, G, prm, stream);
     case SCKV_DTYPE_BF16:
-      return (H % 2 == 0) ? launch_mma_nq<SCKV_DTYPE_BF16, 2, 5>(pool, G, prm, stream)
-                          : launch_mma_nq<SCKV_DTYPE_BF16, 1, 10>(pool, G, prm, stream);
+      return (H % 2 == 0) ? launch_mma_nq<SCKV_DTYPE_BF16, 2, 4>(pool, G, prm, stream)
+                          : launch_mma_nq<SCKV_DTYPE_BF16, 1, 8>(pool, G, prm, stream);
     case SCKV_DTYPE_FP8_E4M3:
       // the page's 2*H scales travel as one bulk copy: needs H even (and <= 32)
       if (H > 32 || H % 2 != 0) return SCKV_ERR_UNSUPPORTED;

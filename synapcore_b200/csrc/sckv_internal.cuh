@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <stdio.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -206,17 +207,32 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Error helper for host code.
-#define SCKV_CUDA_CHECK(expr)                      \
-  do {                                             \
-    cudaError_t _e = (expr);                       \
-    if (_e != cudaSuccess) return SCKV_ERR_CUDA;   \
+// Error helpers for host code. A failing CUDA call leaves a description
+// ("file:line what: error name") in a per-thread buffer that
+// sckv_last_error() returns, so SCKV_ERR_CUDA can be traced to its call.
+inline char* sckv_error_buffer() {
+  static thread_local char buf[256] = {0};
+  return buf;
+}
+
+inline int sckv_record_error(const char* file, int line, const char* what, const char* err) {
+  const char* base = file;
+  for (const char* c = file; *c; ++c)
+    if (*c == '/') base = c + 1;
+  snprintf(sckv_error_buffer(), 256, "%s:%d %s: %s", base, line, what, err);
+  return SCKV_ERR_CUDA;
+}
+
+#define SCKV_CUDA_CHECK(expr)                                                            \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    if (_e != cudaSuccess) return sckv_record_error(__FILE__, __LINE__, #expr, cudaGetErrorName(_e)); \
   } while (0)
 
-#define SCKV_LAUNCH_CHECK()                        \
-  do {                                             \
-    cudaError_t _e = cudaGetLastError();           \
-    if (_e != cudaSuccess) return SCKV_ERR_CUDA;   \
+#define SCKV_LAUNCH_CHECK()                                                              \
+  do {                                                                                   \
+    cudaError_t _e = cudaGetLastError();                                                 \
+    if (_e != cudaSuccess) return sckv_record_error(__FILE__, __LINE__, "kernel launch", cudaGetErrorName(_e)); \
   } while (0)
 
 static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

@@ -126,7 +126,7 @@ inline int ensure_tmap(const sckv_pool* pool, int HG, unsigned char* slot, int* 
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess || fn == nullptr)
-      return SCKV_ERR_CUDA;
+      return sckv_record_error(__FILE__, __LINE__, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled not found");
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
   const cuuint64_t eb = (cuuint64_t)sckv_elem_bytes(pool->kv_dtype);
@@ -141,7 +141,11 @@ inline int ensure_tmap(const sckv_pool* pool, int HG, unsigned char* slot, int* 
   CUresult r = encode(reinterpret_cast<CUtensorMap*>(slot), dt, 5, pool->data, dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return SCKV_ERR_CUDA;
+  if (r != CUDA_SUCCESS) {
+    char what[64];
+    snprintf(what, sizeof what, "CUresult %d", (int)r);
+    return sckv_record_error(__FILE__, __LINE__, "cuTensorMapEncodeTiled", what);
+  }
   *ready = HG;
   return SCKV_OK;
 }

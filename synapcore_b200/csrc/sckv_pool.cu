@@ -170,6 +170,8 @@ extern "C" int sckv_clear_status(sckv_pool* p, void* stream) {
 
 extern "C" const char* sckv_version(void) { return "sckv 0.1.0 sm_100a"; }
 
+extern "C" const char* sckv_last_error(void) { return sckv_error_buffer(); }
+
 extern "C" const char* sckv_status_string(int code) {
   switch (code) {
     case SCKV_OK: return "ok";

@@ -441,10 +441,9 @@ int launch_prefill(const sckv_pool* pool, const PrefillParams& prm, int max_tile
   if (rc != SCKV_OK) return rc;
   const int smem = SM::kFixedBytes + 4 * (prm.n_seqs + 2);
   if (smem > 227 * 1024) return SCKV_ERR_INVALID_ARG;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return SCKV_ERR_CUDA;
+  SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess) return SCKV_ERR_CUDA;
+  SCKV_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem));
   if (occ < 1) occ = 1;
   const int64_t items = (int64_t)max_tiles * prm.hkv;
   int64_t grid = (int64_t)pool->num_sms * occ;

@@ -61,6 +61,10 @@ def _make_case(cuda_device, kv_dtype, hq, hkv, ctx_lens, pool_pages, seed, layer
     ("bf16", 16, 8, torch.bfloat16),
     ("fp8_e4m3", 32, 2, torch.bfloat16),
     ("fp8_e4m3", 8, 4, torch.float32),
+    ("int8", 16, 16, torch.float16),
+    ("int8", 8, 2, torch.float16),
+    ("int8", 32, 4, torch.bfloat16),
+    ("int8", 64, 8, torch.float32),
 ])
 @pytest.mark.parametrize("chunk_pages", [0, 3])
 def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages):
@@ -80,6 +84,38 @@ def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages)
         for b in range(len(ctx)):
             assert _rel_err(got[b], ref[b]) <= TOL, (layer, b, _rel_err(got[b], ref[b]))
     assert pool.status()[0] == 0
+    pool.close()
+
+
+@pytest.mark.parametrize("kv_dtype,hq,hkv,qdt", [
+    ("fp16", 8, 2, torch.float16),        # tensor cores, 2 kv heads per stage
+    ("bf16", 32, 8, torch.bfloat16),      # tensor cores, 2 kv heads per stage
+    ("fp16", 12, 3, torch.float16),       # tensor cores, 1 kv head per stage
+    ("bf16", 6, 3, torch.bfloat16),       # tensor cores, 1 kv head per stage
+    ("fp8_e4m3", 32, 8, torch.bfloat16),  # tensor cores, 4 kv heads per stage
+    ("fp8_e4m3", 12, 6, torch.bfloat16),  # tensor cores, 2 kv heads per stage
+    ("fp16", 8, 8, torch.float16),        # CUDA cores
+    ("int8", 16, 4, torch.float16),       # CUDA cores
+])
+def test_decode_long_items_reuse_every_ring_slot_many_times(cuda_device, kv_dtype, hq, hkv, qdt):
+    """One split per sequence and a few work items, so every CTA streams
+    hundreds of pages through its ring and each slot is reused many times by
+    the warps that share a kv head (the case the phase-parity waits must get
+    right); ragged lengths end on partial pages."""
+    ctx = [2000, 1713, 2047, 1]
+    pool, ora, bt, q = _make_case(cuda_device, kv_dtype, hq, hkv, ctx, pool_pages=520, seed=31, layers=1,
+                                  kv_scale=(0.5, 4.0) if kv_dtype == "fp8_e4m3" else None)
+    q_t = torch.from_numpy(q).to(qdt)
+    bt_d = torch.from_numpy(bt).to(cuda_device)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+    for chunk in (bt.shape[1], 37):
+        out = pool.decode_attn(0, q_t.to(cuda_device), bt_d, ctx_d, out_dtype=torch.float32, chunk_pages=chunk)
+        torch.cuda.synchronize()
+        pool.raise_on_status()
+        ref = ora.decode(0, q_t.float().numpy(), bt, np.array(ctx))
+        got = out.cpu().numpy()
+        for b in range(len(ctx)):
+            assert _rel_err(got[b], ref[b]) <= TOL, (chunk, b, _rel_err(got[b], ref[b]))
     pool.close()
 
 

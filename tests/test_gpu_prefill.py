@@ -155,3 +155,39 @@ def test_paged_cache_prefill_uses_tensor_core_kernel_and_matches_decode_path(cud
             torch.cuda.synchronize()
             assert _rel_err(got.cpu().numpy(), ref.cpu().numpy()) <= TOL
     cache.check()
+
+
+def test_paged_cache_int8_prefill_and_decode_match_oracle(cuda_device):
+    """int8 pools (the arena's quant mode, per-token fp16 scales) attend
+    through the SIMT decode kernel; the reference attends over the fp16
+    dequantisation fp16(code * scale) of the same pages."""
+    from oracle.kv_oracle import sdpa_decode, sdpa_prefill
+    from synapcore_b200.paged_cache import PagedKVCache
+
+    rng = np.random.default_rng(9)
+    L, hkv, hq, D, T = 2, 4, 16, 128, 45
+    cache = PagedKVCache(L, hkv, D, max_pages=32, max_seqs=2, max_blocks_per_seq=8, kv_dtype="int8",
+                         device=cuda_device)
+    cache.add_sequence(7)
+    k = torch.from_numpy(rng.standard_normal((L, T, hkv, D)).astype(np.float16)).to(cuda_device)
+    v = torch.from_numpy(rng.standard_normal((L, T, hkv, D)).astype(np.float16)).to(cuda_device)
+    cache.append_prefill(7, k, v)
+    kd, vd = cache.gather(7)  # [L, Hkv, T, D] fp16 dequantised on the device
+    kd, vd = kd.cpu().numpy(), vd.cpu().numpy()
+    q = rng.standard_normal((T, hq, D)).astype(np.float32)
+    for layer in range(L):
+        got = cache.prefill_attention(layer, 7, torch.from_numpy(q).to(cuda_device), 0, out_dtype=torch.float32)
+        ref = sdpa_prefill(q, kd[layer], vd[layer], 0)
+        assert _rel_err(got.cpu().numpy(), ref) <= TOL
+    cache.decode_reserve(1)
+    kn = torch.from_numpy(rng.standard_normal((1, hkv, D)).astype(np.float16)).to(cuda_device)
+    for layer in range(L):
+        cache.decode_append(layer, kn, kn, 1)
+    kd, vd = cache.gather(7)
+    kd, vd = kd.cpu().numpy(), vd.cpu().numpy()
+    qd = rng.standard_normal((1, hq, D)).astype(np.float32)
+    for layer in range(L):
+        got = cache.decode_attention(layer, torch.from_numpy(qd).to(cuda_device), 1, out_dtype=torch.float32)
+        ref = sdpa_decode(qd[0], kd[layer], vd[layer])
+        assert _rel_err(got.cpu().numpy()[0], ref) <= TOL
+    cache.check()
