@@ -73,6 +73,18 @@ WORKLOADS = {
                        batch=64, ctx=(8192, 32768), grow=True, pool_gb=100.0),
     "qwen3-long-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="bf16",
                              qdt=torch.bfloat16, batch=8, ctx=(8192, 32768), grow=True, pool_gb=4.0),
+    # continuous-batching mix: 256 live sequences (~U[16, 8192] tokens, a
+    # quarter of them forked from one shared 1024-token prefix); every step
+    # retires 8 sequences (pages kept cached), admits 8 prompts ~U[64, 2048]
+    # (a quarter forked from the prefix) with causal prefill attention, and
+    # decodes one token for every live sequence; LRU eviction keeps pool
+    # occupancy at or below 90 %.
+    "olmoe-mix": dict(kind="mix", model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="fp16",
+                      qdt=torch.float16, batch=256, ctx=(16, 8192), new_per_step=8, prompt=(64, 2048),
+                      fork_frac=0.25, prefix=1024, pool_pages=72000, evict_at=0.9),
+    "olmoe-mix-small": dict(kind="mix", model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128,
+                            kv="fp16", qdt=torch.float16, batch=32, ctx=(16, 8192), new_per_step=8,
+                            prompt=(64, 2048), fork_frac=0.25, prefix=1024, pool_pages=9000, evict_at=0.9),
 }
 
 
@@ -477,6 +489,322 @@ def bench_ours(args, w_full, world, rank, local):
     return res
 
 
+# ----------------------------------------------------------------------------- continuous-batching mix
+class MixState:
+    """A PagedKVCache driven like a serving loop, with exact host-side
+    accounting of the pool (ring / cached / pinned pages) so the 90 % eviction
+    policy needs no device read on the step path."""
+
+    def __init__(self, w, rank: int, max_steps: int):
+        from synapcore_b200.paged_cache import PagedKVCache
+
+        self.w = w
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        self.rng = np.random.default_rng(300 + rank)
+        L, hq, hkv, d = w["layers"], w["hq"], w["hkv"], w["d"]
+        self.L = L
+        lo, hi = w["ctx"]
+        self.max_new = w["new_per_step"] * w["prompt"][1]
+        max_blocks = (hi + w["prompt"][1] + max_steps + 2 * PAGE) // PAGE + 1
+        self.max_rows = w["batch"] + w["new_per_step"] + 1
+        self.P = int(w["pool_pages"])
+        self.cache = PagedKVCache(L, hkv, d, self.P, self.max_rows, max_blocks, w["kv"], device=dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(4321 + rank)
+        self.src_k = torch.randn((L, hi, hkv, d), generator=g, device=dev).to(w["qdt"])
+        self.src_v = torch.randn((L, hi, hkv, d), generator=g, device=dev).to(w["qdt"])
+        # a step's prompt inputs, flat so that [L, tot, ...] views are contiguous
+        self.pre_k = torch.randn(L * self.max_new * hkv * d, generator=g, device=dev).to(w["qdt"])
+        self.pre_v = torch.randn(L * self.max_new * hkv * d, generator=g, device=dev).to(w["qdt"])
+        self.pre_q = torch.randn(L * self.max_new * hq * d, generator=g, device=dev).to(w["qdt"])
+        self.out_pre = torch.empty((self.max_new, hq, d), dtype=w["qdt"], device=dev)
+        self.q_dec = torch.randn((L, self.max_rows, hq, d), generator=g, device=dev).to(w["qdt"])
+        self.k_dec = torch.randn((L, self.max_rows, hkv, d), generator=g, device=dev).to(w["qdt"])
+        self.v_dec = torch.randn((L, self.max_rows, hkv, d), generator=g, device=dev).to(w["qdt"])
+        self.out_dec = torch.empty((self.max_rows, hq, d), dtype=w["qdt"], device=dev)
+        # pool accounting: ring (free), cached (unpinned, evictable), pinned
+        self.free, self.cached = self.P, 0
+        self.forked = set()
+        self.next_id = 0
+        c = self.cache
+        # the shared prefix: written once, held by one extra pin
+        npre = w["prefix"]
+        c.add_sequence("prefix")
+        self._alloc(-(-npre // PAGE))
+        c.append_prefill("prefix", self.src_k[:, :npre], self.src_v[:, :npre])
+        self.prefix_pages = c.page_ids("prefix")
+        c.pool.pin_pages(torch.tensor(self.prefix_pages, dtype=torch.int32, device=dev), +1)
+        c.remove_sequence("prefix")
+        n_fork = int(round(w["batch"] * w["fork_frac"]))
+        forks = set(self.rng.choice(w["batch"], size=n_fork, replace=False).tolist())
+        for i in range(w["batch"]):
+            sid = self._new_id()
+            c.add_sequence(sid)
+            if i in forks:
+                c.share_prefix(sid, self.prefix_pages)
+                self.forked.add(sid)
+                own = int(self.rng.integers(lo, hi - npre + 1))
+            else:
+                own = int(self.rng.integers(lo, hi + 1))
+            self._alloc(self._pages_needed(c.length(sid), own))
+            c.append_prefill(sid, self.src_k[:, :own], self.src_v[:, :own])
+        torch.cuda.synchronize()
+        self.check_accounting()
+        self.events = []
+
+    def _new_id(self):
+        self.next_id += 1
+        return self.next_id
+
+    @staticmethod
+    def _pages_needed(length: int, add: int) -> int:
+        return -(-(length + add) // PAGE) - (-(-length // PAGE))
+
+    def _alloc(self, n: int):
+        take = min(n, self.free)
+        self.free -= take
+        self.cached -= n - take
+        if self.cached < 0:
+            raise RuntimeError("pool exhausted")
+
+    def occupancy(self) -> int:
+        return self.P - self.free
+
+    def check_accounting(self):
+        st = self.cache.pool.alloc_state()
+        if st["free"] != self.free:
+            raise RuntimeError(f"pool accounting drifted: device ring has {st['free']}, host expects {self.free}")
+
+    def step(self, timing=None, io=None):
+        """One serving step; returns (algorithmic bytes, decode tokens, prefill tokens, launch bytes)."""
+        w, c, L = self.w, self.cache, self.L
+        hkv, hq, d = w["hkv"], w["hq"], w["d"]
+        eb = kv_bytes_per_elem(w["kv"])
+        # 1. retire sequences (their pages stay cached for prefix reuse)
+        live = list(c.seq_at)
+        gone = [live[i] for i in self.rng.choice(len(live), size=w["new_per_step"], replace=False)]
+        for sid in gone:
+            own = -(-c.length(sid) // PAGE) - (len(self.prefix_pages) if sid in self.forked else 0)
+            self.cached += own
+            self.forked.discard(sid)
+        c.remove_sequences(gone, keep_cached=True)
+        # 2. eviction policy: occupancy at most evict_at of the pool
+        limit = int(w["evict_at"] * self.P)
+        if self.occupancy() > limit:
+            k = min(self.occupancy() - limit, self.cached)
+            if k > 0:
+                c.pool.evict_lru(k)
+                self.cached -= k
+                self.free += k
+        # 3. admit new prompts: forks share the prefix pages, all prefill causally
+        plo, phi = w["prompt"]
+        new_ids, T, starts = [], [], []
+        for _ in range(w["new_per_step"]):
+            sid = self._new_id()
+            c.add_sequence(sid)
+            if self.rng.random() < w["fork_frac"]:
+                c.share_prefix(sid, self.prefix_pages)
+                self.forked.add(sid)
+            t = int(self.rng.integers(plo, phi + 1))
+            self._alloc(self._pages_needed(c.length(sid), t))
+            new_ids.append(sid)
+            T.append(t)
+            starts.append(c.length(sid))
+        cu = np.concatenate([[0], np.cumsum(T)]).astype(np.int64)
+        tot = int(cu[-1])
+        if io is not None:
+            io["pre_in"](tot)
+        pk = self.pre_k[:L * tot * hkv * d].view(L, tot, hkv, d)
+        pv = self.pre_v[:L * tot * hkv * d].view(L, tot, hkv, d)
+        pq = self.pre_q[:L * tot * hq * d].view(L, tot, hq, d)
+        c.append_prefill_batch(new_ids, pk, pv, cu.tolist())
+        meta = torch.tensor(np.concatenate([cu, starts]).astype(np.int32)).to(self.dev, non_blocking=True)
+        cu_d, st_d = meta[:len(T) + 1], meta[len(T) + 1:]
+        for l in range(L):
+            if timing is not None:
+                timing["pre"].append(torch.cuda.Event(enable_timing=True))
+                timing["pre"][-1].record()
+            c.prefill_attention_batch(l, new_ids, pq[l], cu_d, st_d, out=self.out_pre[:tot])
+            if timing is not None:
+                timing["pre"].append(torch.cuda.Event(enable_timing=True))
+                timing["pre"][-1].record()
+        # 4. decode one token for every live sequence
+        n = c.n_live
+        self._alloc(sum(1 for r in range(n) if c.lengths[r] % PAGE == 0))
+        if io is not None:
+            io["dec_in"](n)
+        c.decode_reserve(n)
+        for l in range(L):
+            c.decode_append(l, self.k_dec[l, :n], self.v_dec[l, :n], n)
+            if timing is not None:
+                timing["dec"].append(torch.cuda.Event(enable_timing=True))
+                timing["dec"][-1].record()
+            c.decode_attention(l, self.q_dec[l, :n], n, out=self.out_dec[:n])
+            if timing is not None:
+                timing["dec"].append(torch.cuda.Event(enable_timing=True))
+                timing["dec"][-1].record()
+        if io is not None:
+            io["out"](n, tot)
+        # algorithmic bytes
+        ctx = np.asarray(c.lengths[:n], np.int64)
+        dec = int(ctx.sum()) * hkv * d * 2 * eb + int(((ctx + PAGE - 1) // PAGE).sum()) * 4 + n * hq * d * 2 * 2
+        app_tok = hkv * d * 2 * (2 + eb)          # read the new K/V row, write it into its page
+        pre_ctx = np.asarray(starts, np.int64) + np.asarray(T, np.int64)
+        pre = int(pre_ctx.sum()) * hkv * d * 2 * eb + tot * hq * d * 2 * 2
+        total = L * (dec + pre + (n + tot) * app_tok)
+        pre_flops = L * 4 * hq * d * int(sum(t * s + t * (t + 1) // 2 for t, s in zip(T, starts)))
+        return total, n, tot, dec, pre, pre_flops
+
+
+def bench_mix(args, w, world, rank, local):
+    from synapcore_b200 import _native as N
+
+    total_steps = args.warmup + 2 * args.steps + max(1, args.warmup)
+    st = MixState(w, rank, total_steps)
+    for _ in range(args.warmup):
+        st.step()
+    torch.cuda.synchronize()
+    st.cache.check()
+    st.check_accounting()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    timing = {"pre": [], "dec": []}
+    barrier(world)
+    torch.cuda.synchronize()
+    l0 = N.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tot_bytes = dec_tok = pre_tok = 0
+    dec_bytes, pre_bytes, pre_flops = [], [], []
+    e0.record()
+    for _ in range(args.steps):
+        b, n, t, db, pb, pf = st.step(timing)
+        tot_bytes += b
+        dec_tok += n
+        pre_tok += t
+        dec_bytes.append(db)
+        pre_bytes.append(pb)
+        pre_flops.append(pf)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = N.launch_count() - l0
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    dec_ms = [timing["dec"][i].elapsed_time(timing["dec"][i + 1]) for i in range(0, len(timing["dec"]), 2)]
+    pre_ms = [timing["pre"][i].elapsed_time(timing["pre"][i + 1]) for i in range(0, len(timing["pre"]), 2)]
+    st.cache.check()
+    st.check_accounting()
+
+    # ---- e2e: the step's new K/V and queries copied from pinned host memory,
+    # the last layer's outputs read back
+    L, hq, hkv, d = w["layers"], w["hq"], w["hkv"], w["d"]
+    h_pre = [(x.cpu().pin_memory(), x, per) for x, per in ((st.pre_k, hkv * d), (st.pre_v, hkv * d),
+                                                          (st.pre_q, hq * d))]
+    h_dec = [(x.cpu().pin_memory(), x) for x in (st.q_dec, st.k_dec, st.v_dec)]
+    h_out_dec = torch.empty_like(st.out_dec, device="cpu").pin_memory()
+    h_out_pre = torch.empty_like(st.out_pre, device="cpu").pin_memory()
+    moved = {"h2d": 0, "d2h": 0}
+
+    def pre_in(tot):
+        for h, dd, per in h_pre:
+            m = L * tot * per
+            dd[:m].copy_(h[:m], non_blocking=True)
+            moved["h2d"] += m * h.element_size()
+
+    def dec_in(n):
+        for h, dd in h_dec:
+            for l in range(L):
+                dd[l, :n].copy_(h[l, :n], non_blocking=True)
+            moved["h2d"] += L * h[0, :n].numel() * h.element_size()
+
+    def out(n, tot):
+        h_out_dec[:n].copy_(st.out_dec[:n], non_blocking=True)
+        h_out_pre[:tot].copy_(st.out_pre[:tot], non_blocking=True)
+        moved["d2h"] += (n + tot) * hq * d * h_out_dec.element_size()
+
+    io = {"pre_in": pre_in, "dec_in": dec_in, "out": out}
+    for _ in range(max(1, args.warmup)):
+        st.step(io=io)
+    torch.cuda.synchronize()
+    moved = {"h2d": 0, "d2h": 0}
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_bytes = 0
+    f0.record()
+    for _ in range(args.steps):
+        e2e_bytes += st.step(io=io)[0]
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    st.cache.check()
+    st.check_accounting()
+
+    peak, peak_kind = measured_peak_gbs()
+    ms_step = ms_total / args.steps
+    value = world * tot_bytes / (ms_total * 1e-3) / 1e9
+    dec_avg_ms = max_over_ranks(float(np.mean(dec_ms)), world)
+    pre_avg_ms = max_over_ranks(float(np.mean(pre_ms)), world)
+    dec_launch_bytes = float(np.mean(dec_bytes))
+    achieved = dec_launch_bytes / (dec_avg_ms * 1e-3) / 1e9
+    tflops = float(np.mean(pre_flops)) / L / (pre_avg_ms * 1e-3) / 1e12
+    peaks = {}
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    res = {
+        "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w["kv"],
+        "data": "synthetic (seeded N(0,1) K/V/Q, random prompt lengths, retirements and forks)",
+        "tok_per_s": round(world * dec_tok / (ms_total * 1e-3), 1),
+        "prefill_tok_per_s": round(world * pre_tok / (ms_total * 1e-3), 1),
+        "pct_hbm_peak": round(100.0 * value / world / peak, 2),
+        "config": {
+            "workload": f"{args.workload}: continuous batching, {w['model']} shape {w['layers']}L x "
+                        f"{w['hq']}q/{w['hkv']}kv heads x d{w['d']}, {w['kv']} KV, page 16; {w['batch']} live "
+                        f"sequences/GPU ~U{list(w['ctx'])}, {int(w['fork_frac'] * 100)}% forked from a shared "
+                        f"{w['prefix']}-token prefix; per step retire {w['new_per_step']}, admit "
+                        f"{w['new_per_step']} prompts ~U{list(w['prompt'])} (causal prefill), decode all; "
+                        f"LRU eviction above {int(w['evict_at'] * 100)}% of a {w['pool_pages']}-page pool",
+            "global_batch": world * w["batch"],
+            "seq_len": ctx_desc(w),
+            "parallelism": f"sequence-sharded x{world} (independent pools)",
+            "l2": "inputs larger than L2 (KV per decode launch >> 126 MB)",
+        },
+        "e2e": {"value": round(world * e2e_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(moved["h2d"] / args.steps),
+                "d2h_bytes_per_step": int(moved["d2h"] / args.steps)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
+                     "peak_kind": peak_kind, "kernel": "decode_kernel (+combine) per layer launch",
+                     "bytes_per_launch": int(dec_launch_bytes), "avg_launch_ms": round(dec_avg_ms, 4)},
+        "prefill_roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                             "frac": round(tflops / tc_peak, 4), "kernel": "prefill_kernel per layer launch",
+                             "flops_per_launch": int(np.mean(pre_flops) / L), "avg_launch_ms": round(pre_avg_ms, 4)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+    st.cache.pool.close()
+    return res
+
+
 # ----------------------------------------------------------------------------- CPU (reference) arm
 def cpu_sample(w, n_seqs: int, ctx: int, seed: int = 0):
     """A bounded slice of the workload on the host: one layer x n_seqs."""
@@ -572,6 +900,8 @@ def main():
     try:
         if args.impl == "reference":
             res = bench_reference(args, w, world, rank)
+        elif w.get("kind") == "mix":
+            res = bench_mix(args, w, world, rank, local)
         else:
             res = bench_ours(args, w, world, rank, local)
         if rank == 0 and res is not None:

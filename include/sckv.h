@@ -325,6 +325,9 @@ SCKV_API const char* sckv_version(void);
  * ("file:line call: CUDA error name"); "" if none. No reference counterpart
  * (the reference's native calls report only status codes). */
 SCKV_API const char* sckv_last_error(void);
+/* Kernels this library has launched in this process, all devices (for
+ * launch accounting around a timed region). No reference counterpart. */
+SCKV_API unsigned long long sckv_launch_count(void);
 SCKV_API const char* sckv_status_string(int code);
 
 #ifdef __cplusplus

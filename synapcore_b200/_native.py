@@ -94,6 +94,7 @@ _SIGNATURES = [
     ("sckv_kv_insert", c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_double, c_void_p, POINTER(c_uint64)]),
     ("sckv_version", ctypes.c_char_p, []),
     ("sckv_last_error", ctypes.c_char_p, []),
+    ("sckv_launch_count", ctypes.c_ulonglong, []),
     ("sckv_status_string", ctypes.c_char_p, [c_int]),
 ]
 
@@ -123,6 +124,11 @@ def load(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
 
 def lib() -> ctypes.CDLL:
     return load()
+
+
+def launch_count() -> int:
+    """Kernels libsckv has launched in this process so far."""
+    return int(lib().sckv_launch_count())
 
 
 def status_string(code: int) -> str:

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -229,8 +230,16 @@ inline int sckv_record_error(const char* file, int line, const char* what, const
     if (_e != cudaSuccess) return sckv_record_error(__FILE__, __LINE__, #expr, cudaGetErrorName(_e)); \
   } while (0)
 
+// Kernels launched by this library in this process (every launch site is
+// followed by exactly one SCKV_LAUNCH_CHECK, which counts it).
+inline std::atomic<unsigned long long>& sckv_launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
 #define SCKV_LAUNCH_CHECK()                                                              \
   do {                                                                                   \
+    sckv_launch_counter().fetch_add(1, std::memory_order_relaxed);                       \
     cudaError_t _e = cudaGetLastError();                                                 \
     if (_e != cudaSuccess) return sckv_record_error(__FILE__, __LINE__, "kernel launch", cudaGetErrorName(_e)); \
   } while (0)

@@ -172,6 +172,10 @@ extern "C" const char* sckv_version(void) { return "sckv 0.1.0 sm_100a"; }
 
 extern "C" const char* sckv_last_error(void) { return sckv_error_buffer(); }
 
+extern "C" unsigned long long sckv_launch_count(void) {
+  return sckv_launch_counter().load(std::memory_order_relaxed);
+}
+
 extern "C" const char* sckv_status_string(int code) {
   switch (code) {
     case SCKV_OK: return "ok";

@@ -91,6 +91,27 @@ class PagedKVCache:
         self.block_table[last].fill_(-1)
         self.ctx_lens[last] = 0
 
+    def remove_sequences(self, seq_ids: Sequence[Hashable], keep_cached: bool = False) -> None:
+        """remove_sequence for several sequences with one release launch (the
+        pins of all their pages are dropped together, in the order given)."""
+        seq_ids = list(seq_ids)
+        if not seq_ids:
+            return
+        if len(set(seq_ids)) != len(seq_ids):
+            raise ValueError("duplicate sequence ids")
+        parts = []
+        for sid in seq_ids:
+            r = self.row_of[sid]
+            n = self._pages_of(r)
+            if n:
+                parts.append(self.block_table[r, :n])
+        if parts:
+            self.pool.release_pages(torch.cat(parts), keep_cached=keep_cached)
+        for sid in seq_ids:
+            r = self.row_of[sid]
+            self.lengths[r] = 0  # pages already released
+            self.remove_sequence(sid)
+
     def move_to_row(self, seq_id: Hashable, row: int) -> None:
         """Swap two live rows (used to keep decode-phase sequences first)."""
         r = self.row_of[seq_id]
@@ -136,6 +157,84 @@ class PagedKVCache:
         if layer0 + nl == self.num_layers:
             self.lengths[r] += T
             self.ctx_lens[r] = self.lengths[r]
+
+    def _consecutive_rows(self, seq_ids: Sequence[Hashable]) -> int:
+        rows = [self.row_of[s] for s in seq_ids]
+        r0 = rows[0]
+        if rows != list(range(r0, r0 + len(rows))):
+            raise ValueError("sequences must occupy consecutive rows in the given order "
+                             "(sequences added one after another do)")
+        return r0
+
+    def _grow_rows(self, r0: int, n_new: Sequence[int]) -> None:
+        """Pinned pages for rows r0.. so each can hold n_new[i] more tokens:
+        one allocation launch and one block-table scatter for all rows."""
+        rows, cols = [], []
+        for i, t in enumerate(n_new):
+            r = r0 + i
+            have = self._pages_of(r)
+            need = _ceil_div(self.lengths[r] + int(t), PAGE_TOKENS)
+            if need > self.max_blocks:
+                raise ValueError(f"sequence would need {need} blocks > max_blocks_per_seq={self.max_blocks}")
+            rows.extend([r] * (need - have))
+            cols.extend(range(have, need))
+        if rows:
+            ids, _ = self.pool.alloc_pages(len(rows), pin=True)
+            idx = torch.tensor([rows, cols], dtype=torch.int64).to(self.device, non_blocking=True)
+            self.block_table[idx[0], idx[1]] = ids
+
+    def append_prefill_batch(self, seq_ids: Sequence[Hashable], k: torch.Tensor, v: torch.Tensor,
+                             cu_tokens: Sequence[int]) -> None:
+        """Append several sequences' new tokens with one allocation and one
+        append launch: sequence i gets rows cu_tokens[i]..cu_tokens[i+1]-1 of
+        k, v [num_layers, total, Hkv, D]. The sequences must sit on
+        consecutive rows (e.g. added one after another)."""
+        seq_ids = list(seq_ids)
+        n = len(seq_ids)
+        cu = [int(c) for c in cu_tokens]
+        if len(cu) != n + 1 or cu[0] != 0 or any(b < a for a, b in zip(cu, cu[1:])):
+            raise ValueError("cu_tokens must be n+1 non-decreasing offsets from 0")
+        if k.dim() != 4 or k.shape[0] != self.num_layers or k.shape[1] < cu[-1]:
+            raise ValueError("k, v must be [num_layers, >= total tokens, Hkv, D]")
+        r0 = self._consecutive_rows(seq_ids)
+        T = [cu[i + 1] - cu[i] for i in range(n)]
+        self._grow_rows(r0, T)
+        meta = torch.tensor(cu + [self.lengths[r0 + i] for i in range(n)], dtype=torch.int32).to(
+            self.device, non_blocking=True)
+        self.pool.append(k[:, :cu[-1]], v[:, :cu[-1]], meta[:n + 1], meta[n + 1:], self.block_table[r0:r0 + n],
+                         layer0=0, max_blocks=self.max_blocks)
+        for i in range(n):
+            self.lengths[r0 + i] += T[i]
+        self.ctx_lens[r0:r0 + n].copy_(torch.tensor(self.lengths[r0:r0 + n], dtype=torch.int32),
+                                       non_blocking=True)
+
+    def prefill_attention_batch(self, layer: int, seq_ids: Sequence[Hashable], q: torch.Tensor,
+                                cu_q: torch.Tensor, start_pos: torch.Tensor, scale: Optional[float] = None,
+                                out: Optional[torch.Tensor] = None,
+                                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """Causal attention of several sequences' new tokens in one launch:
+        q [total, Hq, D], rows cu_q[i]..cu_q[i+1]-1 of sequence i at positions
+        start_pos[i]+t (device int32 tensors, appended already). Sequences on
+        consecutive rows."""
+        seq_ids = list(seq_ids)
+        r0 = self._consecutive_rows(seq_ids)
+        n = len(seq_ids)
+        try:
+            return self.pool.prefill_attn(layer, q, cu_q, start_pos, self.block_table[r0:r0 + n], scale=scale,
+                                          out=out, out_dtype=out_dtype, max_blocks=self.max_blocks)
+        except N.SCKVError as e:
+            if e.code != N.SCKV_ERR_UNSUPPORTED:
+                raise
+        # pools / head groupings the tensor-core kernel does not build: one
+        # sequence at a time through the decode kernel (reads the offsets back)
+        cu = cu_q.tolist()
+        st = start_pos.tolist()
+        res = out if out is not None else torch.empty(q.shape, dtype=out_dtype or q.dtype, device=self.device)
+        for i, sid in enumerate(seq_ids):
+            if cu[i + 1] > cu[i]:
+                res[cu[i]:cu[i + 1]] = self.prefill_attention(layer, sid, q[cu[i]:cu[i + 1]], st[i], scale=scale,
+                                                              out_dtype=res.dtype)
+        return res
 
     def prefill_attention(self, layer: int, seq_id: Hashable, q: torch.Tensor, start: int,
                           scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
