@@ -48,6 +48,13 @@ __device__ __forceinline__ int clamp_ctx(const DecodeParams& p, int b, bool repo
 // caller can use the CUDA-core kernel instead.
 int launch_decode_mma(const sckv_pool* pool, int G, const DecodeParams& prm, cudaStream_t stream);
 
+// Causal prefill on tcgen05 / tensor memory (sckv_prefill_tc.cu) for f16 and
+// bf16 pools; SCKV_ERR_UNSUPPORTED for anything else.
+int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads, int n_seqs,
+                      int n_tokens, const int32_t* cu_q, const int32_t* start_pos, const int32_t* block_table,
+                      int64_t bt_stride, int max_blocks, float scale, void* out, int out_dtype, int lg_g,
+                      cudaStream_t stream);
+
 // Merge of split partials (shared by both decode kernels).
 int launch_combine(const DecodeParams& prm, cudaStream_t stream);
 

@@ -27,6 +27,7 @@ enum SckvKernelId : int32_t {
   KID_PIN = 10,
   KID_EVICT = 11,
   KID_RESERVE = 12,
+  KID_PREFILL = 13,
 };
 
 // Allocator control words (int64, device).
@@ -36,6 +37,7 @@ enum SckvCtl : int {
   CTL_CLOCK = 2,      // step clock
   CTL_EVICTIONS = 3,  // evictions (LRU victims + explicit frees)
   CTL_ALLOCATED = 4,  // pages currently allocated
+  CTL_PREFILL_NEXT = 6,  // next work item of the running prefill launch (zeroed before each)
   CTL_WORDS = 8,
 };
 
@@ -74,10 +76,13 @@ struct sckv_pool {
   // TMA tensor map over the page data (a CUtensorMap, encoded on first use
   // by the tensor-core decode kernel).
   alignas(64) unsigned char tmap_kv[128];
-  int tmap_ready;  // head-group size the map was encoded for (0 = not yet)
+  int tmap_ready;  // box shape code the map was encoded for (0 = not yet)
   // A second map with one-head boxes (prefill attention).
   alignas(64) unsigned char tmap_kv1[128];
   int tmap1_ready;
+  // A third map with one-head, K-or-V boxes (tensor-memory prefill).
+  alignas(64) unsigned char tmap_kv2[128];
+  int tmap2_ready;
 };
 
 static inline int sckv_elem_bytes(int dtype) {

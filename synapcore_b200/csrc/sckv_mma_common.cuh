@@ -115,27 +115,36 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Encode the pool's tensor map once: a 5-D view (dim, token, head, K|V,
-// layer*page slab) with boxes of 128 bytes x 16 tokens x HG heads x K and V,
-// 128-byte swizzle.
-inline int ensure_tmap(const sckv_pool* pool, int HG, unsigned char* slot, int* ready) {
-  if (*ready == HG) return SCKV_OK;
+// Rank-5 TMA map over the page data: dims {head dim, token, head, K|V,
+// layer x page}, boxes of {128 bytes of the head dim, 16 tokens, HG heads,
+// KVB of K|V, 1 page}, 128-byte swizzle. `slot` caches it in the pool handle;
+// `ready` records HG * 4 + KVB once encoded.
+// The driver's tensor-map encoder, looked up once (nullptr if unavailable).
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || fn == nullptr)
-      return sckv_record_error(__FILE__, __LINE__, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled not found");
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn != nullptr)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
+  return encode;
+}
+
+inline int ensure_tmap(const sckv_pool* pool, int HG, unsigned char* slot, int* ready, int KVB = 2) {
+  if (*ready == HG * 4 + KVB) return SCKV_OK;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr)
+    return sckv_record_error(__FILE__, __LINE__, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled not found");
   const cuuint64_t eb = (cuuint64_t)sckv_elem_bytes(pool->kv_dtype);
   const cuuint64_t D = (cuuint64_t)pool->head_dim, H = (cuuint64_t)pool->num_kv_heads;
   const cuuint64_t dims[5] = {D, (cuuint64_t)SCKV_PAGE_TOKENS, H, 2,
                               (cuuint64_t)pool->num_layers * (cuuint64_t)pool->max_pages};
   const cuuint64_t strides[4] = {D * eb, SCKV_PAGE_TOKENS * D * eb, H * SCKV_PAGE_TOKENS * D * eb,
                                  2 * H * SCKV_PAGE_TOKENS * D * eb};
-  const cuuint32_t box[5] = {(cuuint32_t)(128 / eb), (cuuint32_t)SCKV_PAGE_TOKENS, (cuuint32_t)HG, 2, 1};
+  const cuuint32_t box[5] = {(cuuint32_t)(128 / eb), (cuuint32_t)SCKV_PAGE_TOKENS, (cuuint32_t)HG, (cuuint32_t)KVB,
+                             1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUtensorMapDataType dt = (eb == 2) ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUresult r = encode(reinterpret_cast<CUtensorMap*>(slot), dt, 5, pool->data, dims, strides, box, estr,
@@ -146,7 +155,7 @@ inline int ensure_tmap(const sckv_pool* pool, int HG, unsigned char* slot, int* 
     snprintf(what, sizeof what, "CUresult %d", (int)r);
     return sckv_record_error(__FILE__, __LINE__, "cuTensorMapEncodeTiled", what);
   }
-  *ready = HG;
+  *ready = HG * 4 + KVB;
   return SCKV_OK;
 }
 

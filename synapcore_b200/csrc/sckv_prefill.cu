@@ -18,6 +18,8 @@
 // kernel. FP8 pages decode in registers; their V scale is folded into P
 // relative to a per-item reference scale.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "sckv_decode_common.cuh"
 #include "sckv_mma_common.cuh"
@@ -502,9 +504,19 @@ extern "C" int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q, int 
   prm.q_dtype = q_dtype;
   prm.out_dtype = out_dtype;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  // f16 / bf16 pools: the tensor-memory kernel (sckv_prefill_tc.cu) unless
+  // SCKV_PREFILL_KERNEL=mma asks for this one
+  const char* env = getenv("SCKV_PREFILL_KERNEL");
+  const bool forced = env != nullptr && strcmp(env, "mma") == 0;
+  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  if (!forced) {
+    const int rc = launch_prefill_tc(pool, layer, q, q_dtype, num_q_heads, n_seqs, n_tokens, cu_q, start_pos,
+                                     block_table, bt_stride, max_blocks, scale, out, out_dtype, lg,
+                                     as_stream(stream));
+    if (rc != SCKV_ERR_UNSUPPORTED) return rc;
+  }
   const int BQ = kRows >> lg;
   const int max_tiles = (n_tokens + BQ - 1) / BQ + n_seqs;  // upper bound on sum of ceil(T_s / BQ)
-  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
   cudaStream_t s = as_stream(stream);
   switch (pool->kv_dtype) {
     case SCKV_DTYPE_F16: return launch_prefill<SCKV_DTYPE_F16, 6>(pool, prm, max_tiles, s);

@@ -191,3 +191,51 @@ def test_paged_cache_int8_prefill_and_decode_match_oracle(cuda_device):
         ref = sdpa_decode(qd[0], kd[layer], vd[layer])
         assert _rel_err(got.cpu().numpy()[0], ref) <= TOL
     cache.check()
+
+
+@pytest.mark.parametrize("kv,hq,hkv", [("fp16", 8, 8), ("fp16", 16, 4), ("bf16", 16, 4), ("bf16", 32, 2)])
+def test_tensor_memory_kernel_rescales_and_matches_mma_kernel(cuda_device, kv, hq, hkv, monkeypatch):
+    """Keys grow in magnitude along the sequence, so the running max moves
+    by more than 2^8 several times and the tensor-memory kernel must rescale
+    its O accumulator in TMEM. Its output matches the oracle and the
+    mma.sync kernel (SCKV_PREFILL_KERNEL=mma) within the tolerance."""
+    from synapcore_b200.pool import KVPool
+
+    rng = np.random.default_rng(12)
+    D, P = 128, 64
+    T, start = [300, 77], [50, 0]
+    ctx = [s + t for s, t in zip(start, T)]
+    pool = KVPool(1, hkv, D, P, kv, device=cuda_device)
+    ora = PagedPoolOracle(1, hkv, D, P, kv)
+    growth = (1.0 + np.arange(P * PAGE_TOKENS, dtype=np.float32) / 40.0).reshape(P, 1, 1, PAGE_TOKENS, 1)
+    k = (rng.standard_normal((P, 1, hkv, PAGE_TOKENS, D)).astype(np.float32) * growth)
+    v = rng.standard_normal((P, 1, hkv, PAGE_TOKENS, D)).astype(np.float32)
+    src_t = torch.float16 if kv == "fp16" else torch.bfloat16
+    k_t, v_t = torch.from_numpy(k).to(src_t), torch.from_numpy(v).to(src_t)
+    ids = np.arange(P, dtype=np.int32)
+    pool.write_pages(torch.from_numpy(ids).to(cuda_device), k_t.to(cuda_device), v_t.to(cuda_device))
+    ora.write_pages(ids, k_t.float().numpy(), v_t.float().numpy())
+    mb = (max(ctx) + PAGE_TOKENS - 1) // PAGE_TOKENS
+    bt = np.stack([np.arange(mb, dtype=np.int32), np.arange(mb, 2 * mb, dtype=np.int32)])  # page i = tokens 16i..
+    cu = np.array([0, T[0], T[0] + T[1]], np.int32)
+    st = np.array(start, np.int32)
+    qdt = torch.float16 if kv == "fp16" else torch.bfloat16
+    q_t = torch.from_numpy(rng.standard_normal((sum(T), hq, D)).astype(np.float32)).to(qdt)
+    ref = ora.prefill(0, q_t.float().numpy(), cu, st, bt)
+    outs = {}
+    for which in ("tc", "mma"):
+        if which == "mma":
+            monkeypatch.setenv("SCKV_PREFILL_KERNEL", "mma")
+        else:
+            monkeypatch.delenv("SCKV_PREFILL_KERNEL", raising=False)
+        o = pool.prefill_attn(0, q_t.to(cuda_device), torch.from_numpy(cu).to(cuda_device),
+                              torch.from_numpy(st).to(cuda_device), torch.from_numpy(bt).to(cuda_device),
+                              out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        pool.raise_on_status()
+        outs[which] = o.cpu().numpy()
+    for which, got in outs.items():
+        for b in range(2):
+            err = _rel_err(got[cu[b]:cu[b + 1]], ref[cu[b]:cu[b + 1]])
+            assert err <= TOL, (which, b, err)
+    assert _rel_err(outs["tc"], outs["mma"]) <= TOL
