@@ -795,7 +795,9 @@ def bench_mix(args, w, world, rank, local):
                      "peak_kind": peak_kind, "kernel": "decode_kernel (+combine) per layer launch",
                      "bytes_per_launch": int(dec_launch_bytes), "avg_launch_ms": round(dec_avg_ms, 4)},
         "prefill_roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
-                             "frac": round(tflops / tc_peak, 4), "kernel": "prefill_kernel per layer launch",
+                             "frac": round(tflops / tc_peak, 4),
+                             "kernel": ("prefill_tc_kernel (tcgen05)" if w["kv"] in ("fp16", "bf16")
+                                        else "prefill_kernel (mma.sync)") + " per layer launch",
                              "flops_per_launch": int(np.mean(pre_flops) / L), "avg_launch_ms": round(pre_avg_ms, 4)},
         "clocks": clocks,
     }
