@@ -207,6 +207,29 @@ SCKV_API int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q,
                       int max_blocks, float scale, void* out, int out_dtype,
                       void* stream);
 
+/* Fused attention input for new tokens (16-bit pools): optional RMSNorm of
+ * q and k, rotary position embedding of both at positions start_pos[b] + i,
+ * then the K/V append of sckv_append for one layer; the rotated q lands in
+ * q_out. Replaces the QK-norm, RoPE and KV-cache concat of
+ * ModularAttentionEngine.forward_numpy (models/adapters.py:1171-1207, with
+ * rmsnorm_f32 :1129-1132 and apply_rope_f32 :1134-1146), in fp32 and the
+ * reference's operation order.
+ * q_in/q_out : [n_tokens][num_q_heads][head_dim]; k_in/v_in [n_tokens][Hkv][D].
+ * q_norm_len / k_norm_len: 0 (no norm), head_dim (per-head fp16 weights) or
+ * heads x head_dim (one norm over the whole projection).
+ * inv_freq: device fp32 [head_dim / 2], 1 / theta^(2i / head_dim) as the
+ * reference computes it; positions are divided by rope_scaling.
+ * head_dim 128, at most 256 heads; other pools: SCKV_ERR_UNSUPPORTED. */
+SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
+                     void* q_out, int num_q_heads, int q_dtype,
+                     int q_out_dtype, const void* k_in, const void* v_in,
+                     int src_dtype, const void* q_norm_w, int q_norm_len,
+                     const void* k_norm_w, int k_norm_len, float eps,
+                     const float* inv_freq, float rope_scaling, int n_seqs,
+                     int n_tokens, const int32_t* cu_tokens,
+                     const int32_t* start_pos, const int32_t* block_table,
+                     int64_t bt_stride, int max_blocks, void* stream);
+
 /* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
 #define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)
 

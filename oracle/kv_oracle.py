@@ -134,6 +134,58 @@ def sdpa_decode(q_f32: np.ndarray, k_f16: np.ndarray, v_f16: np.ndarray, scale: 
     return (p @ v)[:, 0, :]
 
 
+def rope_inv_freq(theta: float, head_dim: int) -> np.ndarray:
+    """models/adapters.py:1123-1127 (float32)."""
+    return 1.0 / (float(theta) ** (np.arange(0, head_dim, 2, dtype=np.float32) / float(head_dim)))
+
+
+def rmsnorm_f32(x_f32: np.ndarray, weight_fp16: np.ndarray, eps: float) -> np.ndarray:
+    """models/adapters.py:1129-1132: x / sqrt(mean(x^2) + eps) * w over the last axis."""
+    var = np.mean(x_f32 * x_f32, axis=-1, keepdims=True)
+    normed = x_f32 * (1.0 / np.sqrt(var + eps))
+    return normed * weight_fp16.astype(np.float32)
+
+
+def apply_rope_f32(x_bhld: np.ndarray, inv_freq: np.ndarray, pos_offset: int, scaling: float) -> np.ndarray:
+    """models/adapters.py:1134-1146: rotate the two halves of the head dim by
+    angle (pos / scaling) * inv_freq[i]."""
+    seq_len = x_bhld.shape[2]
+    positions = np.arange(pos_offset, pos_offset + seq_len, dtype=np.float32)[:, None] / scaling
+    angles = positions * inv_freq[None, :]
+    cos = np.cos(angles)[None, None, :, :]
+    sin = np.sin(angles)[None, None, :, :]
+    half = x_bhld.shape[-1] // 2
+    x1, x2 = x_bhld[..., :half], x_bhld[..., half:]
+    return np.concatenate([x1 * cos - x2 * sin, x2 * cos + x1 * sin], axis=-1)
+
+
+def qk_norm_rope(q: np.ndarray, k: np.ndarray, q_w: Optional[np.ndarray], k_w: Optional[np.ndarray], eps: float,
+                 inv_freq: np.ndarray, scaling: float, pos_offset: int) -> Tuple[np.ndarray, np.ndarray]:
+    """The attention-input steps of forward_numpy (models/adapters.py:1171-1195)
+    for one sequence: q [T, Hq, D], k [T, Hkv, D] float32 straight from the
+    projections; optional QK-norm (weights of D = per head, else over the
+    whole projection), RoPE from position pos_offset. Returns (q rotated,
+    float32 [T, Hq, D]; k rotated as stored in the cache, float16 [T, Hkv, D])."""
+    T, hq, d = q.shape
+    hkv = k.shape[1]
+    qf = q.reshape(1, T, hq * d).astype(np.float32)
+    kf = k.reshape(1, T, hkv * d).astype(np.float32)
+    if q_w is not None and k_w is not None:
+        if q_w.shape[-1] == hq * d:
+            qf = rmsnorm_f32(qf, q_w, eps)
+        else:
+            qf = rmsnorm_f32(qf.reshape(1, T, hq, d), q_w, eps).reshape(1, T, hq * d)
+        if k_w.shape[-1] == hkv * d:
+            kf = rmsnorm_f32(kf, k_w, eps)
+        else:
+            kf = rmsnorm_f32(kf.reshape(1, T, hkv, d), k_w, eps).reshape(1, T, hkv * d)
+    qb = qf.reshape(1, T, hq, d).transpose(0, 2, 1, 3)
+    kb = kf.reshape(1, T, hkv, d).transpose(0, 2, 1, 3)
+    qr = apply_rope_f32(qb, inv_freq, pos_offset, scaling)
+    kr = apply_rope_f32(kb, inv_freq, pos_offset, scaling)
+    return qr[0].transpose(1, 0, 2), kr[0].transpose(1, 0, 2).astype(np.float16)
+
+
 def sdpa_prefill(q_f32: np.ndarray, k: np.ndarray, v: np.ndarray, start: int,
                  scale: Optional[float] = None) -> np.ndarray:
     """Causal prompt pass (models/adapters.py:1209-1229 with the -1e9 mask of

@@ -8,13 +8,14 @@ sm_100a CUDA kernels in libsckv.so through its C ABI (include/sckv.h).
 from ._native import SCKVBoundsError, SCKVError, SCKVPoolExhausted
 from .arena import PagedKVArena
 from .kv_index import KVPrefixIndex
-from .paged_cache import PagedKVCache
-from .pool import KVPool
+from .paged_cache import DecodeStepGraph, PagedKVCache
+from .pool import KVPool, rope_inv_freq
 from .prefix_cache import NativeKVPrefixCache, PagedKVStats, chain_merkle_prefix_hash
 from .scheduler import ContinuousBatchScheduler, PagedDecoderModel, PrefixPageIndex
 
 __all__ = [
     "ContinuousBatchScheduler",
+    "DecodeStepGraph",
     "KVPool",
     "PagedDecoderModel",
     "PagedKVCache",
@@ -27,4 +28,5 @@ __all__ = [
     "SCKVError",
     "SCKVPoolExhausted",
     "chain_merkle_prefix_hash",
+    "rope_inv_freq",
 ]

@@ -512,6 +512,116 @@ int grid_for(const sckv_pool* p, int64_t work_items, int threads) {
 
 bool is_src_dtype(int d) { return d == SCKV_DTYPE_F16 || d == SCKV_DTYPE_BF16 || d == SCKV_DTYPE_F32; }
 
+// ---------------------------------------------------------------------------
+// Fused attention input for new tokens: optional RMSNorm of q and k, rotary
+// position embedding of both, then the K/V append (16-bit pools). Restates
+// models/adapters.py:1171-1207 in the reference's operation order, in fp32:
+//   rmsnorm_f32 (:1129-1132): x * (1 / sqrt(mean(x^2) + eps)) * w, over one
+//     head (weights of head_dim) or the whole projection (H x head_dim);
+//   apply_rope_f32 (:1134-1146): angle_i = (pos / scaling) * inv_freq[i],
+//     out = [x1 cos - x2 sin, x2 cos + x1 sin] on the two halves;
+//   k, v -> pool type (round to nearest even) into the token's page slot.
+// The rotated q goes to q_out for the attention call. One CTA (8 warps) per
+// token; a warp handles one head row of 128 values, 4 per lane: dims l and
+// l + 32 of the first half and their partners in the second half, so the
+// rotation needs no lane exchange.
+constexpr int kRopeWarps = 8;
+constexpr int kRopeMaxHeads = 256;
+
+__device__ __forceinline__ float rope_warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(kRopeWarps * 32) append_rope_kernel(
+    Geo g, int layer, const void* q_in, void* q_out, int hq, int q_dtype, int q_out_dtype, const void* k_in,
+    const void* v_in, int src_dtype, const __half* q_w, int q_norm_len, const __half* k_w, int k_norm_len,
+    float eps, const float* inv_freq, float rope_scaling, int n_seqs, int n_tokens, const int32_t* cu,
+    const int32_t* start_pos, const int32_t* bt, int64_t stride, int max_blocks) {
+  __shared__ float ss[2 * kRopeMaxHeads];  // sum of squares per q head, then per k head
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = g.D, half = D / 2;  // D == 128
+  const int hk = g.H;
+  const int b = find_seq(cu, n_seqs, t);
+  const int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
+  const int64_t page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
+  const int dims[4] = {lane, lane + 32, half + lane, half + lane + 32};
+  // pass 1: sums of squares of every q and k head row
+  for (int r = warp; r < hq + hk; r += kRopeWarps) {
+    const bool isq = r < hq;
+    const int64_t base = isq ? ((int64_t)t * hq + r) * D : ((int64_t)t * hk + (r - hq)) * D;
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = sckv_load_as_float(isq ? q_in : k_in, base + dims[i], isq ? q_dtype : src_dtype);
+      a = fmaf(x, x, a);
+    }
+    a = rope_warp_sum(a);
+    if (lane == 0) ss[isq ? r : kRopeMaxHeads + (r - hq)] = a;
+  }
+  __syncthreads();
+  float q_full = 0.f, k_full = 0.f;
+  if (q_norm_len == hq * D && q_norm_len != D)
+    for (int h = 0; h < hq; ++h) q_full += ss[h];
+  if (k_norm_len == hk * D && k_norm_len != D)
+    for (int h = 0; h < hk; ++h) k_full += ss[kRopeMaxHeads + h];
+  const float fpos = __fdiv_rn((float)pos, rope_scaling);
+  float cs[2], sn[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float ang = __fmul_rn(fpos, __ldg(inv_freq + dims[i]));
+    sincosf(ang, &sn[i], &cs[i]);
+  }
+  // pass 2: normalise, rotate, store
+  for (int r = warp; r < hq + hk; r += kRopeWarps) {
+    const bool isq = r < hq;
+    const int h = isq ? r : r - hq;
+    const int64_t base = isq ? ((int64_t)t * hq + h) * D : ((int64_t)t * hk + h) * D;
+    const int nlen = isq ? q_norm_len : k_norm_len;
+    const __half* w = isq ? q_w : k_w;
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = sckv_load_as_float(isq ? q_in : k_in, base + dims[i], isq ? q_dtype : src_dtype);
+    if (nlen != 0) {
+      const bool per_head = nlen == D;
+      const float sum = per_head ? ss[isq ? h : kRopeMaxHeads + h] : (isq ? q_full : k_full);
+      const float var = __fdiv_rn(sum, (float)nlen);
+      const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int wi = per_head ? dims[i] : h * D + dims[i];
+        x[i] = __fmul_rn(__fmul_rn(x[i], inv), __half2float(w[wi]));
+      }
+    }
+    float y[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      y[i] = __fsub_rn(__fmul_rn(x[i], cs[i]), __fmul_rn(x[i + 2], sn[i]));
+      y[i + 2] = __fadd_rn(__fmul_rn(x[i + 2], cs[i]), __fmul_rn(x[i], sn[i]));
+    }
+    if (isq) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sckv_store_from_float(q_out, base + dims[i], q_out_dtype, y[i]);
+    } else if (page >= 0) {
+      const int64_t off = row_off(g, layer, page, 0, h, pos % SCKV_PAGE_TOKENS);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sckv_store_from_float(g.data, off + dims[i], g.dtype, y[i]);
+    }
+  }
+  // v: copied into the page as is
+  if (page >= 0) {
+    for (int r = warp; r < hk; r += kRopeWarps) {
+      const int64_t base = ((int64_t)t * hk + r) * D;
+      const int64_t off = row_off(g, layer, page, 1, r, pos % SCKV_PAGE_TOKENS);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sckv_store_from_float(g.data, off + dims[i], g.dtype, sckv_load_as_float(v_in, base + dims[i], src_dtype));
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" int sckv_append(sckv_pool* p, int layer0, int n_layers, const void* k_new, const void* v_new,
@@ -616,6 +726,37 @@ extern "C" int sckv_copy_pages(sckv_pool* p, const int32_t* src_ids, const int32
   const int64_t slab_bytes = sckv_slab_elems(p) * sckv_elem_bytes(p->kv_dtype);
   int64_t work = (int64_t)n * p->num_layers * (slab_bytes / 16);
   copy_pages_kernel<<<grid_for(p, work, 256), 256, 0, as_stream(stream)>>>(g, src_ids, dst_ids, n);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+extern "C" int sckv_append_rope(sckv_pool* p, int layer, const void* q_in, void* q_out, int num_q_heads,
+                                int q_dtype, int q_out_dtype, const void* k_in, const void* v_in, int src_dtype,
+                                const void* q_norm_w, int q_norm_len, const void* k_norm_w, int k_norm_len,
+                                float eps, const float* inv_freq, float rope_scaling, int n_seqs, int n_tokens,
+                                const int32_t* cu_tokens, const int32_t* start_pos, const int32_t* block_table,
+                                int64_t bt_stride, int max_blocks, void* stream) {
+  if (p == nullptr || layer < 0 || layer >= p->num_layers || n_seqs < 0 || n_tokens < 0 || num_q_heads <= 0)
+    return SCKV_ERR_INVALID_ARG;
+  if (p->kv_dtype != SCKV_DTYPE_F16 && p->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+  if (p->head_dim != 128 || num_q_heads > kRopeMaxHeads || p->num_kv_heads > kRopeMaxHeads)
+    return SCKV_ERR_UNSUPPORTED;
+  if (!is_src_dtype(src_dtype) || !is_src_dtype(q_dtype) || !is_src_dtype(q_out_dtype)) return SCKV_ERR_INVALID_ARG;
+  const int D = p->head_dim;
+  if (q_norm_len != 0 && q_norm_len != D && q_norm_len != num_q_heads * D) return SCKV_ERR_INVALID_ARG;
+  if (k_norm_len != 0 && k_norm_len != D && k_norm_len != p->num_kv_heads * D) return SCKV_ERR_INVALID_ARG;
+  if ((q_norm_len && !q_norm_w) || (k_norm_len && !k_norm_w)) return SCKV_ERR_INVALID_ARG;
+  if (!(rope_scaling > 0.f) || !(eps >= 0.f)) return SCKV_ERR_INVALID_ARG;
+  if (n_seqs == 0 || n_tokens == 0) return SCKV_OK;
+  if (!q_in || !q_out || !k_in || !v_in || !inv_freq || !cu_tokens || !start_pos || !block_table ||
+      bt_stride < max_blocks || max_blocks <= 0)
+    return SCKV_ERR_INVALID_ARG;
+  Geo g = geo_of(p);
+  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  append_rope_kernel<<<n_tokens, kRopeWarps * 32, 0, as_stream(stream)>>>(
+      g, layer, q_in, q_out, num_q_heads, q_dtype, q_out_dtype, k_in, v_in, src_dtype,
+      reinterpret_cast<const __half*>(q_norm_w), q_norm_len, reinterpret_cast<const __half*>(k_norm_w), k_norm_len,
+      eps, inv_freq, rope_scaling, n_seqs, n_tokens, cu_tokens, start_pos, block_table, bt_stride, max_blocks);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }

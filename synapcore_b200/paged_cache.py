@@ -328,3 +328,67 @@ class PagedKVCache:
     def check(self) -> None:
         """Raise if any kernel recorded an error in the device status word."""
         self.pool.raise_on_status()
+
+
+class DecodeStepGraph:
+    """One decode step of a `PagedKVCache` over rows 0..n_rows-1, captured
+    once in a CUDA graph and replayed: page reservation on the device
+    allocator, then for every layer the new token's K/V append and the
+    decode attention (2 + 3 x num_layers kernels issued by one call).
+
+    The step reads its inputs from static buffers `q` [L, n, Hq, D] and `k`,
+    `v` [L, n, Hkv, D] and writes `out` [L, n, Hq, D]; fill them (copy or
+    compute into them) before each `replay()`. Block tables and lengths are
+    read on the device at replay time, so sequences joining, leaving or
+    moving between rows keep the graph valid as long as rows 0..n_rows-1 are
+    the decode batch; another batch size needs another graph.
+    """
+
+    def __init__(self, cache: PagedKVCache, n_rows: int, q_dtype: torch.dtype = torch.float16,
+                 out_dtype: Optional[torch.dtype] = None, num_q_heads: Optional[int] = None,
+                 scale: Optional[float] = None):
+        if not 0 < n_rows <= cache.n_live:
+            raise ValueError("n_rows must be between 1 and the number of live sequences")
+        self.cache, self.n_rows = cache, int(n_rows)
+        L, hkv, d = cache.num_layers, cache.num_kv_heads, cache.head_dim
+        hq = hkv if num_q_heads is None else int(num_q_heads)
+        src_dt = torch.bfloat16 if cache.pool.kv_dtype == "bf16" else torch.float16
+        dev = cache.device
+        self.q = torch.zeros((L, n_rows, hq, d), dtype=q_dtype, device=dev)
+        self.k = torch.zeros((L, n_rows, hkv, d), dtype=src_dt, device=dev)
+        self.v = torch.zeros((L, n_rows, hkv, d), dtype=src_dt, device=dev)
+        self.out = torch.empty((L, n_rows, hq, d), dtype=out_dtype or q_dtype, device=dev)
+        pool = cache.pool
+        self._ws = torch.empty(max(16, pool.decode_workspace_bytes(n_rows, hq, cache.max_blocks, cache.chunk_pages)),
+                               dtype=torch.uint8, device=dev)
+        self._scale = scale
+        # one eager attention (it only reads the pool) sets up the kernels'
+        # launch attributes and tensor maps outside the capture
+        pool.decode_attn(0, self.q[0], cache.block_table[:n_rows], cache.ctx_lens[:n_rows], scale=scale,
+                         out=self.out[0], max_blocks=cache.max_blocks, chunk_pages=cache.chunk_pages,
+                         workspace=self._ws)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def _step(self) -> None:
+        c, n = self.cache, self.n_rows
+        pool = c.pool
+        pool.reserve_decode(c.block_table, c.ctx_lens, n_seqs=n, max_blocks=c.max_blocks)
+        start = c.ctx_lens[:n] - 1
+        for layer in range(c.num_layers):
+            pool.append(self.k[layer], self.v[layer], c._arange[:n + 1], start, c.block_table[:n], layer0=layer,
+                        max_blocks=c.max_blocks)
+            pool.decode_attn(layer, self.q[layer], c.block_table[:n], c.ctx_lens[:n], scale=self._scale,
+                             out=self.out[layer], max_blocks=c.max_blocks, chunk_pages=c.chunk_pages,
+                             workspace=self._ws)
+
+    def replay(self) -> torch.Tensor:
+        """Run the captured step on the current stream; returns `out`."""
+        if self.cache.n_live < self.n_rows:
+            raise RuntimeError("fewer live sequences than the captured batch")
+        self.graph.replay()
+        for r in range(self.n_rows):
+            self.cache.lengths[r] += 1
+        return self.out

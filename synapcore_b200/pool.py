@@ -42,6 +42,15 @@ def torch_dtype_code(dt: torch.dtype) -> int:
         raise TypeError(f"unsupported tensor dtype {dt}; expected float16, bfloat16 or float32") from None
 
 
+def rope_inv_freq(theta: float, head_dim: int, device: Optional[torch.device] = None) -> torch.Tensor:
+    """1 / theta^(2i / head_dim), i < head_dim / 2, computed in float32 exactly as
+    ModularAttentionEngine.__init__ does (models/adapters.py:1123-1127)."""
+    import numpy as np
+
+    inv = 1.0 / (float(theta) ** (np.arange(0, head_dim, 2, dtype=np.float32) / float(head_dim)))
+    return torch.from_numpy(np.asarray(inv, dtype=np.float32)).to(device if device is not None else "cpu")
+
+
 def _stream_ptr(stream: Optional[torch.cuda.Stream]) -> int:
     s = stream if stream is not None else torch.cuda.current_stream()
     return s.cuda_stream
@@ -162,6 +171,57 @@ class KVPool:
                                      torch_dtype_code(k_new.dtype), n_seqs, nt, cu_tokens.data_ptr(),
                                      start_pos.data_ptr(), bt.data_ptr(), bt.stride(0), mb, _stream_ptr(stream)),
                 "sckv_append")
+
+    def append_rope(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                    cu_tokens: torch.Tensor, start_pos: torch.Tensor, block_table: torch.Tensor,
+                    inv_freq: torch.Tensor, rope_scaling: float = 1.0, q_norm_w: Optional[torch.Tensor] = None,
+                    k_norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6, q_out: Optional[torch.Tensor] = None,
+                    q_out_dtype: Optional[torch.dtype] = None, max_blocks: Optional[int] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """QK-norm (optional) + RoPE + append for one layer in one launch.
+        q [n_tokens, Hq, D], k_new / v_new [n_tokens, Hkv, D] straight from the
+        projections; returns the rotated q (q_out)."""
+        q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+        nt, hq, d = q.shape
+        n_seqs = cu_tokens.numel() - 1
+        bt = block_table if block_table.dim() == 2 else block_table.view(1, -1)
+        mb = bt.shape[1] if max_blocks is None else int(max_blocks)
+        if d != self.head_dim or tuple(k_new.shape) != (nt, self.num_kv_heads, d) or k_new.shape != v_new.shape:
+            raise ValueError("q must be [n_tokens, Hq, D] and k_new / v_new [n_tokens, Hkv, D]")
+        if k_new.dtype != v_new.dtype:
+            raise TypeError("k_new and v_new must have the same dtype")
+        if not 0 <= layer < self.num_layers:
+            raise ValueError("layer out of range")
+        for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new)):
+            _need(t, name, self.device)
+        _need(inv_freq, "inv_freq", self.device, torch.float32, d // 2)
+        _need(cu_tokens, "cu_tokens", self.device, torch.int32, 1)
+        _need(start_pos, "start_pos", self.device, torch.int32, n_seqs)
+        _need(bt, "block_table", self.device, torch.int32, contiguous=False)
+        if bt.dim() != 2 or bt.shape[0] < n_seqs or mb > bt.shape[1] or bt.stride(1) != 1:
+            raise ValueError("block_table must be [>= n_seqs, >= max_blocks] with unit column stride")
+        weights = []
+        for name, w in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w)):
+            if w is None:
+                weights.append((None, 0))
+                continue
+            _need(w, name, self.device, torch.float16)
+            weights.append((w, w.numel()))
+        if q_out is None:
+            q_out = torch.empty((nt, hq, d), dtype=q_out_dtype or q.dtype, device=self.device)
+        else:
+            _need(q_out, "q_out", self.device)
+            if tuple(q_out.shape) != (nt, hq, d):
+                raise ValueError("q_out must have q's shape")
+        (qw, qn), (kw, kn) = weights
+        N.check(self.lib.sckv_append_rope(self.handle, layer, q.data_ptr(), q_out.data_ptr(), hq,
+                                          torch_dtype_code(q.dtype), torch_dtype_code(q_out.dtype), k_new.data_ptr(),
+                                          v_new.data_ptr(), torch_dtype_code(k_new.dtype), _ptr(qw), qn, _ptr(kw), kn,
+                                          float(eps), inv_freq.data_ptr(), float(rope_scaling), n_seqs, nt,
+                                          cu_tokens.data_ptr(), start_pos.data_ptr(), bt.data_ptr(), bt.stride(0), mb,
+                                          _stream_ptr(stream)),
+                "sckv_append_rope")
+        return q_out
 
     def write_pages(self, page_ids: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor,
                     stream: Optional[torch.cuda.Stream] = None) -> None:

@@ -261,6 +261,53 @@ def sdpa_cases(ad, arrays):
     return out
 
 
+def qk_rope_cases(ad, arrays):
+    """QK-norm + RoPE as forward_numpy composes them (models/adapters.py:
+    1171-1195), through the reference engine's own rmsnorm_f32 and
+    apply_rope_f32: per-head norm (Qwen3 style), whole-projection norm
+    (OLMoE style), and no norm with a RoPE scaling factor."""
+    out = []
+    for name, hq, hkv, T, pos, theta, scaling, norm, seed in (
+            ("perhead", 8, 2, 5, 37, 1000000.0, 1.0, "head", 11),
+            ("fullwidth", 4, 4, 3, 4090, 10000.0, 1.0, "full", 12),
+            ("nonorm_scaled", 4, 1, 4, 20000, 500000.0, 2.0, None, 13)):
+        d = 128
+        hidden = hq * d
+        cfg = {"model_type": "mixtral", "num_hidden_layers": 1, "num_experts": 8, "num_experts_per_tok": 2,
+               "hidden_size": hidden, "intermediate_size": hidden * 2, "num_attention_heads": hq,
+               "num_key_value_heads": hkv, "vocab_size": 32000, "rms_norm_eps": 1e-6, "rope_theta": theta}
+        eng = ad.ModularAttentionEngine(ad.MixtralAdapter(cfg).spec)
+        eng.rope_scaling_factor = scaling
+        rng = np.random.default_rng(seed)
+        q = rng.standard_normal((1, T, hq * d)).astype(np.float32) * 3
+        k = rng.standard_normal((1, T, hkv * d)).astype(np.float32) * 3
+        if norm == "head":
+            qw = rng.uniform(0.5, 1.5, d).astype(np.float16)
+            kw = rng.uniform(0.5, 1.5, d).astype(np.float16)
+            qn = eng.rmsnorm_f32(q.reshape(1, T, hq, d), qw).reshape(1, T, hq * d)
+            kn = eng.rmsnorm_f32(k.reshape(1, T, hkv, d), kw).reshape(1, T, hkv * d)
+        elif norm == "full":
+            qw = rng.uniform(0.5, 1.5, hq * d).astype(np.float16)
+            kw = rng.uniform(0.5, 1.5, hkv * d).astype(np.float16)
+            qn, kn = eng.rmsnorm_f32(q, qw), eng.rmsnorm_f32(k, kw)
+        else:
+            qw = kw = None
+            qn, kn = q, k
+        qr = eng.apply_rope_f32(qn.reshape(1, T, hq, d).transpose(0, 2, 1, 3), pos_offset=pos)
+        kr = eng.apply_rope_f32(kn.reshape(1, T, hkv, d).transpose(0, 2, 1, 3), pos_offset=pos)
+        arrays[f"rope_{name}_q"] = q.reshape(T, hq, d)
+        arrays[f"rope_{name}_k"] = k.reshape(T, hkv, d)
+        if qw is not None:
+            arrays[f"rope_{name}_qw"] = qw
+            arrays[f"rope_{name}_kw"] = kw
+        arrays[f"rope_{name}_inv_freq"] = eng.rope_inv_freq
+        arrays[f"rope_{name}_q_rot"] = qr[0].transpose(1, 0, 2)
+        arrays[f"rope_{name}_k_cache"] = kr[0].transpose(1, 0, 2).astype(np.float16)
+        out.append({"name": name, "hq": hq, "hkv": hkv, "T": T, "pos": pos, "theta": theta, "scaling": scaling,
+                    "norm": norm, "eps": 1e-6})
+    return out
+
+
 def scheduler_runs(ne, ad, arrays):
     """The reference ContinuousBatchScheduler (engine/scheduler.py) over a
     stub of the reference engine carrying the seeded weights of
@@ -354,6 +401,7 @@ def main():
         "kv_table_long_context": kv_table_long_context(ne),
         "sdpa": sdpa_cases(ad, arrays),
         "scheduler": scheduler_runs(ne, ad, arrays),
+        "qk_rope": qk_rope_cases(ad, arrays),
         "chain_hash": [ne.chain_merkle_prefix_hash(GOLDEN_SEED_ROOT, list(range(16))),
                        ne.chain_merkle_prefix_hash("00" * 32, [0] * 16),
                        ne.chain_merkle_prefix_hash("ff" * 32, [4294967295] * 16)],
