@@ -64,6 +64,9 @@ WORKLOADS = {
                         qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
     "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                             qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
+    # one layer of the full config-4 launch (4.3 GB), for whole-launch captures
+    "qwen3-fp8-1l": dict(model="Qwen3-8B attention", layers=1, hq=32, hkv=8, d=128, kv="fp8_e4m3",
+                         qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
     # long-context scale-out: 64 sequences per GPU, context ~U[8192, 32768],
     # every step appends one token per sequence (contexts grow). bf16 KV of
     # 512 such sequences is ~1.55 TB, above one 8-GPU box, so each GPU keeps

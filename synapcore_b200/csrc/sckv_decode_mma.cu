@@ -49,8 +49,15 @@ struct MmaSmem {
   static constexpr int kBytes = 1024 + kRingBytes + kScaleBytes + 2 * S * 8 + kRedFloats * 4 + 16;
 };
 
+// Resident CTAs per SM the launch bounds promise: three when the ring and
+// reduction area fit three CTAs' shared memory, else two.
 template <int KVDT, int NQT, int HG, int S>
-__global__ void __launch_bounds__(kThreads, 2)
+constexpr int mma_min_blocks() {
+  return MmaSmem<KVDT, NQT, HG, S>::kBytes <= 74 * 1024 ? 3 : 2;
+}
+
+template <int KVDT, int NQT, int HG, int S>
+__global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>()))
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap) {
   using SM = MmaSmem<KVDT, NQT, HG, S>;
   constexpr bool kBF16 = (KVDT == SCKV_DTYPE_BF16);
@@ -521,7 +528,10 @@ int launch_decode_mma(const sckv_pool* pool, int G, const DecodeParams& prm, cud
     case SCKV_DTYPE_FP8_E4M3:
       // the page's 2*H scales travel as one bulk copy: needs H even (and <= 32)
       if (H > 32 || H % 2 != 0) return SCKV_ERR_UNSUPPORTED;
-      return (H % 4 == 0) ? launch_mma_nq<SCKV_DTYPE_FP8_E4M3, 4, 5>(pool, G, prm, stream)
+      // 4 heads per stage: three CTAs of 3 stages per SM keep as many bytes in
+      // flight as two of 5 and hide the MMA / convert latencies better
+      // (Qwen3 FP8: 0.791 -> 0.746 ms per layer launch)
+      return (H % 4 == 0) ? launch_mma_nq<SCKV_DTYPE_FP8_E4M3, 4, 3>(pool, G, prm, stream)
                           : launch_mma_nq<SCKV_DTYPE_FP8_E4M3, 2, 10>(pool, G, prm, stream);
     default:
       return SCKV_ERR_UNSUPPORTED;
