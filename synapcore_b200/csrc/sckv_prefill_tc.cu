@@ -5,30 +5,31 @@
 // 1209-1229, causal mask :1218-1224, query t of a sequence at position
 // start + t sees keys 0..start + t), for f16 and bf16 pools.
 //
-// Work item = (sequence, tile of 128 query rows, kv head). The rows are
-// (token, q head) pairs of the G heads that read the kv head, so a tile holds
-// 128 / G tokens. Persistent CTAs (two per SM) claim items from a counter;
-// 7 warps per CTA:
-//   warp 0     claims items, loads the item's Q (one TMA box per 64-dim half
-//              when q has the pool's type, else the softmax warps write it)
-//              and streams K: 4 pages (64 keys) per tile, one 2 KiB box per
-//              (page, 64-dim half), 128-byte swizzle, into a 2-slot ring laid
-//              out as the UMMA K-major canonical tile (consecutive pages are
-//              consecutive rows).
-//   warp 6     streams V the same way into its own 2-slot ring (one TMA issue
-//              holds its warp ~0.1 us, so K and V get a warp each).
-//   warp 1     allocates 256 tensor-memory columns and issues the MMAs:
-//                S[b] (128 x 64 fp32)  = Q . K^T        8 x tcgen05.mma (K = 16)
-//                O    (128 x 128 fp32) += P[b] . V      4 x tcgen05.mma (A from TMEM)
-//              S double-buffered, so S(j+1) runs while the softmax works on
-//              S(j); K(j) is released when S(j) finishes, V(j) after PV(j).
-//              Completion is signalled with tcgen05.commit on mbarriers.
-//   warps 2-5  softmax: thread i owns query row i (TMEM lane i): loads its 64
-//              scores with tcgen05.ld, masks (only tiles the causal limit cuts),
-//              keeps a stale running max (moves only by more than 2^8,
-//              rescaling O in TMEM when it does), writes P = 2^(s*scale - m)
-//              as f16 / bf16 back over S (tcgen05.st), and at the end of the
-//              item normalises its O row and stores it.
+// Work item = (sequence, two tiles of 128 query rows, kv head). The rows
+// are (token, q head) pairs of the G heads that read the kv head, so a tile
+// holds 128 / G tokens; both tiles share every K/V tile loaded. One
+// persistent CTA per SM (512 TMEM columns) claims items from a counter;
+// 16 warps:
+//   warps 0, 3  claim items (warp 0), load the item's Q (one TMA box per
+//              64-dim half and tile when q has the pool's type, else the
+//              softmax warps write it) and stream K: 4 pages (64 keys) per
+//              tile, one 2 KiB box per (page, 64-dim half), 128-byte swizzle,
+//              into a 3-slot ring laid out as the UMMA K-major canonical tile
+//              (consecutive pages are consecutive rows); each warp copies two
+//              pages of a tile (one TMA issue holds its warp ~0.1 us).
+//   warps 2, 12 stream V the same way into their own ring.
+//   warp 1     allocates the tensor memory and issues the MMAs:
+//                S[w][b] (128 x 64 fp32) = Q[w] . K^T   8 x tcgen05.mma (K = 16)
+//                O[w]    (128 x 128 fp32) += P[w][b] . V  4 x tcgen05.mma (A from TMEM)
+//              for both Q tiles w, S double-buffered; K(j) is released when
+//              both S(j) finished, V(j) after both PV(j). Completion is
+//              signalled with tcgen05.commit on mbarriers.
+//   warps 4-7, 8-11  softmax of Q tile 0, 1: thread i owns query row i (TMEM
+//              lane i): loads its 64 scores with tcgen05.ld, masks (only tiles
+//              the causal limit cuts), keeps a stale running max (moves only
+//              by more than 2^8, rescaling O in TMEM when it does), writes
+//              P = 2^(s*scale - m) as f16 / bf16 back over S (tcgen05.st), and
+//              at the end of the item normalises its O row and stores it.
 // bf16 pools split P into bf16 hi + lo parts (two PV products) so P's
 // rounding stays below 2^-16 relative; f16 pools use P in f16.
 // Slots past the sequence's last token (they may hold anything) are zeroed
@@ -44,30 +45,37 @@ using namespace sckv_mma;
 namespace {
 
 constexpr int kHDim = 128;
-constexpr int kRowsTc = 128;                  // query rows per item (UMMA M)
-constexpr int kKeysTc = 64;                   // keys per tile (4 pages)
+constexpr int kRowsTc = 128;                  // query rows per Q tile (UMMA M)
+constexpr int kQTiles = 2;                    // Q tiles per item, sharing every K/V tile
+constexpr int kKeysTc = 64;                   // keys per K/V tile (4 pages)
 constexpr int kPagesTc = kKeysTc / SCKV_PAGE_TOKENS;
-constexpr int kStagesTc = 2;
-constexpr int kThreadsTc = 224;  // warp 0 K / Q copies, 1 MMA, 2-5 softmax, 6 V copies
-constexpr int kSoftmaxThreads = 128;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0;                 // S[b] at columns 64 b
-constexpr uint32_t kColO = 128;
+constexpr int kStagesTc = 3;
+constexpr int kThreadsTc = 512;  // 16 warps, roles below
+constexpr int kSoftmaxThreads = 128;  // per softmax warpgroup (one per Q tile)
+constexpr uint32_t kTmemCols = 512;
+// TMEM columns: S[w][b] at 64 (2 w + b), O[w] at 256 + 128 w
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColO = 256;
 
-constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of Q: 16 KiB
+// warps: 0 claims items, loads Q and half of each K tile; 3 the other half
+// of K; 2 and 12 the two halves of V; 1 issues the MMAs; 4-7 and 8-11 are
+// the softmax warpgroups of Q tiles 0 and 1; 13-15 idle
+constexpr int kWarpK0 = 0, kWarpMma = 1, kWarpV0 = 2, kWarpK1 = 3, kWarpV1 = 12;
+
+constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of a Q tile: 16 KiB
+constexpr int kQTileBytes = 2 * kQHalf;
 constexpr int kTileHalf = kKeysTc * 128;      // one 64-dim half of a K or V tile: 8 KiB
 constexpr int kSlotBytes = 2 * kTileHalf;     // a K (or V) tile: lo and hi halves
-constexpr int kOffK = 2 * kQHalf;             // K ring [kStagesTc]
+constexpr int kOffK = kQTiles * kQTileBytes;  // K ring [kStagesTc]
 constexpr int kOffV = kOffK + kStagesTc * kSlotBytes;  // V ring [kStagesTc]
 constexpr int kOffBar = kOffV + kStagesTc * kSlotBytes;
-constexpr int kNumBars = 22;
+constexpr int kNumBars = 40;
 constexpr int kOffItemRing = kOffBar + kNumBars * 8;  // int[4]
 constexpr int kOffTmemSlot = kOffItemRing + 16;
 constexpr int kOffAbort = kOffTmemSlot + 4;
 constexpr int kOffPartial = kOffTmemSlot + 16;
 constexpr int kOffTileCum = kOffPartial + kThreadsTc * 4;
 constexpr int kFixedSmem = 1024 + kOffTileCum;  // + 4 * (n_seqs + 1)
-
 
 struct TcParams {
   const void* q;
@@ -213,9 +221,12 @@ __device__ __forceinline__ uint4 load_q8(const void* q, int64_t idx, int dtype) 
   return r;
 }
 
-// One work item's geometry, derived identically by every role.
+// One work item's geometry, derived identically by every role. An item is
+// (sequence, pair of 128-row Q tiles, kv head); Q tile w holds tokens
+// tok0 + w BQ .. tok0 + (w + 1) BQ - 1.
 struct TcItem {
-  int seq, h, s0, T, tok0, key_last, jlast, n_tiles, ctx_total, vlim, q_base;
+  int seq, h, s0, T, tok0, n_k, jlast, vlim, q_base;
+  int n_w[kQTiles];  // K tiles Q tile w needs (0: the tile holds no token)
 };
 
 __device__ __forceinline__ TcItem tc_item(const TcParams& p, const int* tile_cum, int total_tiles, int item, int BQ) {
@@ -228,15 +239,23 @@ __device__ __forceinline__ TcItem tc_item(const TcParams& p, const int* tile_cum
     if (tile_cum[mid] <= gt) lo = mid; else hi = mid - 1;
   }
   it.seq = lo;
-  const int tile = gt - tile_cum[lo];
+  const int pair = gt - tile_cum[lo];
   it.T = tc_seq_tokens(p, it.seq, &it.s0, false);
-  it.tok0 = tile * BQ;
-  const int tok_last = min(it.T, it.tok0 + BQ) - 1;
-  it.key_last = it.s0 + tok_last;                      // last key any row of the item sees
-  it.jlast = it.key_last / SCKV_PAGE_TOKENS;            // last page
-  it.n_tiles = it.key_last / kKeysTc + 1;
-  it.ctx_total = it.s0 + it.T;
-  it.vlim = min(it.ctx_total, (it.jlast + 1) * SCKV_PAGE_TOKENS);  // V rows at or past this key get zeroed
+  it.tok0 = pair * kQTiles * BQ;
+  int key_last = 0;
+#pragma unroll
+  for (int w = 0; w < kQTiles; ++w) {
+    const int t_lo = it.tok0 + w * BQ;
+    if (t_lo < it.T) {
+      key_last = it.s0 + min(it.T, t_lo + BQ) - 1;  // last key a row of this tile sees
+      it.n_w[w] = key_last / kKeysTc + 1;
+    } else {
+      it.n_w[w] = 0;
+    }
+  }
+  it.n_k = it.n_w[0] > it.n_w[1] ? it.n_w[0] : it.n_w[1];
+  it.jlast = key_last / SCKV_PAGE_TOKENS;  // last page of the item (the last live tile's)
+  it.vlim = min(it.s0 + it.T, (it.jlast + 1) * SCKV_PAGE_TOKENS);  // V rows at or past this key get zeroed
   it.q_base = __ldg(p.cu_q + it.seq);
   return it;
 }
@@ -251,42 +270,41 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Persistent: each CTA claims items from a counter in the pool's control
-// words (heaviest-first order within each sequence) until they run out.
-// Tiles of all its items are numbered by one running counter g, which fixes
-// every barrier's phase (stage g % 2, S / P buffer g & 1). Calls on one pool
-// must not overlap on the GPU (they share the counter).
+// Persistent, one CTA per SM: each CTA claims items from a counter in the
+// pool's control words (heaviest-first order within each sequence) until
+// they run out. K/V tiles of all its items are numbered by one running
+// counter (ring slot g % 3), and each softmax warpgroup numbers its own S
+// tiles by another (S / P buffer g & 1), which fixes every barrier's phase.
+// Calls on one pool must not overlap on the GPU (they share the counter).
 template <bool kBF16>
-__global__ void __launch_bounds__(kThreadsTc, 2)
+__global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap,
                       const __grid_constant__ CUtensorMap qmap) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
-  // K and V have rings of their own: K(g) is released as soon as S(g) is
-  // done, so K(g + 2) streams in while the softmax still works on tile g.
-  uint64_t* k_full = bars + 14;    // [2] K tile landed (TMA)
-  uint64_t* k_empty = bars + 16;   // [2] S finished with the K slot (commit)
-  uint64_t* v_full = bars + 18;    // [2] V tile landed (TMA)
-  uint64_t* v_empty = bars + 20;   // [2] PV finished with the V slot (commit)
-  uint64_t* s_full = bars + 0;     // [2] S(g) in TMEM (commit)
-  uint64_t* p_full = bars + 2;     // [2] P(g) in TMEM (128 softmax threads)
-  // [2] PV(g) finished (commit to pv_done[g & 1]). A softmax thread waits for
-  // PV(g) only after S(g) landed (or, for a rescale, S(g + 1)), and that
-  // commit covers every MMA issued before it, PV(g - 2) included; PV(g + 2)
-  // cannot start before this thread writes P(g + 2). So the barrier is at
-  // PV(g)'s phase or one past it and the parity wait is unambiguous however
-  // rarely the thread waits on it.
-  uint64_t* pv_done = bars + 4;
-  uint64_t* q_full = bars + 6;    // Q of the item in shared memory (TMA, or 128 softmax threads)
-  uint64_t* q_empty = bars + 7;   // every S of the item finished (commit): Q may be replaced
-  uint64_t* o_empty = bars + 8;   // the item's O was read out (128 softmax threads)
-  uint64_t* mma_done = bars + 9;  // every issued MMA finished (drain)
-  // [4] item k's index is in item_ring[k & 3] (producer). The producer runs
-  // at most two items ahead of the softmax warps (its Q load for item k + 1
-  // waits for all S of item k, and S of item k past its second tile waits
-  // for the softmax of item k), so a slot is never rewritten while unread.
-  uint64_t* item_full = bars + 10;
+  uint64_t* k_full = bars + 0;     // [3] K tile landed (two producer warps' TMA)
+  uint64_t* k_empty = bars + 3;    // [3] every S product of the K tile finished (commit)
+  uint64_t* v_full = bars + 6;     // [3] V tile landed
+  uint64_t* v_empty = bars + 9;    // [3] every PV product of the V tile finished (commit)
+  uint64_t* s_full = bars + 12;    // [w][2] S of warpgroup w's tile in TMEM (commit)
+  uint64_t* p_full = bars + 16;    // [w][2] P of warpgroup w's tile in TMEM (128 threads)
+  // [w][2] PV of warpgroup w's tile g finished (commit to pv_done[w][g & 1]).
+  // A softmax thread waits for PV(g) only after S(g) (epilogue) or S(g + 1)
+  // (O rescale) landed; that commit covers every MMA issued before it,
+  // PV(g - 2) included, and PV(g + 2) cannot start before this thread writes
+  // P(g + 2). So the barrier is at PV(g)'s phase or one past it and the
+  // parity wait is unambiguous however rarely the thread waits on it.
+  uint64_t* pv_done = bars + 20;
+  uint64_t* o_empty = bars + 24;   // [w] warpgroup w's O was read out (128 threads)
+  uint64_t* q_full = bars + 26;    // Q of the item in shared memory (TMA, or 256 softmax threads)
+  uint64_t* q_empty = bars + 27;   // every S of the item finished (commit): Q may be replaced
+  uint64_t* mma_done = bars + 28;  // every issued MMA finished (drain)
+  // [4] item k's index is in item_ring[k & 3] (warp 0). The producers run at
+  // most two items ahead of the softmax warps (Q of item k + 1 waits for all
+  // S of item k, and S of item k past its second tile waits for the softmax
+  // of item k), so a slot is never rewritten while unread.
+  uint64_t* item_full = bars + 29;
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + kOffItemRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + kOffAbort);
@@ -296,9 +314,10 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = 1 << p.lg_g;
-  const int BQ = kRowsTc >> p.lg_g;  // tokens per item
+  const int BQ = kRowsTc >> p.lg_g;  // tokens per Q tile
+  const int BQ2 = kQTiles * BQ;      // tokens per item
 
-  // ---- tiles per sequence, prefix-summed by the whole CTA
+  // ---- Q-tile pairs per sequence, prefix-summed by the whole CTA
   {
     const int per = (p.n_seqs + kThreadsTc - 1) / kThreadsTc;
     const int s0 = threadIdx.x * per, s1 = min(p.n_seqs, s0 + per);
@@ -306,15 +325,19 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
     for (int s = s0; s < s1; ++s) {
       int st;
       const int T = tc_seq_tokens(p, s, &st, blockIdx.x == 0);
-      local += (T + BQ - 1) / BQ;
+      local += (T + BQ2 - 1) / BQ2;
     }
     partial[threadIdx.x] = local;
     if (threadIdx.x == 0) {
       for (int i = 0; i < kNumBars; ++i) {
         uint64_t* bar = &bars[i];
-        const bool by_softmax = bar == &p_full[0] || bar == &p_full[1] || bar == o_empty ||
-                                (bar == q_full && !p.q_tma);
-        mbar_init(bar, by_softmax ? kSoftmaxThreads : 1);
+        uint32_t count = 1;
+        if (bar >= k_full && bar < k_full + kStagesTc) count = 2;   // two K producer warps
+        if (bar >= v_full && bar < v_full + kStagesTc) count = 2;   // two V producer warps
+        if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads;
+        if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads;
+        if (bar == q_full && !p.q_tma) count = kQTiles * kSoftmaxThreads;
+        mbar_init(bar, count);
       }
       *abort_flag = 0;
       fence_mbar_init();
@@ -334,7 +357,7 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
     for (int s = s0; s < s1; ++s) {
       int st;
       const int T = tc_seq_tokens(p, s, &st, false);
-      run += (T + BQ - 1) / BQ;
+      run += (T + BQ2 - 1) / BQ2;
       tile_cum[s + 1] = run;
     }
     __syncthreads();
@@ -342,7 +365,7 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
   const int total_tiles = tile_cum[p.n_seqs];
   const int n_items = total_tiles * p.hkv;
 
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -353,21 +376,25 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 6) {
+  if (warp == kWarpK0 || warp == kWarpK1 || warp == kWarpV0 || warp == kWarpV1) {
     // ------------------------------------------------------------ producers
-    // warp 0 claims items and streams Q and the K ring, warp 6 streams the
-    // V ring: two issuing warps, because one TMA issue holds its warp ~0.1 us
+    // one TMA issue holds its warp ~0.1 us, so K and V each get two warps,
+    // each copying two of a tile's four pages
     if (lane == 0) {
-      const int kv = warp == 6 ? 1 : 0;
+      const int kv = (warp == kWarpV0 || warp == kWarpV1) ? 1 : 0;
+      const int part = (warp == kWarpK1 || warp == kWarpV1) ? 1 : 0;  // pages 2 part, 2 part + 1
+      const bool leader = warp == kWarpK0;
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-      if (kv == 0 && p.q_tma)
+      if (leader && p.q_tma)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&qmap)) : "memory");
       const int64_t layer_base = (int64_t)p.layer * p.max_pages;
-      int g = 0, q_issued = 0, issued = 0;
+      uint64_t* fulls = kv ? v_full : k_full;
+      uint64_t* empties = kv ? v_empty : k_empty;
+      int g = 0, q_issued = 0;
       bool aborted = false;
       for (int k = 0;; ++k) {
         int item;
-        if (kv == 0) {
+        if (leader) {
           // claim the next item; an index >= n_items tells every role to stop
           item = aborted ? n_items : (int)min((unsigned long long)n_items, atomicAdd(p.next_item, 1ULL));
           item_ring[k & 3] = item;
@@ -381,94 +408,88 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
         }
         if (item >= n_items) break;
         const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
-        if (kv == 0 && p.q_tma) {
-          if (k > 0 &&
-              (*abort_flag || !mbar_wait_bounded(q_empty, (k - 1) & 1, SCKV_WAIT_LIMIT_NS))) {
+        if (leader && p.q_tma) {
+          if (k > 0 && (*abort_flag || !mbar_wait_bounded(q_empty, (k - 1) & 1, SCKV_WAIT_LIMIT_NS))) {
             aborted = true;
             continue;  // publishes the stop marker next
           }
-          mbar_arrive_expect_tx(q_full, 2u * kQHalf);
-          tma_load_3d(smem_u32(base), &qmap, 0, it.h * G, it.q_base + it.tok0, q_full);
-          tma_load_3d(smem_u32(base + kQHalf), &qmap, 64, it.h * G, it.q_base + it.tok0, q_full);
+          const int live = it.n_w[1] > 0 ? 2 : 1;
+          mbar_arrive_expect_tx(q_full, (uint32_t)live * 2u * kQHalf);
+          for (int w = 0; w < live; ++w) {
+            const int tok = it.q_base + it.tok0 + w * BQ;
+            tma_load_3d(smem_u32(base + w * kQTileBytes), &qmap, 0, it.h * G, tok, q_full);
+            tma_load_3d(smem_u32(base + w * kQTileBytes + kQHalf), &qmap, 64, it.h * G, tok, q_full);
+          }
           ++q_issued;
         }
         const int32_t* bt_row = p.block_table + (int64_t)it.seq * p.bt_stride;
-        // page ids of local tile j, fetched one tile ahead so their load
-        // latency overlaps the copies being issued (a TMA issue orders
-        // everything before it)
-        auto fetch_ids = [&](int j, int (&ids)[kPagesTc]) {
+        // this warp's two page ids of local tile j, fetched one tile ahead
+        // so their load latency overlaps the copies being issued
+        auto fetch_ids = [&](int j, int (&ids)[2]) {
 #pragma unroll
-          for (int pg = 0; pg < kPagesTc; ++pg) {
-            const int blk = j * kPagesTc + pg;
-            ids[pg] = blk <= it.jlast ? __ldg(bt_row + blk) : 0;
+          for (int i = 0; i < 2; ++i) {
+            const int blk = j * kPagesTc + 2 * part + i;
+            ids[i] = blk <= it.jlast ? __ldg(bt_row + blk) : 0;
           }
         };
-        int ids_next[kPagesTc], ids_cur[kPagesTc];
+        int ids_next[2], ids_cur[2];
         fetch_ids(0, ids_next);
-        for (int j = 0; j < it.n_tiles; ++j) {
-#pragma unroll
-          for (int pg = 0; pg < kPagesTc; ++pg) ids_cur[pg] = ids_next[pg];
-          if (j + 1 < it.n_tiles) fetch_ids(j + 1, ids_next);
-          // K(g) waits only for S(g - 2) to finish, V(g) for PV(g - 2)
+        for (int j = 0; j < it.n_k; ++j) {
+          ids_cur[0] = ids_next[0];
+          ids_cur[1] = ids_next[1];
+          if (j + 1 < it.n_k) fetch_ids(j + 1, ids_next);
           const int gt = g + j;
           const int st = gt % kStagesTc;
-          uint64_t* full = kv ? &v_full[st] : &k_full[st];
-          uint64_t* empty = kv ? &v_empty[st] : &k_empty[st];
           if (gt >= kStagesTc &&
-              (*abort_flag || !mbar_wait_bounded(empty, ((gt / kStagesTc) - 1) & 1, SCKV_WAIT_LIMIT_NS))) {
+              (*abort_flag ||
+               !mbar_wait_bounded(&empties[st], ((gt / kStagesTc) - 1) & 1, SCKV_WAIT_LIMIT_NS))) {
             aborted = true;
             break;
           }
-          const int np = min(kPagesTc, it.jlast + 1 - j * kPagesTc);
+          // pages of the tile this warp copies (the last tile may have fewer)
+          const int first = j * kPagesTc + 2 * part;
+          const int np = max(0, min(2, it.jlast + 1 - first));
           const uint32_t slot = smem_u32(base + (kv ? kOffV : kOffK) + st * kSlotBytes);
-          mbar_arrive_expect_tx(full, (uint32_t)np * 2u * 2048u);
-          for (int pg = 0; pg < np; ++pg) {
-            int32_t page = ids_cur[pg];
+          mbar_arrive_expect_tx(&fulls[st], (uint32_t)np * 2u * 2048u);
+          for (int i = 0; i < np; ++i) {
+            int32_t page = ids_cur[i];
             if (page < 0 || page >= p.max_pages) {
               sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_PREFILL);
               page = 0;
             }
             const int slab = (int)(layer_base + page);
-            tma_load_5d(slot + pg * 2048, &tmap, 0, 0, it.h, kv, slab, full);
-            tma_load_5d(slot + kTileHalf + pg * 2048, &tmap, 64, 0, it.h, kv, slab, full);
+            const int pg = 2 * part + i;
+            tma_load_5d(slot + pg * 2048, &tmap, 0, 0, it.h, kv, slab, &fulls[st]);
+            tma_load_5d(slot + kTileHalf + pg * 2048, &tmap, 64, 0, it.h, kv, slab, &fulls[st]);
           }
-          ++issued;
         }
-        g += it.n_tiles;
-        if (kv == 1 && aborted) break;
+        if (aborted && !leader) break;
+        g += it.n_k;
       }
       if (aborted) {
         if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
         *abort_flag = 1;
       }
       // nothing of ours may still be landing when the CTA retires
-      uint64_t* fulls = kv ? v_full : k_full;
-      for (int t = issued > kStagesTc ? issued - kStagesTc : 0; t < issued; ++t)
+      for (int t = g > kStagesTc ? g - kStagesTc : 0; t < g; ++t)
         mbar_wait_bounded(&fulls[t % kStagesTc], (t / kStagesTc) & 1, SCKV_WAIT_LIMIT_NS);
       if (q_issued > 0) mbar_wait_bounded(q_full, (q_issued - 1) & 1, SCKV_WAIT_LIMIT_NS);
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t kIdescS = instr_desc_f16(kBF16, kKeysTc, false);
     constexpr uint32_t kIdescPV = instr_desc_f16(kBF16, kHDim, true);
-    const uint32_t q_smem = smem_u32(base);
     bool ok = true;
-    int g = 0, k = 0;
-    // PV of global tile gi = local tile li of item k: O (+)= P . V
-    auto issue_pv = [&](const TcItem& it, int gi, int li) -> bool {
-      const int b = gi & 1;
+    int gk = 0;                     // K/V tiles issued
+    int gs[kQTiles] = {0, 0};       // S tiles issued per warpgroup
+    int items_w[kQTiles] = {0, 0};  // items with a live Q tile w so far
+    // PV of local K/V tile i (global gi): O[w] (+)= P[w] . V for each live Q tile
+    auto issue_pv = [&](const TcItem& it, int gi, int i, const int (&gw0)[kQTiles]) -> bool {
       const int st = gi % kStagesTc;
-      if (!warp_wait(&p_full[b], (gi >> 1) & 1)) return false;
-      tc_fence_after();
-      if (li == 0 && k > 0) {
-        // O still holds the previous item until its epilogue has read it
-        if (!warp_wait(o_empty, (k - 1) & 1)) return false;
-        tc_fence_after();
-      }
       if (!warp_wait(&v_full[st], (gi / kStagesTc) & 1)) return false;
       tc_fence_after();
       uint8_t* vslot = base + kOffV + st * kSlotBytes;
-      const int key0 = li * kKeysTc;
+      const int key0 = i * kKeysTc;
       if (key0 + kKeysTc > it.vlim) {
         // zero the V rows of keys >= vlim (both 64-dim halves): their slots
         // were never written or hold an older tile
@@ -482,24 +503,40 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      if (lane == 0) {
-        const uint32_t v_smem = smem_u32(vslot);
+      const uint32_t v_smem = smem_u32(vslot);
 #pragma unroll
-        for (int pg = 0; pg < kPagesTc; ++pg) {
-          // B = V rows of page pg: N = 128 dims in two 64-dim halves (LBO),
-          // K = 16 keys in two groups of 8 rows (SBO)
-          const uint64_t bdesc = smem_desc_sw128(v_smem + pg * 2048, kTileHalf, 1024);
-          const uint32_t a_col = tmem + kColS + (uint32_t)(b * kKeysTc) + (uint32_t)(pg * 8);
-          umma_ts(tmem + kColO, a_col, bdesc, kIdescPV, (li > 0 || pg > 0) ? 1u : 0u);
-          if (kBF16) umma_ts(tmem + kColO, a_col + 32, bdesc, kIdescPV, 1u);
+      for (int w = 0; w < kQTiles; ++w) {
+        if (i >= it.n_w[w]) continue;
+        const int gw = gw0[w] + i;
+        const int b = gw & 1;
+        if (!warp_wait(&p_full[w * 2 + b], (gw >> 1) & 1)) return false;
+        tc_fence_after();
+        if (i == 0 && items_w[w] > 0) {
+          // O[w] still holds this warpgroup's previous item until its
+          // epilogue has read it
+          if (!warp_wait(&o_empty[w], (items_w[w] - 1) & 1)) return false;
+          tc_fence_after();
         }
-        umma_commit(&v_empty[st]);
-        umma_commit(&pv_done[b]);
+        if (lane == 0) {
+          const uint32_t s_col = tmem + kColS + (uint32_t)((2 * w + b) * kKeysTc);
+          const uint32_t o_col = tmem + kColO + (uint32_t)(w * kHDim);
+#pragma unroll
+          for (int pg = 0; pg < kPagesTc; ++pg) {
+            // B = V rows of page pg: N = 128 dims in two 64-dim halves (LBO),
+            // K = 16 keys in two groups of 8 rows (SBO)
+            const uint64_t bdesc = smem_desc_sw128(v_smem + pg * 2048, kTileHalf, 1024);
+            umma_ts(o_col, s_col + (uint32_t)(pg * 8), bdesc, kIdescPV, (i > 0 || pg > 0) ? 1u : 0u);
+            if (kBF16) umma_ts(o_col, s_col + (uint32_t)(pg * 8 + 32), bdesc, kIdescPV, 1u);
+          }
+          umma_commit(&pv_done[w * 2 + b]);
+        }
+        __syncwarp();
       }
+      if (lane == 0) umma_commit(&v_empty[st]);
       __syncwarp();
       return true;
     };
-    for (; ok; ++k) {
+    for (int k = 0; ok; ++k) {
       if (*abort_flag || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
         ok = false;
         break;
@@ -512,10 +549,10 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
         break;
       }
       tc_fence_after();
-      for (int j = 0; j < it.n_tiles; ++j) {
-        const int gj = g + j;
+      const int gw0[kQTiles] = {gs[0], gs[1]};
+      for (int j = 0; j < it.n_k; ++j) {
+        const int gj = gk + j;
         const int st = gj % kStagesTc;
-        const int b = gj & 1;
         if (*abort_flag || !warp_wait(&k_full[st], (gj / kStagesTc) & 1)) {
           ok = false;
           break;
@@ -524,27 +561,38 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
         if (lane == 0) {
           const uint32_t k_smem = smem_u32(base + kOffK + st * kSlotBytes);
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const int half = ks >> 2, kk = ks & 3;
-            const uint64_t adesc = smem_desc_sw128(q_smem + half * kQHalf + kk * 32, 16, 1024);
-            const uint64_t bdesc = smem_desc_sw128(k_smem + half * kTileHalf + kk * 32, 16, 1024);
-            umma_ss(tmem + kColS + (uint32_t)(b * kKeysTc), adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
+          for (int w = 0; w < kQTiles; ++w) {
+            if (j >= it.n_w[w]) continue;
+            const int b = (gw0[w] + j) & 1;
+            const uint32_t q_smem = smem_u32(base + w * kQTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const int half = ks >> 2, kk = ks & 3;
+              const uint64_t adesc = smem_desc_sw128(q_smem + half * kQHalf + kk * 32, 16, 1024);
+              const uint64_t bdesc = smem_desc_sw128(k_smem + half * kTileHalf + kk * 32, 16, 1024);
+              umma_ss(tmem + kColS + (uint32_t)((2 * w + b) * kKeysTc), adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[w * 2 + b]);
           }
           umma_commit(&k_empty[st]);
-          umma_commit(&s_full[b]);
-          if (j == it.n_tiles - 1) umma_commit(q_empty);  // Q no longer read once these S are done
+          if (j == it.n_k - 1) umma_commit(q_empty);  // Q no longer read once these S are done
         }
         __syncwarp();
-        if (j >= 1 && !issue_pv(it, gj - 1, j - 1)) {
+        if (j >= 1 && !issue_pv(it, gj - 1, j - 1, gw0)) {
           ok = false;
           break;
         }
       }
-      if (!ok || !issue_pv(it, g + it.n_tiles - 1, it.n_tiles - 1)) {
+      if (!ok || !issue_pv(it, gk + it.n_k - 1, it.n_k - 1, gw0)) {
         ok = false;
         break;
       }
-      g += it.n_tiles;
+      gk += it.n_k;
+#pragma unroll
+      for (int w = 0; w < kQTiles; ++w) {
+        gs[w] += it.n_w[w];
+        if (it.n_w[w] > 0) ++items_w[w];
+      }
     }
     if (!ok) {
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
@@ -554,11 +602,18 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
     if (lane == 0) umma_commit(mma_done);
     __syncwarp();
     warp_wait(mma_done, 0);
-  } else {
+  } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ softmax
-    const int quad = warp & 3;            // TMEM lanes 32 quad .. 32 quad + 31
-    const int row = quad * 32 + lane;     // query row = TMEM lane
+    const int w = (warp - 4) >> 2;       // Q tile of this warpgroup
+    const int quad = warp & 3;           // TMEM lanes 32 quad .. 32 quad + 31
+    const int row = quad * 32 + lane;    // query row = TMEM lane
     const uint32_t t_row = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t col_s = kColS + (uint32_t)(2 * w * kKeysTc);
+    const uint32_t col_o = kColO + (uint32_t)(w * kHDim);
+    uint64_t* my_s_full = s_full + 2 * w;
+    uint64_t* my_p_full = p_full + 2 * w;
+    uint64_t* my_pv_done = pv_done + 2 * w;
+    uint8_t* q_tile = base + w * kQTileBytes;
     bool ok = true;
     int g = 0;
     for (int k = 0; ok; ++k) {
@@ -569,29 +624,32 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
       const int item = item_ring[k & 3];
       if (item >= n_items) break;
       const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
-      const int rtok = it.tok0 + (row >> p.lg_g);
+      const int rtok = it.tok0 + w * BQ + (row >> p.lg_g);
       const int rhead = it.h * G + (row & (G - 1));
       const bool valid = rtok < it.T;
       const int lim = valid ? it.s0 + rtok : -1;  // last key this row sees
+      const int tile_lim = it.s0 + it.tok0 + w * BQ;  // keys up to here are seen by every row of the tile
       if (!p.q_tma) {
         // Q row -> shared memory, 128-byte swizzled K-major (the layout a TMA
-        // copy with SWIZZLE_128B produces). The previous item's S products
-        // are all finished: this thread waited for every one of them.
+        // copy with SWIZZLE_128B produces). This warpgroup's previous S
+        // products are all finished: it waited for every one of them.
         const int64_t qoff = ((int64_t)(it.q_base + rtok) * p.hq + rhead) * kHDim;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const int half = c >> 3, ch = c & 7;
           const uint4 v = valid ? load_q8<kBF16>(p.q, qoff + c * 8, p.q_dtype) : make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(base + half * kQHalf + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(q_tile + half * kQHalf + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
         }
         fence_proxy_async_smem();
         mbar_arrive(q_full);
       }
+      const int n = it.n_w[w];
+      if (n == 0) continue;  // no token of this item falls in this Q tile
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.n_tiles; ++j) {
+      for (int j = 0; j < n; ++j) {
         const int gj = g + j;
         const int b = gj & 1;
-        if (*abort_flag || !warp_wait(&s_full[b], (gj >> 1) & 1)) {
+        if (*abort_flag || !warp_wait(&my_s_full[b], (gj >> 1) & 1)) {
           ok = false;
           break;
         }
@@ -599,8 +657,8 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
         float sv[kKeysTc];
         {
           uint32_t r0[32], r1[32];
-          tmem_ld32(t_row + kColS + b * kKeysTc, r0);
-          tmem_ld32(t_row + kColS + b * kKeysTc + 32, r1);
+          tmem_ld32(t_row + col_s + b * kKeysTc, r0);
+          tmem_ld32(t_row + col_s + b * kKeysTc + 32, r1);
           tc_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -609,10 +667,10 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
           }
         }
         // row max of the raw scores (the scale is positive); tiles every row
-        // of the item sees in full skip the causal mask
+        // of the Q tile sees in full skip the causal mask
         const int key0 = j * kKeysTc;
         float pm = -INFINITY;
-        if (key0 + kKeysTc - 1 <= it.s0 + it.tok0) {
+        if (key0 + kKeysTc - 1 <= tile_lim) {
 #pragma unroll
           for (int c = 0; c < kKeysTc; ++c) pm = fmaxf(pm, sv[c]);
         } else {
@@ -637,9 +695,9 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
           l *= alpha;
         }
         if (__any_sync(0xffffffffu, rescale) && j > 0) {
-          // O holds PV of tiles 0..j-1 of this item: wait for the last, then
+          // O holds PV of tiles 0..j-1 of this Q tile: wait for the last, then
           // scale this warp's rows
-          if (!warp_wait(&pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1)) {
+          if (!warp_wait(&my_pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1)) {
             ok = false;
             break;
           }
@@ -647,11 +705,11 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
 #pragma unroll 1
           for (int cc = 0; cc < 4; ++cc) {
             uint32_t r[32];
-            tmem_ld32(t_row + kColO + cc * 32, r);
+            tmem_ld32(t_row + col_o + cc * 32, r);
             tc_wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * alpha);
-            tmem_st32(t_row + kColO + cc * 32, r);
+            tmem_st32(t_row + col_o + cc * 32, r);
           }
           tc_wait_st();
         }
@@ -670,18 +728,18 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
             ph[c] = pack2<kBF16>(p0, p1);
             if (kBF16) plo[c] = pack2<true>(p0 - round16<true>(p0), p1 - round16<true>(p1));
           }
-          tmem_st32(t_row + kColS + b * kKeysTc, ph);
-          if (kBF16) tmem_st32(t_row + kColS + b * kKeysTc + 32, plo);
+          tmem_st32(t_row + col_s + b * kKeysTc, ph);
+          if (kBF16) tmem_st32(t_row + col_s + b * kKeysTc + 32, plo);
           l += ls0 + ls1;
           tc_wait_st();
         }
         tc_fence_before();
-        mbar_arrive(&p_full[b]);
+        mbar_arrive(&my_p_full[b]);
       }
       if (!ok) break;
-      // ---- epilogue: O / l for this thread's row, once the item's last PV finished
-      const int glast = g + it.n_tiles - 1;
-      if (!warp_wait(&pv_done[glast & 1], (glast >> 1) & 1)) {
+      // ---- epilogue: O / l for this thread's row, once the tile's last PV finished
+      const int glast = g + n - 1;
+      if (!warp_wait(&my_pv_done[glast & 1], (glast >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -691,7 +749,7 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t r[32];
-        tmem_ld32(t_row + kColO + cc * 32, r);
+        tmem_ld32(t_row + col_o + cc * 32, r);
         tc_wait_ld();
         if (valid) {
           if (p.out_dtype == SCKV_DTYPE_F32) {
@@ -706,21 +764,21 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
             uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + obase + cc * 32;
 #pragma unroll
             for (int c = 0; c < 32; c += 8) {
-              uint4 w;
-              uint32_t* wp = &w.x;
+              uint4 wv;
+              uint32_t* wp = &wv.x;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const float a = __uint_as_float(r[c + 2 * kk]) * inv, bb = __uint_as_float(r[c + 2 * kk + 1]) * inv;
                 wp[kk] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
               }
-              *reinterpret_cast<uint4*>(o + c) = w;
+              *reinterpret_cast<uint4*>(o + c) = wv;
             }
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(o_empty);  // O may be overwritten by the next item's PV
-      g += it.n_tiles;
+      mbar_arrive(&o_empty[w]);  // O[w] may be overwritten by the next item's PV
+      g += n;
     }
     if (!ok) {
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
@@ -729,7 +787,7 @@ __global__ void __launch_bounds__(kThreadsTc, 2)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
@@ -743,13 +801,11 @@ int launch_tc(const sckv_pool* pool, const TcParams& prm, int max_items, const C
   int rc = ensure_tmap(pool, 1, mp->tmap_kv2, &mp->tmap2_ready, 1);
   if (rc != SCKV_OK) return rc;
   const int smem = kFixedSmem + 4 * (prm.n_seqs + 1);
+  if (smem > 227 * 1024) return SCKV_ERR_UNSUPPORTED;
   SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   SCKV_CUDA_CHECK(cudaMemsetAsync(prm.next_item, 0, sizeof(unsigned long long), stream));
-  int occ = 0;
-  SCKV_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreadsTc, smem));
-  if (occ < 1) occ = 1;
-  if (occ > 2) occ = 2;  // two CTAs x 256 TMEM columns fill an SM's tensor memory
-  int grid = pool->num_sms * occ;
+  // one CTA per SM: 512 TMEM columns are the whole of an SM's tensor memory
+  int grid = pool->num_sms;
   if (grid > max_items) grid = max_items;
   const CUtensorMap* kv_map = reinterpret_cast<const CUtensorMap*>(pool->tmap_kv2);
   kern<<<grid, kThreadsTc, smem, stream>>>(prm, *kv_map, prm.q_tma ? qmap : *kv_map);
@@ -792,7 +848,8 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.next_item = reinterpret_cast<unsigned long long*>(pool->ctl + CTL_PREFILL_NEXT);
   const int BQ = kRowsTc >> lg_g;
-  const int64_t max_tiles = (int64_t)(n_tokens + BQ - 1) / BQ + n_seqs;  // >= sum of ceil(T_s / BQ)
+  const int BQ2 = kQTiles * BQ;
+  const int64_t max_tiles = (int64_t)(n_tokens + BQ2 - 1) / BQ2 + n_seqs;  // >= sum of ceil(T_s / BQ2)
   const int64_t max_items = max_tiles * pool->num_kv_heads;
   if (max_items > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
   // q in the MMA's element type arrives by TMA: a 3-D view (dim, head,
