@@ -14,7 +14,7 @@
 //              64-dim half and tile when q has the pool's type, else the
 //              softmax warps write it) and stream K: 4 pages (64 keys) per
 //              tile, one 2 KiB box per (page, 64-dim half), 128-byte swizzle,
-//              into a 3-slot ring laid out as the UMMA K-major canonical tile
+//              into a 4-slot ring laid out as the UMMA K-major canonical tile
 //              (consecutive pages are consecutive rows); each warp copies two
 //              pages of a tile (one TMA issue holds its warp ~0.1 us).
 //   warps 2, 12 stream V the same way into their own ring.
@@ -49,7 +49,7 @@ constexpr int kRowsTc = 128;                  // query rows per Q tile (UMMA M)
 constexpr int kQTiles = 2;                    // Q tiles per item, sharing every K/V tile
 constexpr int kKeysTc = 64;                   // keys per K/V tile (4 pages)
 constexpr int kPagesTc = kKeysTc / SCKV_PAGE_TOKENS;
-constexpr int kStagesTc = 3;
+constexpr int kStagesTc = 4;
 constexpr int kThreadsTc = 512;  // 16 warps, roles below
 constexpr int kSoftmaxThreads = 128;  // per softmax warpgroup (one per Q tile)
 constexpr uint32_t kTmemCols = 512;
@@ -69,7 +69,7 @@ constexpr int kSlotBytes = 2 * kTileHalf;     // a K (or V) tile: lo and hi halv
 constexpr int kOffK = kQTiles * kQTileBytes;  // K ring [kStagesTc]
 constexpr int kOffV = kOffK + kStagesTc * kSlotBytes;  // V ring [kStagesTc]
 constexpr int kOffBar = kOffV + kStagesTc * kSlotBytes;
-constexpr int kNumBars = 40;
+constexpr int kNumBars = 4 * kStagesTc + 4 + 4 + 4 + 2 + 3 + 4;
 constexpr int kOffItemRing = kOffBar + kNumBars * 8;  // int[4]
 constexpr int kOffTmemSlot = kOffItemRing + 16;
 constexpr int kOffAbort = kOffTmemSlot + 4;
@@ -273,7 +273,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 // Persistent, one CTA per SM: each CTA claims items from a counter in the
 // pool's control words (heaviest-first order within each sequence) until
 // they run out. K/V tiles of all its items are numbered by one running
-// counter (ring slot g % 3), and each softmax warpgroup numbers its own S
+// counter (ring slot g % 4), and each softmax warpgroup numbers its own S
 // tiles by another (S / P buffer g & 1), which fixes every barrier's phase.
 // Calls on one pool must not overlap on the GPU (they share the counter).
 template <bool kBF16>
@@ -283,28 +283,28 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
-  uint64_t* k_full = bars + 0;     // [3] K tile landed (two producer warps' TMA)
-  uint64_t* k_empty = bars + 3;    // [3] every S product of the K tile finished (commit)
-  uint64_t* v_full = bars + 6;     // [3] V tile landed
-  uint64_t* v_empty = bars + 9;    // [3] every PV product of the V tile finished (commit)
-  uint64_t* s_full = bars + 12;    // [w][2] S of warpgroup w's tile in TMEM (commit)
-  uint64_t* p_full = bars + 16;    // [w][2] P of warpgroup w's tile in TMEM (128 threads)
+  uint64_t* k_full = bars;                      // [S] K tile landed (two producer warps' TMA)
+  uint64_t* k_empty = bars + kStagesTc;         // [S] every S product of the K tile finished (commit)
+  uint64_t* v_full = bars + 2 * kStagesTc;      // [S] V tile landed
+  uint64_t* v_empty = bars + 3 * kStagesTc;     // [S] every PV product of the V tile finished (commit)
+  uint64_t* s_full = bars + 4 * kStagesTc;      // [w][2] S of warpgroup w's tile in TMEM (commit)
+  uint64_t* p_full = s_full + 4;                // [w][2] P of warpgroup w's tile in TMEM (128 threads)
   // [w][2] PV of warpgroup w's tile g finished (commit to pv_done[w][g & 1]).
   // A softmax thread waits for PV(g) only after S(g) (epilogue) or S(g + 1)
   // (O rescale) landed; that commit covers every MMA issued before it,
   // PV(g - 2) included, and PV(g + 2) cannot start before this thread writes
   // P(g + 2). So the barrier is at PV(g)'s phase or one past it and the
   // parity wait is unambiguous however rarely the thread waits on it.
-  uint64_t* pv_done = bars + 20;
-  uint64_t* o_empty = bars + 24;   // [w] warpgroup w's O was read out (128 threads)
-  uint64_t* q_full = bars + 26;    // Q of the item in shared memory (TMA, or 256 softmax threads)
-  uint64_t* q_empty = bars + 27;   // every S of the item finished (commit): Q may be replaced
-  uint64_t* mma_done = bars + 28;  // every issued MMA finished (drain)
+  uint64_t* pv_done = p_full + 4;
+  uint64_t* o_empty = pv_done + 4;              // [w] warpgroup w's O was read out (128 threads)
+  uint64_t* q_full = o_empty + 2;               // Q of the item in shared memory (TMA, or 256 softmax threads)
+  uint64_t* q_empty = q_full + 1;               // every S of the item finished (commit): Q may be replaced
+  uint64_t* mma_done = q_full + 2;              // every issued MMA finished (drain)
   // [4] item k's index is in item_ring[k & 3] (warp 0). The producers run at
   // most two items ahead of the softmax warps (Q of item k + 1 waits for all
   // S of item k, and S of item k past its second tile waits for the softmax
   // of item k), so a slot is never rewritten while unread.
-  uint64_t* item_full = bars + 29;
+  uint64_t* item_full = q_full + 3;
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + kOffItemRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + kOffAbort);
