@@ -545,6 +545,9 @@ class MixState:
 
     def __init__(self, w, rank: int, max_steps: int):
         from synapcore_b200.paged_cache import PagedKVCache
+        from synapcore_b200.pool import to_device
+
+        self.to_device = to_device
 
         self.w = w
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -667,7 +670,7 @@ class MixState:
         pv = self.pre_v[:L * tot * hkv * d].view(L, tot, hkv, d)
         pq = self.pre_q[:L * tot * hq * d].view(L, tot, hq, d)
         c.append_prefill_batch(new_ids, pk, pv, cu.tolist())
-        meta = torch.tensor(np.concatenate([cu, starts]).astype(np.int32)).to(self.dev, non_blocking=True)
+        meta = self.to_device(np.concatenate([cu, starts]).astype(np.int32), torch.int32, self.dev)
         cu_d, st_d = meta[:len(T) + 1], meta[len(T) + 1:]
         for l in range(L):
             if timing is not None:

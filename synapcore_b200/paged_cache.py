@@ -22,7 +22,7 @@ from typing import Dict, Hashable, List, Optional, Sequence, Tuple
 import torch
 
 from . import _native as N
-from .pool import KVPool, PAGE_TOKENS
+from .pool import KVPool, PAGE_TOKENS, to_device
 
 
 def _ceil_div(a: int, b: int) -> int:
@@ -180,7 +180,7 @@ class PagedKVCache:
             cols.extend(range(have, need))
         if rows:
             ids, _ = self.pool.alloc_pages(len(rows), pin=True)
-            idx = torch.tensor([rows, cols], dtype=torch.int64).to(self.device, non_blocking=True)
+            idx = to_device([rows, cols], torch.int64, self.device)
             self.block_table[idx[0], idx[1]] = ids
 
     def append_prefill_batch(self, seq_ids: Sequence[Hashable], k: torch.Tensor, v: torch.Tensor,
@@ -199,14 +199,12 @@ class PagedKVCache:
         r0 = self._consecutive_rows(seq_ids)
         T = [cu[i + 1] - cu[i] for i in range(n)]
         self._grow_rows(r0, T)
-        meta = torch.tensor(cu + [self.lengths[r0 + i] for i in range(n)], dtype=torch.int32).to(
-            self.device, non_blocking=True)
+        meta = to_device(cu + [self.lengths[r0 + i] for i in range(n)], torch.int32, self.device)
         self.pool.append(k[:, :cu[-1]], v[:, :cu[-1]], meta[:n + 1], meta[n + 1:], self.block_table[r0:r0 + n],
                          layer0=0, max_blocks=self.max_blocks)
         for i in range(n):
             self.lengths[r0 + i] += T[i]
-        self.ctx_lens[r0:r0 + n].copy_(torch.tensor(self.lengths[r0:r0 + n], dtype=torch.int32),
-                                       non_blocking=True)
+        self.ctx_lens[r0:r0 + n].copy_(to_device(self.lengths[r0:r0 + n], torch.int32, self.device))
 
     def prefill_attention_batch(self, layer: int, seq_ids: Sequence[Hashable], q: torch.Tensor,
                                 cu_q: torch.Tensor, start_pos: torch.Tensor, scale: Optional[float] = None,
@@ -243,8 +241,8 @@ class PagedKVCache:
         <= start+t. q [T, Hq, D] -> [T, Hq, D]."""
         r = self.row_of[seq_id]
         T = q.shape[0]
-        cu = torch.tensor([0, T], dtype=torch.int32, device=self.device)
-        st = torch.tensor([start], dtype=torch.int32, device=self.device)
+        meta = to_device([0, T, start], torch.int32, self.device)
+        cu, st = meta[:2], meta[2:]
         try:
             return self.pool.prefill_attn(layer, q, cu, st, self.block_table[r:r + 1], scale=scale,
                                           out_dtype=out_dtype, max_blocks=self.max_blocks)
@@ -290,7 +288,7 @@ class PagedKVCache:
         n = len(page_ids)
         if n == 0:
             return
-        ids = torch.as_tensor(list(page_ids), dtype=torch.int32).to(self.device)
+        ids = to_device(list(page_ids), torch.int32, self.device)
         self.block_table[r, :n].copy_(ids)
         self.pool.pin_pages(ids, +1)
         self.lengths[r] = n * PAGE_TOKENS

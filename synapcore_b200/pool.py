@@ -75,12 +75,23 @@ def _need(t: torch.Tensor, name: str, device: torch.device, dtype: Optional[torc
         raise ValueError(f"{name} has {t.numel()} elements, needs at least {min_numel}")
 
 
+def to_device(values, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """Host values -> a device tensor through pinned memory, without a stream
+    synchronisation. (A copy from pageable host memory makes CUDA wait for
+    the stream's earlier work before it starts, so the host stops feeding
+    the GPU; the pinned copy is queued behind that work instead and the
+    caching host allocator keeps the buffer alive until it ran.)"""
+    t = values if isinstance(values, torch.Tensor) else torch.as_tensor(values, dtype=dtype)
+    t = t.to(dtype=dtype).contiguous()
+    if t.device.type == "cuda":
+        return t.to(device)
+    return t.pin_memory().to(device, non_blocking=True)
+
+
 def _dev_i32(x, device) -> torch.Tensor:
-    if isinstance(x, torch.Tensor):
-        t = x.to(device=device, dtype=torch.int32)
-    else:
-        t = torch.as_tensor(x, dtype=torch.int32, device=device)
-    return t.contiguous()
+    if isinstance(x, torch.Tensor) and x.device.type == "cuda":
+        return x.to(device=device, dtype=torch.int32).contiguous()
+    return to_device(x, torch.int32, device)
 
 
 class KVPool:

@@ -30,6 +30,7 @@ from typing import Deque, Dict, List, Optional, Protocol, Sequence, Set, TypedDi
 import torch
 
 from .paged_cache import PAGE_TOKENS, PagedKVCache
+from .pool import to_device
 
 
 class PagedDecoderModel(Protocol):
@@ -237,7 +238,7 @@ class ContinuousBatchScheduler:
                 matched = len(pages) * PAGE_TOKENS
                 req.kv_prefix_skipped = matched
         rem = req.prompt_ids[matched:]
-        toks = torch.tensor(rem, dtype=torch.int64, device=self.device)
+        toks = to_device(rem, torch.int64, self.device)
         positions = torch.arange(matched, matched + len(rem), dtype=torch.int64, device=self.device)
 
         def attend(l, q, k, v):
@@ -259,8 +260,8 @@ class ContinuousBatchScheduler:
         B = len(reqs)
         for r, req in enumerate(reqs):
             cache.move_to_row(req.request_id, r)
-        toks = torch.tensor([req.generated_ids[-1] for req in reqs], dtype=torch.int64, device=self.device)
-        positions = torch.tensor([req.pos_offset for req in reqs], dtype=torch.int64, device=self.device)
+        toks = to_device([req.generated_ids[-1] for req in reqs], torch.int64, self.device)
+        positions = to_device([req.pos_offset for req in reqs], torch.int64, self.device)
         cache.decode_reserve(B)
 
         def attend(l, q, k, v):
