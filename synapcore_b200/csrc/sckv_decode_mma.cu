@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
       m[nq][0] = m[nq][1] = -INFINITY;
       l[nq][0] = l[nq][1] = 0.f;
     }
-    float vref = 0.f;  // FP8: reference V scale of this warp's accumulator
+    float vref = 0.f;      // FP8: reference V scale of this warp's accumulator
+    float inv_vref = 0.f;  // 1 / vref (0 while vref is 0)
 
     for (int i = sub; i < n; i += kWPH) {
       const uint32_t gi = gbase + i;
@@ -265,11 +266,12 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         }
 
         // ---------------- online softmax, stale running max: the reference max
-        // moves only when a page's max exceeds it by more than 2^8, so p <= 256
-        // and the accumulator rescale is rare.
+        // moves only when a score exceeds it by more than 2^8, so p <= 256 and
+        // the accumulator rescale is rare. Every lane tests its own scores
+        // against the (column-uniform) reference; the column max over the 8
+        // lanes of a q column is reduced only when some score crossed it.
         const float sscale = p.scale_log2 * kscale;
         float sv[NQT][4];
-        float pmx[NQT][2];
         bool grow = false;
 #pragma unroll
         for (int nq = 0; nq < NQT; ++nq) {
@@ -279,12 +281,7 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
             const float sB = (g + 8 < nv) ? (sc[nq][2 + c] + sc2[nq][2 + c]) * sscale : -INFINITY;
             sv[nq][c] = sA;
             sv[nq][2 + c] = sB;
-            float mx = fmaxf(sA, sB);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            pmx[nq][c] = mx;
-            grow |= (mx > m[nq][c] + 8.f);
+            grow |= (fmaxf(sA, sB) > m[nq][c] + 8.f);
           }
         }
         if (__any_sync(0xffffffffu, grow)) {
@@ -292,7 +289,11 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
           for (int nq = 0; nq < NQT; ++nq) {
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              const float mn = fmaxf(m[nq][c], pmx[nq][c]);
+              float mx = fmaxf(sv[nq][c], sv[nq][2 + c]);
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+              const float mn = fmaxf(m[nq][c], mx);
               const float alpha = (mn == -INFINITY) ? 1.f : exp2f(m[nq][c] - mn);
               m[nq][c] = mn;
               l[nq][c] *= alpha;
@@ -308,8 +309,11 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         // P stays in the normal f16 range; the accumulator is in units of vref.
         float pscale = 1.f;
         if (kFP8) {
-          if (vref == 0.f) vref = vscale;
-          pscale = (vref > 0.f) ? vscale / vref : 0.f;
+          if (vref == 0.f) {
+            vref = vscale;
+            inv_vref = (vscale > 0.f) ? 1.f / vscale : 0.f;
+          }
+          pscale = vscale * inv_vref;
           if (pscale > 64.f) {
             const float rb = vref / vscale;
 #pragma unroll
@@ -319,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
 #pragma unroll
                 for (int c = 0; c < 4; ++c) acc[nq][mi][c] *= rb;
             vref = vscale;
+            inv_vref = 1.f / vscale;
             pscale = 1.f;
           }
         }
@@ -329,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float mref = m[nq][c];
-            pa[c] = (mref == -INFINITY) ? 0.f : exp2f(sv[nq][c] - mref);
-            pbv[c] = (mref == -INFINITY) ? 0.f : exp2f(sv[nq][2 + c] - mref);
+            pa[c] = (mref == -INFINITY) ? 0.f : ex2_approx(sv[nq][c] - mref);
+            pbv[c] = (mref == -INFINITY) ? 0.f : ex2_approx(sv[nq][2 + c] - mref);
             l[nq][c] += pa[c] + pbv[c];
             if (kFP8) {
               pa[c] *= pscale;

@@ -37,16 +37,22 @@ enum SckvCtl : int {
   CTL_CLOCK = 2,      // step clock
   CTL_EVICTIONS = 3,  // evictions (LRU victims + explicit frees)
   CTL_ALLOCATED = 4,  // pages currently allocated
-  CTL_PREFILL_NEXT = 6,  // next work item of the running prefill launch (zeroed before each)
   CTL_WORDS = 8,
 };
 
 // Page states.
 enum SckvPageState : int32_t { PAGE_FREE = 0, PAGE_ALLOCATED = 1 };
 
-// Layout of the allocator region (alloc_state):
+// Work counters for persistent kernels that claim items dynamically: each
+// launch takes the next one round-robin (zeroed on its stream just before
+// the launch), so launches on different streams do not share a counter
+// unless more than SCKV_WORK_COUNTERS of them are in flight at once.
+#define SCKV_WORK_COUNTERS 64
+
+// Layout of the allocator region (alloc_state), each part 256-byte aligned:
 //   int64 ctl[CTL_WORDS]
-//   int32 status[4]  (+ padding to 64 bytes)
+//   int32 status[4]
+//   uint64 work[SCKV_WORK_COUNTERS]
 //   int32 ring[P]
 //   int64 last_used[P]
 //   int32 pin[P]
@@ -65,6 +71,8 @@ struct sckv_pool {
   void* alloc_state;
   int64_t* ctl;
   int32_t* status;
+  unsigned long long* work_counters;
+  mutable unsigned int next_work_counter;  // host-side round-robin index (atomic)
   int32_t* ring;
   int64_t* last_used;
   int32_t* pin;
@@ -84,6 +92,12 @@ struct sckv_pool {
   alignas(64) unsigned char tmap_kv2[128];
   int tmap2_ready;
 };
+
+// Next work counter of the pool for one launch (thread-safe on the host).
+static inline unsigned long long* sckv_take_work_counter(const sckv_pool* p) {
+  const unsigned int i = __atomic_fetch_add(&p->next_work_counter, 1u, __ATOMIC_RELAXED);
+  return p->work_counters + (i % SCKV_WORK_COUNTERS);
+}
 
 static inline int sckv_elem_bytes(int dtype) {
   switch (dtype) {

@@ -84,6 +84,13 @@ __device__ __forceinline__ void cvt_fp8x4(uint32_t x, uint32_t& lo, uint32_t& hi
       : "r"(x));
 }
 
+// 2^x by the hardware approximation (flushes denormals; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if (BF16) {

@@ -10,7 +10,7 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct AllocLayout {
-  size_t ctl, status, ring, last_used, pin, state, total;
+  size_t ctl, status, work, ring, last_used, pin, state, total;
 };
 
 AllocLayout alloc_layout(int64_t P) {
@@ -18,6 +18,7 @@ AllocLayout alloc_layout(int64_t P) {
   size_t off = 0;
   a.ctl = off;       off = align_up(off + CTL_WORDS * sizeof(int64_t));
   a.status = off;    off = align_up(off + 4 * sizeof(int32_t));
+  a.work = off;      off = align_up(off + SCKV_WORK_COUNTERS * sizeof(unsigned long long));
   a.ring = off;      off = align_up(off + static_cast<size_t>(P) * sizeof(int32_t));
   a.last_used = off; off = align_up(off + static_cast<size_t>(P) * sizeof(int64_t));
   a.pin = off;       off = align_up(off + static_cast<size_t>(P) * sizeof(int32_t));
@@ -73,6 +74,7 @@ static int pool_init_common(sckv_pool* p, int L, int H, int D, int T, int64_t P,
   char* base = static_cast<char*>(p->alloc_state);
   p->ctl = reinterpret_cast<int64_t*>(base + a.ctl);
   p->status = reinterpret_cast<int32_t*>(base + a.status);
+  p->work_counters = reinterpret_cast<unsigned long long*>(base + a.work);
   p->ring = reinterpret_cast<int32_t*>(base + a.ring);
   p->last_used = reinterpret_cast<int64_t*>(base + a.last_used);
   p->pin = reinterpret_cast<int32_t*>(base + a.pin);

@@ -170,13 +170,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// 2^x by the hardware approximation (flushes denormals; 2^-inf = 0).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Every lane of the warp waits; the result is the same on all lanes.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   const bool ok = mbar_wait_bounded(bar, parity, SCKV_WAIT_LIMIT_NS);
@@ -846,7 +839,7 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
   prm.q_dtype = q_dtype;
   prm.out_dtype = out_dtype;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.next_item = reinterpret_cast<unsigned long long*>(pool->ctl + CTL_PREFILL_NEXT);
+  prm.next_item = sckv_take_work_counter(pool);
   const int BQ = kRowsTc >> lg_g;
   const int BQ2 = kQTiles * BQ;
   const int64_t max_tiles = (int64_t)(n_tokens + BQ2 - 1) / BQ2 + n_seqs;  // >= sum of ceil(T_s / BQ2)

@@ -239,3 +239,27 @@ def test_tensor_memory_kernel_rescales_and_matches_mma_kernel(cuda_device, kv, h
             err = _rel_err(got[cu[b]:cu[b + 1]], ref[cu[b]:cu[b + 1]])
             assert err <= TOL, (which, b, err)
     assert _rel_err(outs["tc"], outs["mma"]) <= TOL
+
+
+def test_prefill_launches_on_two_streams_share_one_pool(cuda_device):
+    """Each launch claims work items from its own counter: concurrent prefills
+    of one pool on two streams both cover every item."""
+    T = [300, 5, 260, 64, 190]
+    start = [0, 40, 16, 0, 33]
+    pool, ora, bt, cu, st, q = _case(cuda_device, "fp16", 16, 4, T, start, pool_pages=200, layers=2)
+    dev = pool.device
+    q_t = torch.from_numpy(q).to(torch.float16).to(dev)
+    cu_t, st_t, bt_t = (torch.from_numpy(a).to(dev) for a in (cu, st, bt))
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    torch.cuda.synchronize()
+    outs = []
+    for rep in range(8):
+        for layer, s in ((0, s1), (1, s2)):
+            with torch.cuda.stream(s):
+                outs.append((layer, pool.prefill_attn(layer, q_t, cu_t, st_t, bt_t, stream=s)))
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    refs = {layer: ora.prefill(layer, q_t.float().cpu().numpy(), cu, st, bt) for layer in (0, 1)}
+    for layer, out in outs:
+        got = out.float().cpu().numpy()
+        assert _rel_err(got, refs[layer]) <= TOL, layer
