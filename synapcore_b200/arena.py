@@ -27,6 +27,7 @@ from typing import Deque, Dict, List, Optional, Tuple, Union
 import numpy as np
 import torch
 
+from .npz_io import parallel_for
 from .pool import KVPool, PAGE_TOKENS
 
 ArrayLike = Union[np.ndarray, torch.Tensor]
@@ -183,6 +184,51 @@ class PagedKVArena:
                 k, v = k[sel], v[sel]
             pool.write_pages(self._ids([ids[i] for i in sel]), k, v)
             return ids
+
+    def reserve_page(self, prefix_hash_hex: str) -> int:
+        """The allocation step of write_page_fp16 alone (same clock, free-list
+        and LRU effects); the caller writes the page bytes later."""
+        with self.lock:
+            self._check_pool()
+            return self._allocate_page_slot_unlocked(prefix_hash_hex)
+
+    def write_loaded_pages(self, entries: List[Tuple[int, Dict[str, np.ndarray]]]) -> None:
+        """Write pages reloaded from `.npz` blocks, in list order, with one
+        pinned host -> device copy per array kind and one write launch per
+        kind. Each entry is (page_id, arrays) with arrays either {k, v}
+        ([L, 1, H, 16, D] fp16) or {kq, ks, vq, vs} (int8 codes and fp16
+        scales). A page id listed twice keeps its last entry, as writing the
+        entries one by one would."""
+        last: Dict[int, int] = {}
+        for i, (pid, _) in enumerate(entries):
+            last[int(pid)] = i
+        plain = [entries[i] for i in sorted(last.values()) if "kq" not in entries[i][1]]
+        quant = [entries[i] for i in sorted(last.values()) if "kq" in entries[i][1]]
+        L, H, T, D = self.num_layers, self.num_kv_heads, self.PAGE_TOKENS, self.head_dim
+        with self.lock:
+            pool = self._check_pool()
+            if plain:
+                k = self._stage([a["k"] for _, a in plain], (L, H, T, D), torch.float16)
+                v = self._stage([a["v"] for _, a in plain], (L, H, T, D), torch.float16)
+                pool.write_pages(self._ids([p for p, _ in plain]), k, v)
+            if quant:
+                kq = self._stage([a["kq"] for _, a in quant], (L, H, T, D), torch.int8)
+                vq = self._stage([a["vq"] for _, a in quant], (L, H, T, D), torch.int8)
+                ks = self._stage([a["ks"] for _, a in quant], (L, H, T), torch.float16)
+                vs = self._stage([a["vs"] for _, a in quant], (L, H, T), torch.float16)
+                pool.write_pages_quantized(self._ids([p for p, _ in quant]), kq, ks, vq, vs)
+
+    def _stage(self, arrays: List[np.ndarray], shape: Tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        """Stack host arrays into one pinned buffer and start its copy to the
+        device (the pinned block is not reused before the copy completes)."""
+        host = torch.empty((len(arrays),) + shape, dtype=dtype, pin_memory=True)
+        h = host.numpy()
+
+        def fill(i: int) -> None:
+            h[i] = np.asarray(arrays[i]).reshape(shape)
+
+        parallel_for(fill, len(arrays))
+        return host.to(self.device, non_blocking=True)
 
     def write_page_quantized(self, prefix_hash_hex: str, kq: ArrayLike, ks: ArrayLike, vq: ArrayLike,
                              vs: ArrayLike) -> int:

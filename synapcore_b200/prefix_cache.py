@@ -5,7 +5,10 @@ Behaviour follows native/native_engine.py:2125-2435 (NumPy path):
 into the arena and registered in the KV hash table, one `.npz` per block on
 disk (keys k, v — or kq, ks, vq, vs in int8 mode) under an LRU disk budget,
 and longest-prefix matching that takes arena hits first and reloads evicted
-blocks from disk. The page bytes live on the GPU; the int8 codes saved to
+blocks from disk. A match allocates reloaded pages during its walk (the
+reference's bookkeeping order), then reads their block files in parallel and
+moves them to the device in one pinned copy and one write launch per block
+kind. The page bytes live on the GPU; the int8 codes saved to
 disk are read back from the device quantiser, so they are the codes the
 reference's quantize_kv_int8_numpy would produce.
 
@@ -26,6 +29,7 @@ import torch
 
 from .arena import PagedKVArena
 from .kv_index import KVPrefixIndex
+from .npz_io import read_npz_many
 
 
 class PagedKVStats(TypedDict):
@@ -150,6 +154,7 @@ class NativeKVPrefixCache:
         n_full = max(0, len(token_ids) - 1) // self.BLOCK_SIZE
         prev = seed_root_hex
         pids: List[int] = []
+        staged: List[Tuple[int, Path]] = []
         for bi in range(n_full):
             cur = chain_merkle_prefix_hash(prev, token_ids[bi * self.BLOCK_SIZE:(bi + 1) * self.BLOCK_SIZE])
             pid = self.arena.lookup_page_id(cur)
@@ -161,16 +166,19 @@ class NativeKVPrefixCache:
             found = self.bridge.kv_lookup(bytes.fromhex(cur))
             path = self._npz_path(cur)
             if (found or path.exists()) and path.exists():
-                with np.load(path) as data:
-                    if "kq" in data:
-                        pid = self.arena.write_page_quantized(cur, data["kq"], data["ks"], data["vq"], data["vs"])
-                    else:
-                        pid = self.arena.write_page_fp16(cur, data["k"], data["v"])
+                # the page is allocated now (same clock / LRU / free-list
+                # order as a write per block); the block files are read in
+                # parallel after the walk and written in one staged copy
+                pid = self.arena.reserve_page(cur)
+                staged.append((pid, path))
                 pids.append(pid)
                 self.blocks_loaded_from_disk += 1
                 prev = cur
             else:
                 break
+        if staged:
+            arrays = read_npz_many([path for _, path in staged])
+            self.arena.write_loaded_pages([(pid, a) for (pid, _), a in zip(staged, arrays)])
         return pids
 
     def match_longest_prefix(self, token_ids: List[int], seed_root_hex: str

@@ -181,3 +181,71 @@ def test_fp16_prefix_cache_matches_reference_semantics(cuda_device, tmp_path):
         if max_pages == 8:
             np.testing.assert_array_equal(kd.cpu().numpy(), k[:, :, :, :80])
             np.testing.assert_array_equal(vd.cpu().numpy(), v[:, :, :, :80])
+
+
+def test_int8_prefix_cache_reload_matches_reference_semantics(cuda_device, tmp_path):
+    """int8 mode: blocks reloaded from disk in one staged write per match,
+    against the oracle's one-write-per-block walk. With 3 arena pages the
+    walk's own allocations evict pages it already listed."""
+    from oracle.kv_oracle import ArenaOracle, KVTableOracle, PrefixCacheOracle
+    from synapcore_b200 import NativeKVPrefixCache
+
+    rng = np.random.default_rng(11)
+    toks = list(range(3, 3 + 97))
+    k = (rng.standard_normal((2, 1, 4, 97, 128)) * 0.7).astype(np.float16)
+    v = (rng.standard_normal((2, 1, 4, 97, 128)) * 0.7).astype(np.float16)
+    for max_pages in (3, 8):
+        cache = NativeKVPrefixCache(tmp_path / f"d{max_pages}", None, num_layers=2, num_kv_heads=4, head_dim=128,
+                                    max_pages=max_pages, max_disk_blocks=8, quant_mode="int8",
+                                    timestamp_fn=lambda: 2.0)
+        ora = PrefixCacheOracle(tmp_path / f"o{max_pages}" / "kv_cache_blocks",
+                                ArenaOracle(max_pages, 2, 4, 128, "int8"), KVTableOracle(), max_disk_blocks=8)
+        assert cache.save_prefix_blocks_numpy(toks, k, v, "cd" * 32) == 6
+        assert ora.save(toks, k, v, "cd" * 32, timestamp=lambda: 2.0) == 6
+        # drop the arena's tables so every block comes back from disk
+        for a in (cache.arena, ora.arena):
+            a.page_table.clear()
+            a.reverse_page_table.clear()
+            a.page_last_used.clear()
+            a.free_pages.clear()
+            a.free_pages.extend(range(a.max_pages))
+        n, kd, vd = cache.match_longest_prefix(toks, "cd" * 32)
+        n_o, k_o, v_o = ora.match(toks, "cd" * 32)
+        assert n == n_o == 96
+        np.testing.assert_array_equal(kd.cpu().numpy(), k_o)
+        np.testing.assert_array_equal(vd.cpu().numpy(), v_o)
+        assert cache.arena.page_table == ora.arena.page_table
+        assert cache.arena.page_last_used == ora.arena.page_last_used
+        assert list(cache.arena.free_pages) == list(ora.arena.free_pages)
+        assert cache.blocks_loaded_from_disk == ora.blocks_loaded_from_disk == 6
+
+
+def test_fp16_cache_reloads_int8_blocks_as_dequantised_pages(cuda_device, tmp_path):
+    """An fp16 cache over a store written in int8 mode stores
+    fp16(q * f32(scale)) for each reloaded block, as the reference's
+    write_page_quantized does in fp16 mode."""
+    from oracle.kv_oracle import dequantize_kv_int8
+    from synapcore_b200 import NativeKVPrefixCache
+
+    rng = np.random.default_rng(12)
+    toks = list(range(50, 50 + 65))
+    k = rng.standard_normal((2, 1, 4, 65, 128)).astype(np.float16)
+    v = rng.standard_normal((2, 1, 4, 65, 128)).astype(np.float16)
+    writer = NativeKVPrefixCache(tmp_path, None, num_layers=2, num_kv_heads=4, head_dim=128, max_pages=8,
+                                 max_disk_blocks=8, quant_mode="int8", timestamp_fn=lambda: 0.0)
+    assert writer.save_prefix_blocks_numpy(toks, k, v, "ef" * 32) == 4
+    reader = NativeKVPrefixCache(tmp_path, None, num_layers=2, num_kv_heads=4, head_dim=128, max_pages=8,
+                                 max_disk_blocks=8, quant_mode="fp16", timestamp_fn=lambda: 0.0)
+    n, kd, vd = reader.match_longest_prefix(toks, "ef" * 32)
+    assert n == 64 and reader.blocks_loaded_from_disk == 4
+    from synapcore_b200.prefix_cache import chain_merkle_prefix_hash
+
+    prev, want_k, want_v = "ef" * 32, [], []
+    for b in range(4):
+        cur = chain_merkle_prefix_hash(prev, toks[16 * b:16 * (b + 1)])
+        with np.load(reader.kv_dir / f"{cur[:32]}_np.npz") as d:
+            want_k.append(dequantize_kv_int8(d["kq"], d["ks"]))
+            want_v.append(dequantize_kv_int8(d["vq"], d["vs"]))
+        prev = cur
+    np.testing.assert_array_equal(kd.cpu().numpy(), np.concatenate(want_k, axis=3))
+    np.testing.assert_array_equal(vd.cpu().numpy(), np.concatenate(want_v, axis=3))
