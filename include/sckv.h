@@ -230,6 +230,37 @@ SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
                      const int32_t* start_pos, const int32_t* block_table,
                      int64_t bt_stride, int max_blocks, void* stream);
 
+/* Projections + per-head QK-norm + RoPE + K/V append of one layer in one
+ * tcgen05 kernel (16-bit pools, head_dim 128). Replaces q/k/v = x @ W^T
+ * (models/adapters.py:1167-1169, fp16 weights), the per-head RMSNorm
+ * (:1171-1185), RoPE (:1191-1192) and the KV-cache concat (:1194-1207) of
+ * ModularAttentionEngine.forward_numpy: k and v of token i of sequence b
+ * land in slot start_pos[b] + i of the sequence's pages of `layer`, the
+ * rotated q in q_out [n_tokens][num_q_heads][128].
+ * x : [n_tokens][hidden] in x_dtype (F16 or BF16, the weights' type);
+ *     x_lo (optional, same shape) is added to x in the products — an fp32
+ *     input split by sckv_split_hi_lo keeps fp32 accuracy this way.
+ * w_q [num_q_heads*128][hidden], w_k / w_v [Hkv*128][hidden] row-major.
+ * q_norm_len / k_norm_len: 0 or 128 (per-head fp16 weights); whole-width
+ * norms return SCKV_ERR_UNSUPPORTED (use the projections + sckv_append_rope).
+ * workspace: >= n_tokens * 512 bytes (the per-token cos / sin table).
+ * hidden % 8 == 0; x, x_lo, weights, q_out and workspace 16-byte aligned. */
+SCKV_API int sckv_qkv_append(sckv_pool* pool, int layer, const void* x,
+                     const void* x_lo, int x_dtype, int n_tokens, int hidden,
+                     const void* w_q, const void* w_k, const void* w_v,
+                     int num_q_heads, const void* q_norm_w, int q_norm_len,
+                     const void* k_norm_w, int k_norm_len, float eps,
+                     const float* inv_freq, float rope_scaling, int n_seqs,
+                     const int32_t* cu_tokens, const int32_t* start_pos,
+                     const int32_t* block_table, int64_t bt_stride,
+                     int max_blocks, void* q_out, int q_out_dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* fp32 x -> hi = round(x), lo = round(x - hi) in F16 or BF16 (n elements):
+ * the two-part input of sckv_qkv_append for fp32 activations. */
+SCKV_API int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo,
+                     int dtype, void* stream);
+
 /* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
 #define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)
 

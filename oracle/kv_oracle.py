@@ -186,6 +186,19 @@ def qk_norm_rope(q: np.ndarray, k: np.ndarray, q_w: Optional[np.ndarray], k_w: O
     return qr[0].transpose(1, 0, 2), kr[0].transpose(1, 0, 2).astype(np.float16)
 
 
+def qkv_project(x_f32: np.ndarray, w_q: np.ndarray, w_k: np.ndarray, w_v: np.ndarray, hq: int, hkv: int
+                ) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """The projections of forward_numpy (models/adapters.py:1167-1169):
+    x [T, hidden] float32 times each fp16 weight [out, hidden] widened to
+    float32 and transposed. Returns q [T, Hq, D], k and v [T, Hkv, D] float32."""
+    x = x_f32.astype(np.float32)
+    q = x @ w_q.astype(np.float32).T
+    k = x @ w_k.astype(np.float32).T
+    v = x @ w_v.astype(np.float32).T
+    T = x.shape[0]
+    return q.reshape(T, hq, -1), k.reshape(T, hkv, -1), v.reshape(T, hkv, -1)
+
+
 def sdpa_prefill(q_f32: np.ndarray, k: np.ndarray, v: np.ndarray, start: int,
                  scale: Optional[float] = None) -> np.ndarray:
     """Causal prompt pass (models/adapters.py:1209-1229 with the -1e9 mask of

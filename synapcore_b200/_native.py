@@ -77,6 +77,11 @@ _SIGNATURES = [
      [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int,
       c_void_p, c_int, c_float, c_void_p, c_float, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int,
       c_void_p]),
+    ("sckv_qkv_append", c_int,
+     [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+      c_void_p, c_int, c_float, c_void_p, c_float, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+      c_int, c_void_p, c_size_t, c_void_p]),
+    ("sckv_split_hi_lo", c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_prefill_attn", c_int,
      [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float,
       c_void_p, c_int, c_void_p]),

@@ -28,6 +28,7 @@ enum SckvKernelId : int32_t {
   KID_EVICT = 11,
   KID_RESERVE = 12,
   KID_PREFILL = 13,
+  KID_QKV = 14,
 };
 
 // Allocator control words (int64, device).
@@ -126,6 +127,16 @@ __device__ __forceinline__ void sckv_report(int32_t* status, int32_t code,
     status[2] = kernel;
   }
   atomicAdd(&status[3], 1);
+}
+
+// Sequence of token t: the last b with cu[b] <= t (cu: n_seqs + 1 offsets).
+__device__ __forceinline__ int sckv_find_seq(const int32_t* cu, int n_seqs, int t) {
+  int lo = 0, hi = n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(cu + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
 }
 
 // ---------------------------------------------------------------------------

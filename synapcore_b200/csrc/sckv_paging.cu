@@ -88,14 +88,6 @@ __device__ __forceinline__ void store8_16(void* dst, int64_t idx, int dtype, con
 }
 
 // Find sequence b with cu[b] <= t < cu[b+1] (cu non-decreasing, cu[0] = 0).
-__device__ __forceinline__ int find_seq(const int32_t* cu, int n_seqs, int t) {
-  int lo = 0, hi = n_seqs - 1;
-  while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
-    if (__ldg(cu + mid) <= t) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
 
 // Resolve the destination page of (seq b, position pos); -1 on error (reported).
 __device__ __forceinline__ int64_t resolve_page(const Geo& g, const int32_t* bt, int64_t stride,
@@ -125,7 +117,7 @@ __global__ void append16_kernel(Geo g, int layer0, int n_layers, const void* k_n
     int kv = (int)(r % 2); r /= 2;
     int t = (int)(r % n_tokens);
     int l = (int)(r / n_tokens);
-    int b = find_seq(cu, n_seqs, t);
+    int b = sckv_find_seq(cu, n_seqs, t);
     int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
     int64_t page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
     if (page < 0) continue;
@@ -182,7 +174,7 @@ __global__ void append_int8_kernel(Geo g, int layer0, int n_layers, const void* 
     int kv = (int)(r % 2); r /= 2;
     int t = (int)(r % n_tokens);
     int l = (int)(r / n_tokens);
-    int b = find_seq(cu, n_seqs, t);
+    int b = sckv_find_seq(cu, n_seqs, t);
     int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
     int64_t page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
     if (page < 0) continue;
@@ -544,7 +536,7 @@ __global__ void __launch_bounds__(kRopeWarps * 32) append_rope_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = g.D, half = D / 2;  // D == 128
   const int hk = g.H;
-  const int b = find_seq(cu, n_seqs, t);
+  const int b = sckv_find_seq(cu, n_seqs, t);
   const int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
   const int64_t page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
   const int dims[4] = {lane, lane + 32, half + lane, half + lane + 32};

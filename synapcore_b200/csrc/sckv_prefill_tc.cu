@@ -8,7 +8,7 @@
 // Work item = (sequence, two tiles of 128 query rows, kv head). The rows
 // are (token, q head) pairs of the G heads that read the kv head, so a tile
 // holds 128 / G tokens; both tiles share every K/V tile loaded. One
-// persistent CTA per SM (512 TMEM columns) claims items from a counter;
+// persistent CTA per SM (512 TMEM columns) claims items from a work counter;
 // 16 warps:
 //   warps 0, 3  claim items (warp 0), load the item's Q (one TMA box per
 //              64-dim half and tile when q has the pool's type, else the
@@ -39,8 +39,10 @@
 
 #include "sckv_internal.cuh"
 #include "sckv_mma_common.cuh"
+#include "sckv_tcgen05.cuh"
 
 using namespace sckv_mma;
+using namespace sckv_tc;
 
 namespace {
 
@@ -99,82 +101,6 @@ struct TcParams {
   unsigned long long* next_item;  // work counter, zero at launch
   float scale_log2;
 };
-
-// ------------------------------------------------------------------ tcgen05
-// Shared-memory matrix descriptor, 128-byte swizzle (sm100 layout: start,
-// leading and stride byte offsets in 16-byte units, version 1, swizzle code 2).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Instruction descriptor of kind::f16 with fp32 accumulation, M = 128.
-__host__ __device__ constexpr uint32_t instr_desc_f16(bool bf16, int n, bool b_mn_major) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kRowsTc >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
-      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
-      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-// Every lane of the warp waits; the result is the same on all lanes.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  const bool ok = mbar_wait_bounded(bar, parity, SCKV_WAIT_LIMIT_NS);
-  return __all_sync(0xffffffffu, ok);
-}
 
 // Tokens of sequence s (0 and a reported bounds error if its offsets or
 // start are out of range).
@@ -263,12 +189,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Persistent, one CTA per SM: each CTA claims items from a counter in the
-// pool's control words (heaviest-first order within each sequence) until
-// they run out. K/V tiles of all its items are numbered by one running
-// counter (ring slot g % 4), and each softmax warpgroup numbers its own S
-// tiles by another (S / P buffer g & 1), which fixes every barrier's phase.
-// Calls on one pool must not overlap on the GPU (they share the counter).
+// Persistent, one CTA per SM: each CTA claims items from the launch's work
+// counter (one of the pool's, taken round-robin per launch and zeroed just
+// before it, so launches on other streams use other counters), heaviest-first
+// within each sequence, until they run out. K/V tiles of all its items are
+// numbered by one running counter (ring slot g % 4), and each softmax
+// warpgroup numbers its own S tiles by another (S / P buffer g & 1), which
+// fixes every barrier's phase.
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap,

@@ -1,0 +1,457 @@
+// Fused attention input on the 5th-generation tensor cores: the q / k / v
+// projections, the optional per-head QK-norm, RoPE and the K/V page append of
+// one layer in one kernel.
+//
+// Replaces, for one layer of ModularAttentionEngine.forward_numpy
+// (models/adapters.py:1148-1207): q/k/v = x @ W^T with fp16 weights
+// (:1167-1169), the per-head RMSNorm of q and k (:1171-1185, rmsnorm_f32
+// :1129-1132), RoPE at positions start + i (:1191-1192, apply_rope_f32
+// :1134-1146) and the KV-cache concat of fp16(k), fp16(v) (:1194-1207). The
+// rotated q goes to q_out for the attention kernels.
+//
+// One CTA computes a 128-token x 128-dim tile: one head of q, k or v
+// (grid.x = q heads, then k heads, then v heads; grid.y = token tiles), so
+// every thread of the epilogue owns one token's whole head vector in one
+// tensor-memory lane and the norm and the (i, i + 64) rotation pairs stay
+// inside the thread.
+//   warp 0     TMA: per 64-wide step of the hidden dim, the x tile (and its
+//              low part, for fp32 inputs split into hi + lo) and the weight
+//              tile (128 rows of W), 128-byte swizzle, into a 4-stage ring.
+//   warp 1     allocates 128 TMEM columns and issues
+//              acc (128 x 128 fp32) += x . W^T   4 x tcgen05.mma (K = 16) per step
+//              (8 with the low part); tcgen05.commit frees the stage.
+//   warps 2-5  epilogue: tcgen05.ld of the thread's row, per-head RMSNorm,
+//              RoPE with a per-token cos / sin table (computed once per call
+//              by rope_table_kernel, the same operations as
+//              sckv_append_rope), rounding to the output / pool type and
+//              the stores (q_out row, or the K / V row of the token's page).
+// The epilogue follows the reference's fp32 operation order with IEEE
+// operations; the projection sums in fp32 in the tensor core's order.
+#include <cuda.h>
+#include <math.h>
+
+#include "sckv_internal.cuh"
+#include "sckv_mma_common.cuh"
+#include "sckv_tcgen05.cuh"
+
+using namespace sckv_mma;
+using namespace sckv_tc;
+
+namespace {
+
+constexpr int kQkvBM = 128;                      // tokens per tile (UMMA M)
+constexpr int kQkvBN = 128;                      // output dims per tile = one head (UMMA N)
+constexpr int kQkvBK = 64;                       // hidden elements per step: 128-byte rows
+constexpr int kQkvTile = kQkvBM * kQkvBK * 2;    // one operand tile: 16 KiB
+constexpr int kQkvThreads = 192;
+constexpr uint32_t kQkvTmemCols = 128;
+constexpr int kQkvStages = 4;
+constexpr int kRopePairs = 64;                   // head_dim / 2
+
+template <bool kSplit>
+struct QkvSmem {
+  static constexpr int kStageBytes = (kSplit ? 3 : 2) * kQkvTile;  // x, W (, x_lo)
+  static constexpr int kBarOff = kQkvStages * kStageBytes;
+  static constexpr int kBytes = 1024 + kBarOff + (2 * kQkvStages + 1) * 8 + 16;
+};
+
+struct QkvParams {
+  void* q_out;
+  void* pool_data;
+  int32_t* status;
+  const __half* q_norm_w;  // [128] or null
+  const __half* k_norm_w;  // [128] or null
+  const float2* rope_cs;   // [n_tok][64] (cos, sin)
+  const int32_t* cu;
+  const int32_t* start_pos;
+  const int32_t* bt;
+  int64_t bt_stride;
+  int64_t max_pages;
+  int max_blocks;
+  int n_seqs;
+  int n_tok;
+  int hidden;
+  int hq;
+  int hkv;
+  int layer;
+  int q_out_dtype;
+  int pool_dtype;
+  float eps;
+};
+
+// cos / sin of every (token, frequency) pair: position start_pos[b] + i
+// divided by rope_scaling, times inv_freq[j], as sckv_append_rope computes
+// them (apply_rope_f32, models/adapters.py:1134-1146).
+__global__ void rope_table_kernel(const float* inv_freq, float rope_scaling, int n_seqs, int n_tok,
+                                  const int32_t* cu, const int32_t* start_pos, float2* cs) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n_tok * kRopePairs) return;
+  const int t = (int)(idx / kRopePairs), j = (int)(idx % kRopePairs);
+  const int b = sckv_find_seq(cu, n_seqs, t);
+  const int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
+  const float fpos = __fdiv_rn((float)pos, rope_scaling);
+  const float ang = __fmul_rn(fpos, __ldg(inv_freq + j));
+  float s, c;
+  sincosf(ang, &s, &c);
+  cs[idx] = make_float2(c, s);
+}
+
+// fp32 x -> hi = round(x), lo = round(x - hi) in the MMA's 16-bit type, so
+// hi . W + lo . W carries x to ~2^-22 relative (W is exact in that type).
+__global__ void split_hi_lo_kernel(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, int bf16) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    if (bf16) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+      hi[i] = __bfloat16_as_ushort(h);
+      lo[i] = __bfloat16_as_ushort(l);
+    } else {
+      const __half h = __float2half_rn(v);
+      const __half l = __float2half_rn(v - __half2float(h));
+      hi[i] = __half_as_ushort(h);
+      lo[i] = __half_as_ushort(l);
+    }
+  }
+}
+
+// 32 fp32 values -> 32 elements of `dtype` at dst + idx (idx % 8 == 0, 16-byte aligned).
+__device__ __forceinline__ void store32(void* dst, int64_t idx, int dtype, const float (&y)[32]) {
+  if (dtype == SCKV_DTYPE_F32) {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + idx);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+  } else {
+    const bool bf = dtype == SCKV_DTYPE_BF16;
+    uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(dst) + idx);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        w[k] = bf ? pack2<true>(y[8 * i + 2 * k], y[8 * i + 2 * k + 1])
+                  : pack2<false>(y[8 * i + 2 * k], y[8 * i + 2 * k + 1]);
+      d[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <bool kBF16, bool kSplit>
+__global__ void __launch_bounds__(kQkvThreads, 1)
+    qkv_append_kernel(const QkvParams p, const __grid_constant__ CUtensorMap xmap,
+                      const __grid_constant__ CUtensorMap xlomap, const __grid_constant__ CUtensorMap wqmap,
+                      const __grid_constant__ CUtensorMap wkmap, const __grid_constant__ CUtensorMap wvmap) {
+  using SM = QkvSmem<kSplit>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + SM::kBarOff);  // [S] stage landed (TMA)
+  uint64_t* empty = full + kQkvStages;                               // [S] stage read by its MMAs (commit)
+  uint64_t* acc_full = empty + kQkvStages;                           // every MMA finished (commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x;  // output head: q heads, then k heads, then v heads
+  const int m0 = blockIdx.y * kQkvBM;
+  const int nk = (p.hidden + kQkvBK - 1) / kQkvBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kQkvStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kQkvTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const CUtensorMap* wmap = n < p.hq ? &wqmap : (n < p.hq + p.hkv ? &wkmap : &wvmap);
+      const int row0 = (n < p.hq ? n : (n < p.hq + p.hkv ? n - p.hq : n - p.hq - p.hkv)) * kQkvBN;
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap)) : "memory");
+      int issued = 0;
+      for (int s = 0; s < nk; ++s) {
+        const int st = s % kQkvStages;
+        if (s >= kQkvStages) {
+          if (*abort_flag || !mbar_wait_bounded(&empty[st], ((s / kQkvStages) - 1) & 1, SCKV_WAIT_LIMIT_NS)) {
+            if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, n, KID_QKV);
+            *abort_flag = 1;
+            break;
+          }
+        }
+        const uint32_t stage = smem_u32(base + st * SM::kStageBytes);
+        mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
+        tma_load_2d(stage, &xmap, s * kQkvBK, m0, &full[st]);
+        tma_load_2d(stage + kQkvTile, wmap, s * kQkvBK, row0, &full[st]);
+        if (kSplit) tma_load_2d(stage + 2 * kQkvTile, &xlomap, s * kQkvBK, m0, &full[st]);
+        ++issued;
+      }
+      // copies still in flight land before the CTA may exit
+      for (int k = issued > kQkvStages ? issued - kQkvStages : 0; k < issued; ++k)
+        mbar_wait_bounded(&full[k % kQkvStages], (k / kQkvStages) & 1, SCKV_WAIT_LIMIT_NS);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t kIdesc = instr_desc_f16(kBF16, kQkvBN, false);
+    bool ok = true;
+    for (int s = 0; s < nk; ++s) {
+      const int st = s % kQkvStages;
+      if (*abort_flag || !warp_wait(&full[st], (s / kQkvStages) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t a = smem_u32(base + st * SM::kStageBytes);
+        const uint32_t b = a + kQkvTile;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          // A = x rows (tokens), B = W rows (output dims), both K-major:
+          // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
+          const uint64_t bdesc = smem_desc_sw128(b + kk * 32, 16, 1024);
+          umma_ss(tmem, smem_desc_sw128(a + kk * 32, 16, 1024), bdesc, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+          if (kSplit) umma_ss(tmem, smem_desc_sw128(a + 2 * kQkvTile + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
+        }
+        umma_commit(&empty[st]);
+      }
+      __syncwarp();
+    }
+    if (!ok) {
+      if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, n, KID_QKV);
+      if (lane == 0) *abort_flag = 1;
+    }
+    // fires once every MMA issued above has finished (at once if none was)
+    if (lane == 0) umma_commit(acc_full);
+    __syncwarp();
+    warp_wait(acc_full, 0);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes 32 quad .. 32 quad + 31
+    const int t = m0 + quad * 32 + lane;
+    const bool ready = warp_wait(acc_full, 0);
+    tc_fence_after();
+    // warp-uniform: the tensor-memory loads below are warp-wide
+    const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
+    if (ready && !aborted) {
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+      const int kind = n < p.hq ? 0 : (n < p.hq + p.hkv ? 1 : 2);  // q, k, v
+      const int head = kind == 0 ? n : (kind == 1 ? n - p.hq : n - p.hq - p.hkv);
+      const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
+      // every lane reads the tensor memory (the loads are warp-wide); rows
+      // past the last token are computed and dropped
+      float inv = 1.f;
+      if (nw != nullptr) {
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = __uint_as_float(r[i]);
+            ss = __fmaf_rn(x, x, ss);
+          }
+        }
+        inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kQkvBN), p.eps)));
+      }
+      const bool live = t < p.n_tok;
+      int64_t dst = -1;
+      void* out = p.q_out;
+      int out_dtype = p.q_out_dtype;
+      if (live) {
+        if (kind == 0) {
+          dst = ((int64_t)t * p.hq + head) * kQkvBN;
+        } else {
+          const int b = sckv_find_seq(p.cu, p.n_seqs, t);
+          const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
+          const int blk = pos / SCKV_PAGE_TOKENS;
+          int32_t page = -1;
+          if (pos < 0 || blk >= p.max_blocks) {
+            sckv_report(p.status, SCKV_ERR_BOUNDS, pos < 0 ? pos : blk, KID_QKV);
+          } else {
+            page = __ldg(p.bt + (int64_t)b * p.bt_stride + blk);
+            if (page < 0 || page >= p.max_pages) {
+              sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_QKV);
+              page = -1;
+            }
+          }
+          if (page >= 0) {
+            // data layout [L][P][K|V][H][16][D]
+            const int64_t slab = (int64_t)p.layer * p.max_pages + page;
+            dst = (((slab * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kQkvBN;
+          }
+          out = p.pool_data;
+          out_dtype = p.pool_dtype;
+        }
+      }
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        // dims d = 32 hf + i and their rotation partners d + 64
+        uint32_t r1[32], r2[32];
+        tmem_ld32(trow + hf * 32, r1);
+        tmem_ld32(trow + 64 + hf * 32, r2);
+        tc_wait_ld();
+        if (dst < 0) continue;
+        float y1[32], y2[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int d = hf * 32 + i;
+          float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
+          if (nw != nullptr) {
+            x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
+            x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
+          }
+          if (kind < 2) {
+            const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + d);
+            y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+            y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+          } else {
+            y1[i] = x1;
+            y2[i] = x2;
+          }
+        }
+        store32(out, dst + hf * 32, out_dtype, y1);
+        store32(out, dst + 64 + hf * 32, out_dtype, y2);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kQkvTmemCols);
+  }
+}
+
+// 2-D map over a row-major [rows][hidden] 16-bit matrix, boxes of 64 x 128.
+int encode_rows(CUtensorMap* map, const void* ptr, int rows, int hidden, bool bf16) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return SCKV_ERR_CUDA;
+  const cuuint64_t dims[2] = {(cuuint64_t)hidden, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)hidden * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kQkvBK, (cuuint32_t)kQkvBM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                            const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SCKV_OK : sckv_record_error(__FILE__, __LINE__, "cuTensorMapEncodeTiled", "failed");
+}
+
+template <bool kBF16, bool kSplit>
+int launch_qkv(const QkvParams& prm, const CUtensorMap (&maps)[5], int n_heads, int m_tiles, cudaStream_t stream) {
+  auto kern = qkv_append_kernel<kBF16, kSplit>;
+  constexpr int smem = QkvSmem<kSplit>::kBytes;
+  static_assert(smem <= 227 * 1024, "shared memory");
+  SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kern<<<dim3(n_heads, m_tiles), kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3], maps[4]);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo, int dtype, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !hi || !lo))) return SCKV_ERR_INVALID_ARG;
+  if (dtype != SCKV_DTYPE_F16 && dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
+  if (n == 0) return SCKV_OK;
+  const int64_t blocks = (n + 255) / 256;
+  split_hi_lo_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, as_stream(stream)>>>(
+      x, n, reinterpret_cast<uint16_t*>(hi), reinterpret_cast<uint16_t*>(lo), dtype == SCKV_DTYPE_BF16);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const void* x_lo, int x_dtype,
+                               int n_tokens, int hidden, const void* w_q, const void* w_k, const void* w_v,
+                               int num_q_heads, const void* q_norm_w, int q_norm_len, const void* k_norm_w,
+                               int k_norm_len, float eps, const float* inv_freq, float rope_scaling, int n_seqs,
+                               const int32_t* cu_tokens, const int32_t* start_pos, const int32_t* block_table,
+                               int64_t bt_stride, int max_blocks, void* q_out, int q_out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (pool == nullptr || layer < 0 || layer >= pool->num_layers) return SCKV_ERR_INVALID_ARG;
+  if (n_tokens < 0 || n_seqs < 0 || num_q_heads <= 0 || hidden <= 0) return SCKV_ERR_INVALID_ARG;
+  if (x_dtype != SCKV_DTYPE_F16 && x_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
+  if (q_out_dtype != SCKV_DTYPE_F32 && q_out_dtype != SCKV_DTYPE_F16 && q_out_dtype != SCKV_DTYPE_BF16)
+    return SCKV_ERR_INVALID_ARG;
+  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+  if (pool->head_dim != kQkvBN) return SCKV_ERR_UNSUPPORTED;
+  // norms over the whole projection need every head of a token: the
+  // unfused path (projection, then sckv_append_rope) covers them
+  if ((q_norm_len != 0 && q_norm_len != kQkvBN) || (k_norm_len != 0 && k_norm_len != kQkvBN))
+    return SCKV_ERR_UNSUPPORTED;
+  if ((q_norm_len != 0 && q_norm_w == nullptr) || (k_norm_len != 0 && k_norm_w == nullptr))
+    return SCKV_ERR_INVALID_ARG;
+  if (hidden % 8 != 0) return SCKV_ERR_UNSUPPORTED;  // 16-byte row pitch for the tensor maps
+  if (n_tokens == 0 || n_seqs == 0) return SCKV_OK;
+  if (!x || !w_q || !w_k || !w_v || !inv_freq || !cu_tokens || !start_pos || !block_table || !q_out ||
+      !workspace || max_blocks <= 0 || bt_stride < max_blocks || !(rope_scaling != 0.f))
+    return SCKV_ERR_INVALID_ARG;
+  if (workspace_bytes < (size_t)n_tokens * kRopePairs * sizeof(float2)) return SCKV_ERR_INVALID_ARG;
+  if (!aligned16(x) || (x_lo && !aligned16(x_lo)) || !aligned16(w_q) || !aligned16(w_k) || !aligned16(w_v) ||
+      !aligned16(q_out) || !aligned16(workspace))
+    return SCKV_ERR_ALIGNMENT;
+  const int hkv = pool->num_kv_heads;
+  const int64_t n_heads = (int64_t)num_q_heads + 2LL * hkv;
+  const int64_t m_tiles = ((int64_t)n_tokens + kQkvBM - 1) / kQkvBM;
+  if (n_heads > INT32_MAX || m_tiles > 65535) return SCKV_ERR_UNSUPPORTED;
+  if ((int64_t)num_q_heads * kQkvBN > INT32_MAX || (int64_t)hkv * kQkvBN > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
+
+  const bool bf16 = x_dtype == SCKV_DTYPE_BF16;
+  CUtensorMap maps[5];
+  int rc = encode_rows(&maps[0], x, n_tokens, hidden, bf16);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[1], x_lo ? x_lo : x, n_tokens, hidden, bf16);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[2], w_q, num_q_heads * kQkvBN, hidden, bf16);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[3], w_k, hkv * kQkvBN, hidden, bf16);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[4], w_v, hkv * kQkvBN, hidden, bf16);
+  if (rc != SCKV_OK) return rc;
+
+  cudaStream_t s = as_stream(stream);
+  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  float2* cs = reinterpret_cast<float2*>(workspace);
+  const int64_t n_cs = (int64_t)n_tokens * kRopePairs;
+  rope_table_kernel<<<(unsigned)((n_cs + 255) / 256), 256, 0, s>>>(inv_freq, rope_scaling, n_seqs, n_tokens,
+                                                                     cu_tokens, start_pos, cs);
+  SCKV_LAUNCH_CHECK();
+
+  QkvParams prm{};
+  prm.q_out = q_out;
+  prm.pool_data = pool->data;
+  prm.status = pool->status;
+  prm.q_norm_w = q_norm_len ? reinterpret_cast<const __half*>(q_norm_w) : nullptr;
+  prm.k_norm_w = k_norm_len ? reinterpret_cast<const __half*>(k_norm_w) : nullptr;
+  prm.rope_cs = cs;
+  prm.cu = cu_tokens;
+  prm.start_pos = start_pos;
+  prm.bt = block_table;
+  prm.bt_stride = bt_stride;
+  prm.max_pages = pool->max_pages;
+  prm.max_blocks = max_blocks;
+  prm.n_seqs = n_seqs;
+  prm.n_tok = n_tokens;
+  prm.hidden = hidden;
+  prm.hq = num_q_heads;
+  prm.hkv = hkv;
+  prm.layer = layer;
+  prm.q_out_dtype = q_out_dtype;
+  prm.pool_dtype = pool->kv_dtype;
+  prm.eps = eps;
+  if (bf16) {
+    return x_lo ? launch_qkv<true, true>(prm, maps, (int)n_heads, (int)m_tiles, s)
+                : launch_qkv<true, false>(prm, maps, (int)n_heads, (int)m_tiles, s);
+  }
+  return x_lo ? launch_qkv<false, true>(prm, maps, (int)n_heads, (int)m_tiles, s)
+              : launch_qkv<false, false>(prm, maps, (int)n_heads, (int)m_tiles, s);
+}

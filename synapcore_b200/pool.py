@@ -234,6 +234,94 @@ class KVPool:
                 "sckv_append_rope")
         return q_out
 
+    def qkv_append(self, layer: int, x: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor,
+                   cu_tokens: torch.Tensor, start_pos: torch.Tensor, block_table: torch.Tensor,
+                   inv_freq: torch.Tensor, rope_scaling: float = 1.0, q_norm_w: Optional[torch.Tensor] = None,
+                   k_norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6, q_out: Optional[torch.Tensor] = None,
+                   q_out_dtype: torch.dtype = torch.float32, max_blocks: Optional[int] = None,
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """q/k/v projections of x [n_tokens, hidden] with row-major weights
+        (w_q [Hq*D, hidden], w_k / w_v [Hkv*D, hidden], float16 or bfloat16),
+        optional per-head QK-norm, RoPE, and the K/V append for one layer, in
+        one tensor-core launch; returns the rotated q [n_tokens, Hq, D].
+        An fp32 x is split into hi + lo parts of the weights' type, so the
+        products keep fp32 accuracy; a 16-bit x must have the weights' type.
+        Whole-width norms (weights of Hq*D / Hkv*D elements) need every head
+        of a token in one place and take the unfused route: the projections
+        as fp32 matmuls, then append_rope."""
+        nt, hidden = x.shape
+        wdt = w_q.dtype
+        if wdt not in (torch.float16, torch.bfloat16) or w_k.dtype != wdt or w_v.dtype != wdt:
+            raise TypeError("w_q, w_k, w_v must share one dtype, float16 or bfloat16")
+        d = self.head_dim
+        if w_q.dim() != 2 or w_q.shape[1] != hidden or w_q.shape[0] % d != 0:
+            raise ValueError("w_q must be [Hq*D, hidden]")
+        hq = w_q.shape[0] // d
+        hkv = self.num_kv_heads
+        for name, w in (("w_k", w_k), ("w_v", w_v)):
+            if tuple(w.shape) != (hkv * d, hidden):
+                raise ValueError(f"{name} must be [Hkv*D, hidden]")
+        full_width = any(w is not None and w.numel() != d for w in (q_norm_w, k_norm_w))
+        if full_width:
+            xf = x.float()
+            q = (xf @ w_q.float().T).view(nt, hq, d)
+            k = (xf @ w_k.float().T).view(nt, hkv, d)
+            v = (xf @ w_v.float().T).view(nt, hkv, d)
+            return self.append_rope(layer, q, k, v, cu_tokens, start_pos, block_table, inv_freq, rope_scaling,
+                                    q_norm_w, k_norm_w, eps, q_out, q_out_dtype, max_blocks, stream)
+        x = x.contiguous()
+        w_q, w_k, w_v = w_q.contiguous(), w_k.contiguous(), w_v.contiguous()
+        n_seqs = cu_tokens.numel() - 1
+        bt = block_table if block_table.dim() == 2 else block_table.view(1, -1)
+        mb = bt.shape[1] if max_blocks is None else int(max_blocks)
+        if not 0 <= layer < self.num_layers:
+            raise ValueError("layer out of range")
+        for name, t in (("x", x), ("w_q", w_q), ("w_k", w_k), ("w_v", w_v)):
+            _need(t, name, self.device)
+        _need(inv_freq, "inv_freq", self.device, torch.float32, d // 2)
+        _need(cu_tokens, "cu_tokens", self.device, torch.int32, 1)
+        _need(start_pos, "start_pos", self.device, torch.int32, n_seqs)
+        _need(bt, "block_table", self.device, torch.int32, contiguous=False)
+        if bt.dim() != 2 or bt.shape[0] < n_seqs or mb > bt.shape[1] or bt.stride(1) != 1:
+            raise ValueError("block_table must be [>= n_seqs, >= max_blocks] with unit column stride")
+        norms = []
+        for name, w in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w)):
+            if w is None:
+                norms.append((None, 0))
+            else:
+                _need(w, name, self.device, torch.float16)
+                norms.append((w, w.numel()))
+        x_lo = None
+        if x.dtype == torch.float32:
+            hi = torch.empty((nt, hidden), dtype=wdt, device=self.device)
+            x_lo = torch.empty_like(hi)
+            N.check(self.lib.sckv_split_hi_lo(x.data_ptr(), x.numel(), hi.data_ptr(), x_lo.data_ptr(),
+                                              torch_dtype_code(wdt), _stream_ptr(stream)), "sckv_split_hi_lo")
+            x = hi
+        elif x.dtype != wdt:
+            raise TypeError("a 16-bit x must have the weights' dtype")
+        if q_out is None:
+            q_out = torch.empty((nt, hq, d), dtype=q_out_dtype, device=self.device)
+        else:
+            _need(q_out, "q_out", self.device)
+            if tuple(q_out.shape) != (nt, hq, d):
+                raise ValueError("q_out must be [n_tokens, Hq, D]")
+        ws = torch.empty(max(1, nt) * (d // 2) * 2, dtype=torch.float32, device=self.device)
+        (qw, qn), (kw, kn) = norms
+        N.check(self.lib.sckv_qkv_append(self.handle, layer, x.data_ptr(), _ptr(x_lo), torch_dtype_code(x.dtype), nt,
+                                         hidden, w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr(), hq, _ptr(qw), qn,
+                                         _ptr(kw), kn, float(eps), inv_freq.data_ptr(), float(rope_scaling), n_seqs,
+                                         cu_tokens.data_ptr(), start_pos.data_ptr(), bt.data_ptr(), bt.stride(0), mb,
+                                         q_out.data_ptr(), torch_dtype_code(q_out.dtype), ws.data_ptr(),
+                                         ws.numel() * 4, _stream_ptr(stream)),
+                "sckv_qkv_append")
+        if stream is not None:
+            # temporaries freed on return stay reserved until `stream` is past them
+            for t in (ws, x_lo, x if x_lo is not None else None):
+                if t is not None:
+                    t.record_stream(stream)
+        return q_out
+
     def write_pages(self, page_ids: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor,
                     stream: Optional[torch.cuda.Stream] = None) -> None:
         """k_src, v_src: [n, L, H, 16, D] float16 / bfloat16 / float32."""
