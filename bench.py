@@ -88,6 +88,13 @@ WORKLOADS = {
     "olmoe-mix-small": dict(kind="mix", model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128,
                             kv="fp16", qdt=torch.float16, batch=32, ctx=(16, 8192), new_per_step=8,
                             prompt=(64, 2048), fork_frac=0.25, prefix=1024, pool_pages=9000, evict_at=0.9),
+    # the attention input either side of the cache: q/k/v projections of
+    # the hidden states (bf16 activations and weights), per-head QK-norm,
+    # RoPE and the K/V append, fused in one launch per layer (sckv_qkv_append)
+    "qwen3-qkv": dict(kind="qkv", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
+                      kv="bf16", batch=128, tokens_per_seq=1, ctx=16384),
+    "qwen3-qkv-prefill": dict(kind="qkv", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
+                              kv="bf16", batch=8, tokens_per_seq=1024, ctx=0),
 }
 
 
@@ -537,6 +544,236 @@ def bench_ours(args, w_full, world, rank, local):
     return res
 
 
+# ----------------------------------------------------------------------------- fused attention input
+def qkv_flops(w, n_tok: int) -> int:
+    return 2 * n_tok * w["hidden"] * (w["hq"] + 2 * w["hkv"]) * w["d"]
+
+
+def qkv_bytes(w, n_tok: int) -> int:
+    """Algorithmic bytes of one layer launch: weights + x read, q_out + K/V rows written (bf16)."""
+    hd = (w["hq"] + 2 * w["hkv"]) * w["d"]
+    return 2 * (hd * w["hidden"] + n_tok * w["hidden"] + n_tok * hd)
+
+
+def bench_qkv(args, w, world, rank, local):
+    """One step = sckv_qkv_append for every layer over the step's tokens
+    (decode: one token per sequence; prefill: whole prompts)."""
+    from synapcore_b200.pool import KVPool, rope_inv_freq
+
+    dev = torch.device("cuda", local)
+    L, H, hq, d, hidden = w["layers"], w["hkv"], w["hq"], w["d"], w["hidden"]
+    B, tps = w["batch"], w["tokens_per_seq"]
+    n_tok = B * tps
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    scale = hidden ** -0.5
+    wq = [torch.randn(hq * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+    wk = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+    wv = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+    qn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+    kn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+    x = torch.randn(L, n_tok, hidden, device=dev, generator=g).to(torch.bfloat16)
+    ctx0 = w["ctx"]
+    mb = (ctx0 + tps + PAGE - 1) // PAGE
+    # only the pages the new tokens land in exist; earlier blocks are never touched
+    b0 = ctx0 // PAGE
+    nb = mb - b0
+    pool = KVPool(L, H, d, B * nb, w["kv"], device=dev)
+    bt = torch.zeros(B, mb, dtype=torch.int32, device=dev)
+    bt[:, b0:] = torch.arange(B * nb, dtype=torch.int32, device=dev).view(B, nb)
+    cu = torch.arange(0, n_tok + 1, tps, dtype=torch.int32, device=dev)
+    start = torch.full((B,), ctx0, dtype=torch.int32, device=dev)
+    inv = rope_inv_freq(1e6, d, dev)
+    q_out = torch.empty(L, n_tok, hq, d, dtype=torch.bfloat16, device=dev)
+
+    def step(xs, outs):
+        for l in range(L):
+            pool.qkv_append(l, xs[l], wq[l], wk[l], wv[l], cu, start, bt, inv, q_norm_w=qn, k_norm_w=kn,
+                            q_out=outs[l])
+
+    # a step is launch-bound at decode sizes (host work per call ~ the
+    # kernel's time), so each step is replayed from a CUDA graph, as a
+    # serving loop would; one graph per input / output buffer pair
+    comp = torch.cuda.current_stream()
+    d_x = [x, torch.empty_like(x)]
+    d_q = [q_out, torch.empty_like(q_out)]
+    d_x[1].copy_(x)
+    from synapcore_b200 import _native as N
+
+    n0 = N.launch_count()
+    step(x, q_out)
+    launches_per_step = N.launch_count() - n0  # rope table + projection (+ split-K finish) per layer
+    graphs = []
+    cap = torch.cuda.Stream()
+    for b in range(2):
+        cap.wait_stream(comp)
+        with torch.cuda.stream(cap):
+            step(d_x[b], d_q[b])
+        torch.cuda.synchronize()
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=cap):
+            step(d_x[b], d_q[b])
+        graphs.append(gph)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graphs[0].replay()
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graphs[0].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    launch_ms = ms_total / args.steps / L  # rope table + projection kernel of one layer
+    pool.raise_on_status()
+
+    # e2e: each step copies its hidden states in from pinned host memory and
+    # reads the rotated q back (double-buffered across steps, as a serving loop would)
+    h_x = x.cpu().pin_memory()
+    h_q = [torch.empty(q_out.shape, dtype=q_out.dtype).pin_memory() for _ in range(2)]
+    cstream = torch.cuda.Stream()
+    evs = {k: [torch.cuda.Event() for _ in range(2)] for k in ("in_ready", "in_free", "out_ready", "out_done")}
+
+    def e2e_run(n):
+        def copy_in(i):
+            b = i % 2
+            with torch.cuda.stream(cstream):
+                if i >= 2:
+                    cstream.wait_event(evs["in_free"][b])
+                d_x[b].copy_(h_x, non_blocking=True)
+                evs["in_ready"][b].record(cstream)
+        copy_in(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                copy_in(i + 1)
+            comp.wait_event(evs["in_ready"][b])
+            if i >= 2:
+                comp.wait_event(evs["out_done"][b])
+            graphs[b].replay()
+            evs["in_free"][b].record(comp)
+            evs["out_ready"][b].record(comp)
+            with torch.cuda.stream(cstream):
+                cstream.wait_event(evs["out_ready"][b])
+                h_q[b].copy_(d_q[b], non_blocking=True)
+                evs["out_done"][b].record(cstream)
+        comp.wait_event(evs["out_done"][(n - 1) % 2])
+
+    e2e_run(max(1, args.warmup))
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    cstream.wait_stream(comp)
+    e2e_run(args.steps)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    pool.raise_on_status()
+    del graphs
+    launches = launches_per_step * args.steps
+
+    prefill = tps > 1
+    ms_step = ms_total / args.steps
+    flops, nbytes = qkv_flops(w, n_tok), qkv_bytes(w, n_tok)
+    if prefill:
+        unit, per_launch, peak, peak_kind = "TFLOP/s", flops / 1e12, 1590.0, "fallback"
+        pk = REPO / "MEASURED_PEAKS.json"
+        if pk.exists():
+            try:
+                peak, peak_kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured"
+            except Exception:
+                pass
+    else:
+        unit, per_launch = "GB/s", nbytes / 1e9
+        peak, peak_kind = measured_peak_gbs()
+    value = world * L * per_launch / (ms_total * 1e-3 / args.steps)
+    e2e_value = world * L * per_launch / (e2e_ms * 1e-3 / args.steps)
+    achieved = per_launch / (launch_ms * 1e-3)
+    res = {
+        "metric": ("fused q/k/v projection + QK-norm + RoPE + KV append " +
+                   ("TFLOP/s" if prefill else "GB/s (weights + activations)")),
+        "value": round(value, 2),
+        "unit": unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,1/hidden) weights)",
+        "tok_per_s": round(world * n_tok / (ms_step * 1e-3), 1),
+        "config": {
+            "workload": f"{args.workload}: {w['model']} {L} layers, hidden {hidden}, {hq}q/{H}kv heads x d{d}, "
+                        f"per-head QK-norm, RoPE, bf16 pool; {B} sequences x {tps} new token(s) at position "
+                        f"{ctx0} per step, one sckv_qkv_append per layer",
+            "global_batch": world * n_tok,
+            "seq_len": tps,
+            "parallelism": f"sequence-sharded x{world}",
+            "l2": "weights of all layers (%.1f GB) >> L2; each layer's weights are read once per step"
+                  % (L * 2 * (hq + 2 * H) * d * hidden / 1e9),
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": int(h_x.numel() * 2),
+                "d2h_bytes_per_step": int(h_q[0].numel() * 2)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor" if prefill else "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "qkv_append_kernel + rope_table_kernel (+ qkv_finish_kernel when the hidden dim is "
+                               "split) per layer (CUDA-graph replay, step time / layers)",
+                     ("flops_per_launch" if prefill else "bytes_per_launch"): int(flops if prefill else nbytes),
+                     "avg_launch_ms": round(launch_ms, 4)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_qkv(w, prefill, budget_s=args.cpu_seconds)
+    pool.close()
+    return res
+
+
+def cpu_baseline_qkv(w, prefill: bool, budget_s: float = 15.0):
+    """The reference's NumPy projections + QK-norm + RoPE (oracle restatement of
+    models/adapters.py:1167-1194) on one layer x 32 tokens, repeated for ~budget_s."""
+    from oracle.kv_oracle import qk_norm_rope, qkv_project, rope_inv_freq
+
+    rng = np.random.default_rng(0)
+    n, hidden, hq, H, d = 32, w["hidden"], w["hq"], w["hkv"], w["d"]
+    x = rng.standard_normal((n, hidden)).astype(np.float32)
+    wq = (rng.standard_normal((hq * d, hidden)) * hidden ** -0.5).astype(np.float16)
+    wk = (rng.standard_normal((H * d, hidden)) * hidden ** -0.5).astype(np.float16)
+    wv = (rng.standard_normal((H * d, hidden)) * hidden ** -0.5).astype(np.float16)
+    qw, kw = np.ones(d, np.float16), np.ones(d, np.float16)
+    inv = rope_inv_freq(1e6, d)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        q, k, v = qkv_project(x, wq, wk, wv, hq, H)
+        qk_norm_rope(q, k, qw, kw, 1e-6, inv, 1.0, w["ctx"])
+        v.astype(np.float16)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    if prefill:
+        val, unit = reps * qkv_flops(w, n) / el / 1e12, "TFLOP/s"
+    else:
+        val, unit = reps * qkv_bytes(w, n) / el / 1e9, "GB/s"
+    return {"value": round(val, 5), "unit": unit, "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
+            or (os.cpu_count() or 1), "kind": "port",
+            "sample": f"1 layer x {n} tokens (fp32 x, fp16 weights), {reps} reps in {el:.1f}s"}
+
+
 # ----------------------------------------------------------------------------- continuous-batching mix
 class MixState:
     """A PagedKVCache driven like a serving loop, with exact host-side
@@ -909,12 +1146,27 @@ def bench_reference(args, w, world, rank):
     if rank != 0:
         return None
     steps = []
+    qkv = w.get("kind") == "qkv"
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(w, budget_s=args.cpu_seconds / max(1, args.steps))
+        if qkv:
+            r = cpu_baseline_qkv(w, w["tokens_per_seq"] > 1, budget_s=args.cpu_seconds / max(1, args.steps))
+        else:
+            r = cpu_baseline(w, budget_s=args.cpu_seconds / max(1, args.steps))
         if i >= args.warmup:
             steps.append(r["value"])
     val = float(np.mean(steps))
     cores = os.cpu_count() or 1
+    if qkv:
+        return {"metric": ("fused q/k/v projection + QK-norm + RoPE + KV append " +
+                           ("TFLOP/s" if w["tokens_per_seq"] > 1 else "GB/s (weights + activations)")),
+                "impl": "reference", "value": round(val, 5), "unit": r["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+                "config": {"workload": f"{args.workload}: reference NumPy projections + QK-norm + RoPE on a "
+                                       f"bounded host sample", "parallelism": "host cores"},
+                "cpu_baseline": {"value": round(val, 5), "unit": r["unit"], "cores": cores, "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": round(val, 5), "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     return {
         "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
         "impl": "reference",
@@ -955,6 +1207,8 @@ def main():
             res = bench_reference(args, w, world, rank)
         elif w.get("kind") == "mix":
             res = bench_mix(args, w, world, rank, local)
+        elif w.get("kind") == "qkv":
+            res = bench_qkv(args, w, world, rank, local)
         else:
             res = bench_ours(args, w, world, rank, local)
         if rank == 0 and res is not None:

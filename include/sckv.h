@@ -243,7 +243,10 @@ SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
  * w_q [num_q_heads*128][hidden], w_k / w_v [Hkv*128][hidden] row-major.
  * q_norm_len / k_norm_len: 0 or 128 (per-head fp16 weights); whole-width
  * norms return SCKV_ERR_UNSUPPORTED (use the projections + sckv_append_rope).
- * workspace: >= n_tokens * 512 bytes (the per-token cos / sin table).
+ * workspace: >= sckv_qkv_workspace_bytes(...) bytes: the per-token cos / sin
+ * table, plus fp32 partial sums when few token tiles make the kernel split
+ * the hidden dim across CTAs (a second, finishing launch then applies the
+ * norm, rotation and stores).
  * hidden % 8 == 0; x, x_lo, weights, q_out and workspace 16-byte aligned. */
 SCKV_API int sckv_qkv_append(sckv_pool* pool, int layer, const void* x,
                      const void* x_lo, int x_dtype, int n_tokens, int hidden,
@@ -255,6 +258,10 @@ SCKV_API int sckv_qkv_append(sckv_pool* pool, int layer, const void* x,
                      const int32_t* block_table, int64_t bt_stride,
                      int max_blocks, void* q_out, int q_out_dtype,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace sckv_qkv_append needs for this call shape (0 on bad arguments). */
+SCKV_API size_t sckv_qkv_workspace_bytes(const sckv_pool* pool, int n_tokens,
+                     int num_q_heads, int hidden);
 
 /* fp32 x -> hi = round(x), lo = round(x - hi) in F16 or BF16 (n elements):
  * the two-part input of sckv_qkv_append for fp32 activations. */

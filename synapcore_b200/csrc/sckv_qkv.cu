@@ -40,19 +40,24 @@ using namespace sckv_tc;
 namespace {
 
 constexpr int kQkvBM = 128;                      // tokens per tile (UMMA M)
-constexpr int kQkvBN = 128;                      // output dims per tile = one head (UMMA N)
+constexpr int kHead = 128;                       // head_dim: output dims of one head
 constexpr int kQkvBK = 64;                       // hidden elements per step: 128-byte rows
-constexpr int kQkvTile = kQkvBM * kQkvBK * 2;    // one operand tile: 16 KiB
+constexpr int kQkvTile = kQkvBM * kQkvBK * 2;    // one 128-row operand tile: 16 KiB
 constexpr int kQkvThreads = 192;
-constexpr uint32_t kQkvTmemCols = 128;
-constexpr int kQkvStages = 4;
 constexpr int kRopePairs = 64;                   // head_dim / 2
 
-template <bool kSplit>
-struct QkvSmem {
-  static constexpr int kStageBytes = (kSplit ? 3 : 2) * kQkvTile;  // x, W (, x_lo)
-  static constexpr int kBarOff = kQkvStages * kStageBytes;
-  static constexpr int kBytes = 1024 + kBarOff + (2 * kQkvStages + 1) * 8 + 16;
+// kHeads heads of one kind per CTA: UMMA N = 128 kHeads (256 halves the
+// shared-memory reads of x per flop; used when the grid still fills the GPU).
+template <bool kSplit, int kHeads>
+struct QkvCfg {
+  static constexpr int kBN = kHead * kHeads;
+  static constexpr int kStages = (kSplit && kHeads == 2) ? 3 : 4;
+  static constexpr int kStageBytes = (2 + kHeads - 1 + (kSplit ? 1 : 0)) * kQkvTile;  // x, W (, x_lo)
+  static constexpr int kOffW = kQkvTile;
+  static constexpr int kOffLo = kQkvTile * (1 + kHeads);
+  static constexpr int kBarOff = kStages * kStageBytes;
+  static constexpr int kBytes = 1024 + kBarOff + (2 * kStages + 1) * 8 + 16;
+  static constexpr uint32_t kTmemCols = kBN;
 };
 
 struct QkvParams {
@@ -62,6 +67,7 @@ struct QkvParams {
   const __half* q_norm_w;  // [128] or null
   const __half* k_norm_w;  // [128] or null
   const float2* rope_cs;   // [n_tok][64] (cos, sin)
+  float* partial;          // split-K: [k_splits][n_tok][hd_total] fp32 sums, else null
   const int32_t* cu;
   const int32_t* start_pos;
   const int32_t* bt;
@@ -76,8 +82,30 @@ struct QkvParams {
   int layer;
   int q_out_dtype;
   int pool_dtype;
+  int k_steps_per_split;  // hidden steps of 64 per blockIdx.z
+  int hd_total;           // (hq + 2 hkv) * 128 output columns
   float eps;
 };
+
+// Destination page row of token t (k / v): the slab (layer, page) of its
+// block, or -1 (out-of-range position or page, reported once per token by
+// the caller's choice of `report`).
+__device__ __forceinline__ int64_t token_slab(const QkvParams& p, int t, int* pos_out, bool report) {
+  const int b = sckv_find_seq(p.cu, p.n_seqs, t);
+  const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
+  *pos_out = pos;
+  const int blk = pos / SCKV_PAGE_TOKENS;
+  if (pos < 0 || blk >= p.max_blocks) {
+    if (report) sckv_report(p.status, SCKV_ERR_BOUNDS, pos < 0 ? pos : blk, KID_QKV);
+    return -1;
+  }
+  const int32_t page = __ldg(p.bt + (int64_t)b * p.bt_stride + blk);
+  if (page < 0 || page >= p.max_pages) {
+    if (report) sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_QKV);
+    return -1;
+  }
+  return (int64_t)p.layer * p.max_pages + page;
+}
 
 // cos / sin of every (token, frequency) pair: position start_pos[b] + i
 // divided by rope_scaling, times inv_freq[j], as sckv_append_rope computes
@@ -136,12 +164,70 @@ __device__ __forceinline__ void store32(void* dst, int64_t idx, int dtype, const
   }
 }
 
-template <bool kBF16, bool kSplit>
+// Split-K finish: one warp per (token, output head) adds the splits' fp32
+// sums, then applies the per-head RMSNorm, the rotation and the stores of
+// the fused epilogue. Lane i holds dims i, i + 32, i + 64, i + 96, so both
+// rotation pairs (i, i + 64) and (i + 32, i + 96) stay in the lane.
+__global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int k_splits) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int n_heads = p.hq + 2 * p.hkv;
+  if (wid >= (int64_t)p.n_tok * n_heads) return;
+  const int t = (int)(wid / n_heads), hidx = (int)(wid % n_heads);
+  const int kind = hidx < p.hq ? 0 : (hidx < p.hq + p.hkv ? 1 : 2);
+  const int head = kind == 0 ? hidx : (kind == 1 ? hidx - p.hq : hidx - p.hq - p.hkv);
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int z = 0; z < k_splits; ++z) {
+    const float* src = p.partial + ((int64_t)z * p.n_tok + t) * p.hd_total + (int64_t)hidx * kHead;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __fadd_rn(x[i], __ldg(src + lane + 32 * i));
+  }
+  const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
+  if (nw != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss = __fmaf_rn(x[i], x[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHead), p.eps)));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), __half2float(__ldg(nw + lane + 32 * i)));
+  }
+  float y[4] = {x[0], x[1], x[2], x[3]};
+  if (kind < 2) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + lane + 32 * i);
+      y[i] = __fsub_rn(__fmul_rn(x[i], cs.x), __fmul_rn(x[i + 2], cs.y));
+      y[i + 2] = __fadd_rn(__fmul_rn(x[i + 2], cs.x), __fmul_rn(x[i], cs.y));
+    }
+  }
+  int64_t dst;
+  void* out;
+  int out_dtype;
+  if (kind == 0) {
+    dst = ((int64_t)t * p.hq + head) * kHead;
+    out = p.q_out;
+    out_dtype = p.q_out_dtype;
+  } else {
+    int pos = 0;
+    const int64_t slab = token_slab(p, t, &pos, lane == 0 && head == 0);
+    if (slab < 0) return;
+    dst = (((slab * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kHead;
+    out = p.pool_data;
+    out_dtype = p.pool_dtype;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sckv_store_from_float(out, dst + lane + 32 * i, out_dtype, y[i]);
+}
+
+template <bool kBF16, bool kSplit, int kHeads>
 __global__ void __launch_bounds__(kQkvThreads, 1)
     qkv_append_kernel(const QkvParams p, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap xlomap, const __grid_constant__ CUtensorMap wqmap,
                       const __grid_constant__ CUtensorMap wkmap, const __grid_constant__ CUtensorMap wvmap) {
-  using SM = QkvSmem<kSplit>;
+  using SM = QkvCfg<kSplit, kHeads>;
+  constexpr int kQkvStages = SM::kStages;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(base + SM::kBarOff);  // [S] stage landed (TMA)
@@ -152,9 +238,16 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n = blockIdx.x;  // output head: q heads, then k heads, then v heads
+  // output head group: groups of q heads, then of k heads, then of v heads
+  const int gq = (p.hq + kHeads - 1) / kHeads, gk = (p.hkv + kHeads - 1) / kHeads;
+  const int kind = blockIdx.x < gq ? 0 : (blockIdx.x < gq + gk ? 1 : 2);  // q, k, v
+  const int head0 = (blockIdx.x - (kind == 0 ? 0 : (kind == 1 ? gq : gq + gk))) * kHeads;
+  const int kind_heads = kind == 0 ? p.hq : p.hkv;
   const int m0 = blockIdx.y * kQkvBM;
-  const int nk = (p.hidden + kQkvBK - 1) / kQkvBK;
+  // hidden steps s0 .. s0 + nk - 1 of 64 (all of them unless split over blockIdx.z)
+  const int nk_all = (p.hidden + kQkvBK - 1) / kQkvBK;
+  const int s0 = blockIdx.z * p.k_steps_per_split;
+  const int nk = min(nk_all - s0, p.k_steps_per_split);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQkvStages; ++i) {
@@ -165,7 +258,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kQkvTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, SM::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -174,8 +267,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const CUtensorMap* wmap = n < p.hq ? &wqmap : (n < p.hq + p.hkv ? &wkmap : &wvmap);
-      const int row0 = (n < p.hq ? n : (n < p.hq + p.hkv ? n - p.hq : n - p.hq - p.hkv)) * kQkvBN;
+      const CUtensorMap* wmap = kind == 0 ? &wqmap : (kind == 1 ? &wkmap : &wvmap);
+      const int row0 = head0 * kHead;  // rows past the last head read as zeros
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap)) : "memory");
       int issued = 0;
@@ -183,16 +276,17 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         const int st = s % kQkvStages;
         if (s >= kQkvStages) {
           if (*abort_flag || !mbar_wait_bounded(&empty[st], ((s / kQkvStages) - 1) & 1, SCKV_WAIT_LIMIT_NS)) {
-            if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, n, KID_QKV);
+            if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_QKV);
             *abort_flag = 1;
             break;
           }
         }
         const uint32_t stage = smem_u32(base + st * SM::kStageBytes);
         mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
-        tma_load_2d(stage, &xmap, s * kQkvBK, m0, &full[st]);
-        tma_load_2d(stage + kQkvTile, wmap, s * kQkvBK, row0, &full[st]);
-        if (kSplit) tma_load_2d(stage + 2 * kQkvTile, &xlomap, s * kQkvBK, m0, &full[st]);
+        const int kx = (s0 + s) * kQkvBK;
+        tma_load_2d(stage, &xmap, kx, m0, &full[st]);
+        tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
+        if (kSplit) tma_load_2d(stage + SM::kOffLo, &xlomap, kx, m0, &full[st]);
         ++issued;
       }
       // copies still in flight land before the CTA may exit
@@ -201,7 +295,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t kIdesc = instr_desc_f16(kBF16, kQkvBN, false);
+    constexpr uint32_t kIdesc = instr_desc_f16(kBF16, SM::kBN, false);
     bool ok = true;
     for (int s = 0; s < nk; ++s) {
       const int st = s % kQkvStages;
@@ -212,21 +306,21 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t a = smem_u32(base + st * SM::kStageBytes);
-        const uint32_t b = a + kQkvTile;
+        const uint32_t b = a + SM::kOffW;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           // A = x rows (tokens), B = W rows (output dims), both K-major:
           // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
           const uint64_t bdesc = smem_desc_sw128(b + kk * 32, 16, 1024);
           umma_ss(tmem, smem_desc_sw128(a + kk * 32, 16, 1024), bdesc, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
-          if (kSplit) umma_ss(tmem, smem_desc_sw128(a + 2 * kQkvTile + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
+          if (kSplit) umma_ss(tmem, smem_desc_sw128(a + SM::kOffLo + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
         }
         umma_commit(&empty[st]);
       }
       __syncwarp();
     }
     if (!ok) {
-      if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, n, KID_QKV);
+      if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_QKV);
       if (lane == 0) *abort_flag = 1;
     }
     // fires once every MMA issued above has finished (at once if none was)
@@ -241,87 +335,99 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     tc_fence_after();
     // warp-uniform: the tensor-memory loads below are warp-wide
     const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
-    if (ready && !aborted) {
-      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-      const int kind = n < p.hq ? 0 : (n < p.hq + p.hkv ? 1 : 2);  // q, k, v
-      const int head = kind == 0 ? n : (kind == 1 ? n - p.hq : n - p.hq - p.hkv);
-      const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
-      // every lane reads the tensor memory (the loads are warp-wide); rows
-      // past the last token are computed and dropped
-      float inv = 1.f;
-      if (nw != nullptr) {
-        float ss = 0.f;
-#pragma unroll
+    if (ready && !aborted && p.partial != nullptr) {
+      // split-K: raw fp32 sums of this split; qkv_finish_kernel adds the
+      // splits and applies the norm, rotation and stores
+#pragma unroll 1
+      for (int hh = 0; hh < kHeads; ++hh) {
+        const int head = head0 + hh;
+        if (head >= kind_heads) break;  // warp-uniform
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(hh * kHead);
+        const int col0 = (kind == 0 ? 0 : (kind == 1 ? p.hq : p.hq + p.hkv) * kHead) + head * kHead;
+        float* dst = p.partial + ((int64_t)blockIdx.z * p.n_tok + t) * p.hd_total + col0;
+#pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tmem_ld32(trow + c * 32, r);
           tc_wait_ld();
+          if (t < p.n_tok) {
+            float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float x = __uint_as_float(r[i]);
-            ss = __fmaf_rn(x, x, ss);
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                  __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
           }
         }
-        inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kQkvBN), p.eps)));
       }
+    } else if (ready && !aborted) {
+      const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
       const bool live = t < p.n_tok;
-      int64_t dst = -1;
-      void* out = p.q_out;
-      int out_dtype = p.q_out_dtype;
-      if (live) {
-        if (kind == 0) {
-          dst = ((int64_t)t * p.hq + head) * kQkvBN;
-        } else {
-          const int b = sckv_find_seq(p.cu, p.n_seqs, t);
-          const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
-          const int blk = pos / SCKV_PAGE_TOKENS;
-          int32_t page = -1;
-          if (pos < 0 || blk >= p.max_blocks) {
-            sckv_report(p.status, SCKV_ERR_BOUNDS, pos < 0 ? pos : blk, KID_QKV);
-          } else {
-            page = __ldg(p.bt + (int64_t)b * p.bt_stride + blk);
-            if (page < 0 || page >= p.max_pages) {
-              sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_QKV);
-              page = -1;
+      // the token's page slab (k and v tiles); q rows go to q_out
+      int pos = 0;
+      const int64_t slot_row = (live && kind > 0) ? token_slab(p, t, &pos, head0 == 0) : -1;
+#pragma unroll 1
+      for (int hh = 0; hh < kHeads; ++hh) {
+        const int head = head0 + hh;
+        if (head >= kind_heads) break;  // warp-uniform
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(hh * kHead);
+        // every lane reads the tensor memory (the loads are warp-wide); rows
+        // past the last token are computed and dropped
+        float inv = 1.f;
+        if (nw != nullptr) {
+          float ss = 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(trow + c * 32, r);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float x = __uint_as_float(r[i]);
+              ss = __fmaf_rn(x, x, ss);
             }
           }
-          if (page >= 0) {
-            // data layout [L][P][K|V][H][16][D]
-            const int64_t slab = (int64_t)p.layer * p.max_pages + page;
-            dst = (((slab * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kQkvBN;
-          }
+          inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHead), p.eps)));
+        }
+        int64_t dst = -1;
+        void* out = p.q_out;
+        int out_dtype = p.q_out_dtype;
+        if (live && kind == 0) {
+          dst = ((int64_t)t * p.hq + head) * kHead;
+        } else if (slot_row >= 0) {
+          // data layout [L][P][K|V][H][16][D]
+          dst = (((slot_row * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kHead;
           out = p.pool_data;
           out_dtype = p.pool_dtype;
         }
-      }
 #pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {
-        // dims d = 32 hf + i and their rotation partners d + 64
-        uint32_t r1[32], r2[32];
-        tmem_ld32(trow + hf * 32, r1);
-        tmem_ld32(trow + 64 + hf * 32, r2);
-        tc_wait_ld();
-        if (dst < 0) continue;
-        float y1[32], y2[32];
+        for (int hf = 0; hf < 2; ++hf) {
+          // dims d = 32 hf + i and their rotation partners d + 64
+          uint32_t r1[32], r2[32];
+          tmem_ld32(trow + hf * 32, r1);
+          tmem_ld32(trow + 64 + hf * 32, r2);
+          tc_wait_ld();
+          if (dst < 0) continue;
+          float y1[32], y2[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int d = hf * 32 + i;
-          float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
-          if (nw != nullptr) {
-            x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
-            x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
+          for (int i = 0; i < 32; ++i) {
+            const int d = hf * 32 + i;
+            float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
+            if (nw != nullptr) {
+              x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
+              x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
+            }
+            if (kind < 2) {
+              const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + d);
+              y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+              y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+            } else {
+              y1[i] = x1;
+              y2[i] = x2;
+            }
           }
-          if (kind < 2) {
-            const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + d);
-            y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-            y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-          } else {
-            y1[i] = x1;
-            y2[i] = x2;
-          }
+          store32(out, dst + hf * 32, out_dtype, y1);
+          store32(out, dst + 64 + hf * 32, out_dtype, y2);
         }
-        store32(out, dst + hf * 32, out_dtype, y1);
-        store32(out, dst + 64 + hf * 32, out_dtype, y2);
       }
     }
   }
@@ -329,17 +435,17 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kQkvTmemCols);
+    tmem_dealloc(tmem, SM::kTmemCols);
   }
 }
 
-// 2-D map over a row-major [rows][hidden] 16-bit matrix, boxes of 64 x 128.
-int encode_rows(CUtensorMap* map, const void* ptr, int rows, int hidden, bool bf16) {
+// 2-D map over a row-major [rows][hidden] 16-bit matrix, boxes of 64 x box_rows.
+int encode_rows(CUtensorMap* map, const void* ptr, int rows, int hidden, bool bf16, int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return SCKV_ERR_CUDA;
   const cuuint64_t dims[2] = {(cuuint64_t)hidden, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)hidden * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kQkvBK, (cuuint32_t)kQkvBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kQkvBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -348,20 +454,49 @@ int encode_rows(CUtensorMap* map, const void* ptr, int rows, int hidden, bool bf
   return r == CUDA_SUCCESS ? SCKV_OK : sckv_record_error(__FILE__, __LINE__, "cuTensorMapEncodeTiled", "failed");
 }
 
-template <bool kBF16, bool kSplit>
-int launch_qkv(const QkvParams& prm, const CUtensorMap (&maps)[5], int n_heads, int m_tiles, cudaStream_t stream) {
-  auto kern = qkv_append_kernel<kBF16, kSplit>;
-  constexpr int smem = QkvSmem<kSplit>::kBytes;
+template <bool kBF16, bool kSplit, int kHeads>
+int launch_qkv(const QkvParams& prm, const CUtensorMap (&maps)[5], int n_groups, int m_tiles, cudaStream_t stream,
+               int k_splits = 1) {
+  auto kern = qkv_append_kernel<kBF16, kSplit, kHeads>;
+  constexpr int smem = QkvCfg<kSplit, kHeads>::kBytes;
   static_assert(smem <= 227 * 1024, "shared memory");
   SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kern<<<dim3(n_heads, m_tiles), kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3], maps[4]);
+  kern<<<dim3(n_groups, m_tiles, k_splits), kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3],
+                                                                         maps[4]);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Hidden steps per split: the whole hidden dim when the token tiles x heads
+// already give every other SM a CTA, else split so about one CTA per SM
+// streams a slice of the weights (at least 4 steps of 64 per split).
+int qkv_steps_per_split(int64_t n_tokens, int64_t n_heads, int hidden, int num_sms) {
+  const int nk = (hidden + kQkvBK - 1) / kQkvBK;
+  const int64_t ctas = ((n_tokens + kQkvBM - 1) / kQkvBM) * n_heads;
+  if (ctas * 2 > num_sms || nk < 8) return nk;
+  int64_t ks = num_sms / ctas;
+  ks = ks < 2 ? 2 : (ks > 8 ? 8 : ks);
+  if (ks > nk / 4) ks = nk / 4;
+  return (int)((nk + ks - 1) / ks);
+}
+
+size_t qkv_workspace_bytes(int64_t n_tokens, int64_t n_heads, int hidden, int num_sms) {
+  const int per = qkv_steps_per_split(n_tokens, n_heads, hidden, num_sms);
+  const int nk = (hidden + kQkvBK - 1) / kQkvBK;
+  const int64_t ks = (nk + per - 1) / per;
+  size_t b = (size_t)n_tokens * kRopePairs * sizeof(float2);
+  if (ks > 1) b += (size_t)ks * n_tokens * n_heads * kHead * sizeof(float);
+  return b;
+}
+
 }  // namespace
+
+extern "C" size_t sckv_qkv_workspace_bytes(const sckv_pool* pool, int n_tokens, int num_q_heads, int hidden) {
+  if (pool == nullptr || n_tokens < 0 || num_q_heads <= 0 || hidden <= 0) return 0;
+  return qkv_workspace_bytes(n_tokens, (int64_t)num_q_heads + 2LL * pool->num_kv_heads, hidden, pool->num_sms);
+}
 
 extern "C" int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo, int dtype, void* stream) {
   if (n < 0 || (n > 0 && (!x || !hi || !lo))) return SCKV_ERR_INVALID_ARG;
@@ -387,10 +522,10 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (q_out_dtype != SCKV_DTYPE_F32 && q_out_dtype != SCKV_DTYPE_F16 && q_out_dtype != SCKV_DTYPE_BF16)
     return SCKV_ERR_INVALID_ARG;
   if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
-  if (pool->head_dim != kQkvBN) return SCKV_ERR_UNSUPPORTED;
+  if (pool->head_dim != kHead) return SCKV_ERR_UNSUPPORTED;
   // norms over the whole projection need every head of a token: the
   // unfused path (projection, then sckv_append_rope) covers them
-  if ((q_norm_len != 0 && q_norm_len != kQkvBN) || (k_norm_len != 0 && k_norm_len != kQkvBN))
+  if ((q_norm_len != 0 && q_norm_len != kHead) || (k_norm_len != 0 && k_norm_len != kHead))
     return SCKV_ERR_UNSUPPORTED;
   if ((q_norm_len != 0 && q_norm_w == nullptr) || (k_norm_len != 0 && k_norm_w == nullptr))
     return SCKV_ERR_INVALID_ARG;
@@ -399,7 +534,9 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (!x || !w_q || !w_k || !w_v || !inv_freq || !cu_tokens || !start_pos || !block_table || !q_out ||
       !workspace || max_blocks <= 0 || bt_stride < max_blocks || !(rope_scaling != 0.f))
     return SCKV_ERR_INVALID_ARG;
-  if (workspace_bytes < (size_t)n_tokens * kRopePairs * sizeof(float2)) return SCKV_ERR_INVALID_ARG;
+  if (workspace_bytes < qkv_workspace_bytes(n_tokens, (int64_t)num_q_heads + 2LL * pool->num_kv_heads, hidden,
+                                            pool->num_sms))
+    return SCKV_ERR_INVALID_ARG;
   if (!aligned16(x) || (x_lo && !aligned16(x_lo)) || !aligned16(w_q) || !aligned16(w_k) || !aligned16(w_v) ||
       !aligned16(q_out) || !aligned16(workspace))
     return SCKV_ERR_ALIGNMENT;
@@ -407,15 +544,24 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   const int64_t n_heads = (int64_t)num_q_heads + 2LL * hkv;
   const int64_t m_tiles = ((int64_t)n_tokens + kQkvBM - 1) / kQkvBM;
   if (n_heads > INT32_MAX || m_tiles > 65535) return SCKV_ERR_UNSUPPORTED;
-  if ((int64_t)num_q_heads * kQkvBN > INT32_MAX || (int64_t)hkv * kQkvBN > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
+  if ((int64_t)num_q_heads * kHead > INT32_MAX || (int64_t)hkv * kHead > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
+
+  // two heads per CTA (N = 256) once that still gives every SM a tile;
+  // split over the hidden dim when even one head per CTA leaves SMs idle
+  const int64_t groups2 = (num_q_heads + 1) / 2 + 2 * ((hkv + 1) / 2);
+  const int per_split = qkv_steps_per_split(n_tokens, n_heads, hidden, pool->num_sms);
+  const int nk = (hidden + kQkvBK - 1) / kQkvBK;
+  const int k_splits = (nk + per_split - 1) / per_split;
+  const int heads = (k_splits == 1 && groups2 * m_tiles >= pool->num_sms) ? 2 : 1;
+  const int n_groups = heads == 2 ? (int)groups2 : (int)n_heads;
 
   const bool bf16 = x_dtype == SCKV_DTYPE_BF16;
   CUtensorMap maps[5];
-  int rc = encode_rows(&maps[0], x, n_tokens, hidden, bf16);
-  if (rc == SCKV_OK) rc = encode_rows(&maps[1], x_lo ? x_lo : x, n_tokens, hidden, bf16);
-  if (rc == SCKV_OK) rc = encode_rows(&maps[2], w_q, num_q_heads * kQkvBN, hidden, bf16);
-  if (rc == SCKV_OK) rc = encode_rows(&maps[3], w_k, hkv * kQkvBN, hidden, bf16);
-  if (rc == SCKV_OK) rc = encode_rows(&maps[4], w_v, hkv * kQkvBN, hidden, bf16);
+  int rc = encode_rows(&maps[0], x, n_tokens, hidden, bf16, kQkvBM);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[1], x_lo ? x_lo : x, n_tokens, hidden, bf16, kQkvBM);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[2], w_q, num_q_heads * kHead, hidden, bf16, heads * kHead);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[3], w_k, hkv * kHead, hidden, bf16, heads * kHead);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[4], w_v, hkv * kHead, hidden, bf16, heads * kHead);
   if (rc != SCKV_OK) return rc;
 
   cudaStream_t s = as_stream(stream);
@@ -448,10 +594,29 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.q_out_dtype = q_out_dtype;
   prm.pool_dtype = pool->kv_dtype;
   prm.eps = eps;
-  if (bf16) {
-    return x_lo ? launch_qkv<true, true>(prm, maps, (int)n_heads, (int)m_tiles, s)
-                : launch_qkv<true, false>(prm, maps, (int)n_heads, (int)m_tiles, s);
+  prm.k_steps_per_split = per_split;
+  prm.hd_total = (int)(n_heads * kHead);
+  prm.partial = k_splits > 1 ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                                         (size_t)n_tokens * kRopePairs * sizeof(float2))
+                             : nullptr;
+  const int mt = (int)m_tiles;
+  if (k_splits > 1) {
+    rc = x_lo ? (bf16 ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, s, k_splits)
+                      : launch_qkv<false, true, 1>(prm, maps, n_groups, mt, s, k_splits))
+              : (bf16 ? launch_qkv<true, false, 1>(prm, maps, n_groups, mt, s, k_splits)
+                      : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, s, k_splits));
+    if (rc != SCKV_OK) return rc;
+    const int64_t warps = (int64_t)n_tokens * n_heads;
+    qkv_finish_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(prm, k_splits);
+    SCKV_LAUNCH_CHECK();
+    return SCKV_OK;
   }
-  return x_lo ? launch_qkv<false, true>(prm, maps, (int)n_heads, (int)m_tiles, s)
-              : launch_qkv<false, false>(prm, maps, (int)n_heads, (int)m_tiles, s);
+  if (heads == 2) {
+    if (bf16)
+      return x_lo ? launch_qkv<true, true, 2>(prm, maps, n_groups, mt, s) : launch_qkv<true, false, 2>(prm, maps, n_groups, mt, s);
+    return x_lo ? launch_qkv<false, true, 2>(prm, maps, n_groups, mt, s) : launch_qkv<false, false, 2>(prm, maps, n_groups, mt, s);
+  }
+  if (bf16)
+    return x_lo ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, s) : launch_qkv<true, false, 1>(prm, maps, n_groups, mt, s);
+  return x_lo ? launch_qkv<false, true, 1>(prm, maps, n_groups, mt, s) : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, s);
 }

@@ -306,7 +306,8 @@ class KVPool:
             _need(q_out, "q_out", self.device)
             if tuple(q_out.shape) != (nt, hq, d):
                 raise ValueError("q_out must be [n_tokens, Hq, D]")
-        ws = torch.empty(max(1, nt) * (d // 2) * 2, dtype=torch.float32, device=self.device)
+        ws_bytes = int(self.lib.sckv_qkv_workspace_bytes(self.handle, nt, hq, hidden))
+        ws = torch.empty(max(16, ws_bytes) // 4 + 4, dtype=torch.float32, device=self.device)
         (qw, qn), (kw, kn) = norms
         N.check(self.lib.sckv_qkv_append(self.handle, layer, x.data_ptr(), _ptr(x_lo), torch_dtype_code(x.dtype), nt,
                                          hidden, w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr(), hq, _ptr(qw), qn,

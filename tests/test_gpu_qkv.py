@@ -100,15 +100,24 @@ def _run_case(dev, kv_dtype, wdt, x_kind, hq, hkv, hidden, Ts, starts, norm, q_o
 
 
 @pytest.mark.parametrize("kv_dtype,wdt,x_kind,norm,hq,hkv,hidden", [
-    ("fp16", torch.float16, "f32", "head", 8, 2, 520),     # fp32 x split hi + lo; hidden not a multiple of 64
+    ("fp16", torch.float16, "f32", "head", 8, 2, 520),     # fp32 x as hi + lo; hidden % 64 != 0; 2-way split
     ("fp16", torch.float16, "16", None, 4, 4, 256),        # MHA, f16 x, no norm
     ("bf16", torch.bfloat16, "16", "head", 16, 4, 384),
     ("bf16", torch.bfloat16, "f32", None, 8, 1, 128),      # MQA
     ("fp16", torch.float16, "f32", "full", 8, 2, 256),     # whole-width norm: unfused route
+    ("bf16", torch.bfloat16, "f32", "head", 4, 2, 2048),   # few tiles: hidden split 8 ways + finishing launch
 ])
 def test_qkv_append_matches_oracle(cuda_device, kv_dtype, wdt, x_kind, norm, hq, hkv, hidden):
     Ts, starts = [5, 130, 1, 0, 77], [0, 16, 300, 4, 9]   # 213 tokens: two token tiles, the second partial
     _run_case(cuda_device, kv_dtype, wdt, x_kind, hq, hkv, hidden, Ts, starts, norm)
+
+
+@pytest.mark.parametrize("wdt,x_kind", [(torch.bfloat16, "16"), (torch.float16, "f32")])
+def test_qkv_append_two_heads_per_tile_with_odd_head_counts(cuda_device, wdt, x_kind):
+    """1,600 tokens give enough tiles for two heads per CTA (N = 256); odd
+    head counts leave the last group one head short."""
+    kv = "bf16" if wdt == torch.bfloat16 else "fp16"
+    _run_case(cuda_device, kv, wdt, x_kind, 15, 3, 192, [700, 900], [3, 40], "head", seed=9)
 
 
 @pytest.mark.parametrize("q_out_dtype", [torch.float16, torch.bfloat16])
