@@ -64,6 +64,11 @@ WORKLOADS = {
                         qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
     "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                             qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
+    # config 4 with the reference arena's int8 mode (per-token fp16 scales)
+    "qwen3-int8": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="int8",
+                       qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
+    "qwen3-int8-1l": dict(model="Qwen3-8B attention", layers=1, hq=32, hkv=8, d=128, kv="int8",
+                          qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
     # one layer of the full config-4 launch (4.3 GB), for whole-launch captures
     "qwen3-fp8-1l": dict(model="Qwen3-8B attention", layers=1, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                          qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
@@ -112,7 +117,11 @@ def attn_bytes_per_launch(w, ctx=None) -> int:
     pages = (c + PAGE - 1) // PAGE
     b = kv_bytes_per_elem(w["kv"])
     kv = int(c.sum()) * hkv * d * 2 * b
-    scales = int(pages.sum()) * hkv * 2 * 4 if w["kv"] == "fp8_e4m3" else 0
+    scales = 0
+    if w["kv"] == "fp8_e4m3":
+        scales = int(pages.sum()) * hkv * 2 * 4          # one fp32 scale per (page, head, K|V)
+    elif w["kv"] == "int8":
+        scales = int(c.sum()) * hkv * 2 * 2             # one fp16 scale per (token, head, K|V)
     bt = int(pages.sum()) * 4
     qo = len(c) * hq * d * 2 * 2
     return kv + scales + bt + qo
@@ -299,6 +308,15 @@ def build_state(w, rank: int, grow_steps: int = 0):
                 blk.copy_(codes)
                 del codes
         pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
+    elif w["kv"] == "int8":
+        # codes U{-127..127} and per-(token, head) fp16 scales ~ max|x| / 127 of N(0,1)*U[0.5,4] rows
+        for l in range(n_phys):
+            for c0 in range(0, pool_pages, 8192):
+                blk = view[l, c0:c0 + 8192]
+                blk.copy_(torch.randint(-127, 128, blk.shape, dtype=torch.int8, device=dev, generator=g))
+        sv = pool.scale_view()
+        for l in range(n_phys):
+            sv[l].uniform_(1.5 / 127, 12.0 / 127, generator=g)
     else:
         for l in range(n_phys):
             for c0 in range(0, pool_pages, 8192):

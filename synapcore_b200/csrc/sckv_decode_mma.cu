@@ -44,8 +44,10 @@ struct MmaSmem {
   static constexpr int kRingBytes = S * kStageBytes;
   static constexpr int kG = 8 * NQT;                 // q rows per tile
   static constexpr int kRedFloats = kConsumerWarps * kG * (kHD + 2);
-  static constexpr int kScaleSlot = 64;              // floats per stage (2*H <= 64)
-  static constexpr int kScaleBytes = (KVDT == SCKV_DTYPE_FP8_E4M3) ? S * kScaleSlot * 4 : 0;
+  static constexpr int kScaleSlot = 64;              // FP8: floats per stage (2*H <= 64)
+  static constexpr int kTokScaleSlot = 2 * HG * SCKV_PAGE_TOKENS;  // int8: halfs per stage (K, V of HG heads)
+  static constexpr int kScaleBytes = (KVDT == SCKV_DTYPE_FP8_E4M3) ? S * kScaleSlot * 4
+                                     : (KVDT == SCKV_DTYPE_INT8) ? S * kTokScaleSlot * 2 : 0;
   static constexpr int kBytes = 1024 + kRingBytes + kScaleBytes + 2 * S * 8 + kRedFloats * 4 + 16;
 };
 
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
   using SM = MmaSmem<KVDT, NQT, HG, S>;
   constexpr bool kBF16 = (KVDT == SCKV_DTYPE_BF16);
   constexpr bool kFP8 = (KVDT == SCKV_DTYPE_FP8_E4M3);
+  constexpr bool kINT8 = (KVDT == SCKV_DTYPE_INT8);
+  constexpr bool kB8 = kFP8 || kINT8;  // one-byte codes, decoded in registers
   constexpr int kG = SM::kG;
   constexpr int kWPH = kConsumerWarps / HG;  // consumer warps per head
   // Pages go to the kWPH warps of a head in turn (page i -> warp i % kWPH) and
@@ -73,7 +77,9 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // swizzled TMA destinations need 1024-byte alignment
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* sscale = reinterpret_cast<float*>(ring + SM::kRingBytes);  // [S][kScaleSlot]: K scales of all heads, then V
+  float* sscale = reinterpret_cast<float*>(ring + SM::kRingBytes);  // FP8 [S][kScaleSlot]: K scales of all heads, then V
+  // int8 [S][K|V][HG][16]: per-token fp16 scales of this group's heads
+  const __half* stok = reinterpret_cast<const __half*>(ring + SM::kRingBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + SM::kRingBytes + SM::kScaleBytes);
   uint64_t* empty = full + S;
   float* red = reinterpret_cast<float*>(empty + S);
@@ -103,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
     uint32_t gcount = 0;
     bool aborted = false;
-    const uint32_t tx = SM::kStageBytes + (kFP8 ? 8 * p.hkv : 0);
+    const uint32_t tx = SM::kStageBytes + (kFP8 ? 8 * p.hkv : 0) + (kINT8 ? SM::kTokScaleSlot * 2 : 0);
     for (int item = blockIdx.x; item < n_items && !aborted; item += gridDim.x) {
       const int split = item / per_split;
       const int rem = item - split * per_split;
@@ -137,6 +143,14 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         mbar_arrive_expect_tx(&full[st], tx);
         if (kFP8)  // K and V scales of every head of this (layer, page): 8*H contiguous bytes
           bulk_g2s(sscale + st * SM::kScaleSlot, p.fp8_scales + (int64_t)slab * 2 * p.hkv, 8 * p.hkv, &full[st]);
+        if (kINT8) {
+          // scales [layer][page][K|V][head][16 tokens] fp16: the group's HG heads are 32 * HG
+          // contiguous bytes for K and again for V
+          const uint8_t* sb = reinterpret_cast<const uint8_t*>(p.fp8_scales);
+          uint8_t* sd = ring + SM::kRingBytes + st * SM::kTokScaleSlot * 2;
+          bulk_g2s(sd, sb + ((int64_t)slab * 2 * p.hkv + h0) * 32, HG * 32, &full[st]);
+          bulk_g2s(sd + HG * 32, sb + (((int64_t)slab * 2 + 1) * p.hkv + h0) * 32, HG * 32, &full[st]);
+        }
 #pragma unroll
         for (int bx = 0; bx < SM::kBoxes; ++bx)
           tma_load_5d(dst + bx * SM::kBoxStride, &tmap, bx * (128 / MmaKV<KVDT>::kEB), 0, h0, 0, slab, &full[st]);
@@ -177,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
       const int64_t qoff = ((int64_t)b * p.hq + (int64_t)h * G + qr) * kHD;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
-        const int d0 = kFP8 ? 16 * s + 4 * t : 16 * s + 2 * t;
-        const int d1 = kFP8 ? d0 + 2 : d0 + 8;
+        const int d0 = kB8 ? 16 * s + 4 * t : 16 * s + 2 * t;
+        const int d1 = kB8 ? d0 + 2 : d0 + 8;
         float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
         if (qr < G) {
           v0 = sckv_load_as_float(p.q, qoff + d0, p.q_dtype);
@@ -220,9 +234,17 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         const uint32_t sK = stage + hg * kBoxBytes;         // K of head hg, column block 0
         const uint32_t sV = stage + (HG + hg) * kBoxBytes;  // V of head hg, column block 0
         const int nv = min(SCKV_PAGE_TOKENS, ctx - (j0 + i) * SCKV_PAGE_TOKENS);
+        float ksA = 1.f, ksB = 1.f, vsA = 1.f, vsB = 1.f;  // int8: scales of tokens g, g + 8
         if (kFP8) {
           kscale = sscale[st * SM::kScaleSlot + h];
           vscale = sscale[st * SM::kScaleSlot + p.hkv + h];
+        }
+        if (kINT8) {
+          const __half* ts = stok + st * SM::kTokScaleSlot;
+          ksA = __half2float(ts[hg * SCKV_PAGE_TOKENS + g]);
+          ksB = __half2float(ts[hg * SCKV_PAGE_TOKENS + g + 8]);
+          vsA = __half2float(ts[(HG + hg) * SCKV_PAGE_TOKENS + g]);
+          vsB = __half2float(ts[(HG + hg) * SCKV_PAGE_TOKENS + g + 8]);
         }
 
         // ---------------- S^T = K . Q^T (two accumulators to halve the MMA chain)
@@ -233,19 +255,19 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
           for (int c = 0; c < 4; ++c) sc[nq][c] = sc2[nq][c] = 0.f;
         {
           const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-          if (kFP8) {
+          if (kB8) {
 #pragma unroll
             for (int c2 = 0; c2 < 4; ++c2) {
               const int chunk = 2 * c2 + (lane >> 4);
               uint32_t w0, w1, w2, w3;
               ldsm_x4(sK + row * 128 + ((chunk ^ (row & 7)) << 4), w0, w1, w2, w3);
               uint32_t a[4];
-              cvt_fp8x4(w0, a[0], a[2]);
-              cvt_fp8x4(w1, a[1], a[3]);
+              cvt_b8x4<KVDT>(w0, a[0], a[2]);
+              cvt_b8x4<KVDT>(w1, a[1], a[3]);
 #pragma unroll
               for (int nq = 0; nq < NQT; ++nq) mma16816<false>(sc[nq], a, qf[nq][2 * c2][0], qf[nq][2 * c2][1]);
-              cvt_fp8x4(w2, a[0], a[2]);
-              cvt_fp8x4(w3, a[1], a[3]);
+              cvt_b8x4<KVDT>(w2, a[0], a[2]);
+              cvt_b8x4<KVDT>(w3, a[1], a[3]);
 #pragma unroll
               for (int nq = 0; nq < NQT; ++nq)
                 mma16816<false>(sc2[nq], a, qf[nq][2 * c2 + 1][0], qf[nq][2 * c2 + 1][1]);
@@ -270,15 +292,17 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         // the accumulator rescale is rare. Every lane tests its own scores
         // against the (column-uniform) reference; the column max over the 8
         // lanes of a q column is reduced only when some score crossed it.
-        const float sscale = p.scale_log2 * kscale;
+        // int8: the per-token K scale multiplies its score row (tokens g, g + 8)
+        const float sscaleA = p.scale_log2 * kscale * ksA;
+        const float sscaleB = p.scale_log2 * kscale * ksB;
         float sv[NQT][4];
         bool grow = false;
 #pragma unroll
         for (int nq = 0; nq < NQT; ++nq) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const float sA = (g < nv) ? (sc[nq][c] + sc2[nq][c]) * sscale : -INFINITY;
-            const float sB = (g + 8 < nv) ? (sc[nq][2 + c] + sc2[nq][2 + c]) * sscale : -INFINITY;
+            const float sA = (g < nv) ? (sc[nq][c] + sc2[nq][c]) * sscaleA : -INFINITY;
+            const float sB = (g + 8 < nv) ? (sc[nq][2 + c] + sc2[nq][2 + c]) * sscaleB : -INFINITY;
             sv[nq][c] = sA;
             sv[nq][2 + c] = sB;
             grow |= (fmaxf(sA, sB) > m[nq][c] + 8.f);
@@ -327,6 +351,36 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
             pscale = 1.f;
           }
         }
+        // P multipliers of rows g and g + 8: FP8 the page's V-scale ratio;
+        // int8 each token's V scale over the item's reference (token 0 of
+        // the first page), moved to the page's largest live scale when a
+        // ratio passes 64 so P stays in f16 range; 0 for masked rows
+        float pscaleA = pscale, pscaleB = pscale;
+        if (kINT8) {
+          const __half* tv = stok + st * SM::kTokScaleSlot + (HG + hg) * SCKV_PAGE_TOKENS;
+          if (vref == 0.f) {
+            const float v0 = __half2float(tv[0]);
+            vref = (v0 > 0.f) ? v0 : 1.f;
+            inv_vref = 1.f / vref;
+          }
+          pscaleA = (g < nv) ? vsA * inv_vref : 0.f;
+          pscaleB = (g + 8 < nv) ? vsB * inv_vref : 0.f;
+          if (__any_sync(0xffffffffu, pscaleA > 64.f || pscaleB > 64.f)) {
+            float vmax = 0.f;
+            for (int i = 0; i < nv; ++i) vmax = fmaxf(vmax, __half2float(tv[i]));
+            const float rb = vref / vmax;
+#pragma unroll
+            for (int nq = 0; nq < NQT; ++nq)
+#pragma unroll
+              for (int mi = 0; mi < 8; ++mi)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[nq][mi][c] *= rb;
+            vref = vmax;
+            inv_vref = 1.f / vmax;
+            pscaleA = (g < nv) ? vsA * inv_vref : 0.f;
+            pscaleB = (g + 8 < nv) ? vsB * inv_vref : 0.f;
+          }
+        }
         uint32_t pb[NQT][2][2];  // P^T B fragments: [nq][hi/lo part][reg]
 #pragma unroll
         for (int nq = 0; nq < NQT; ++nq) {
@@ -337,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
             pa[c] = (mref == -INFINITY) ? 0.f : ex2_approx(sv[nq][c] - mref);
             pbv[c] = (mref == -INFINITY) ? 0.f : ex2_approx(sv[nq][2 + c] - mref);
             l[nq][c] += pa[c] + pbv[c];
-            if (kFP8) {
-              pa[c] *= pscale;
-              pbv[c] *= pscale;
+            if (kB8) {
+              pa[c] *= pscaleA;
+              pbv[c] *= pscaleB;
             }
           }
           pb[nq][0][0] = movm_t(pack2<kBF16>(pa[0], pa[1]));
@@ -353,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         // ---------------- O^T += V^T . P^T
         {
           const int jm = lane >> 3;
-          if (kFP8) {
+          if (kB8) {
             // ldmatrix.trans over b16 units: a lane gets tokens 2t,2t+1 x dims 2g,2g+1
             // of a 16-byte chunk; A row g <-> dim 2g, row g+8 <-> dim 2g+1.
             const int vtok = (lane & 7) + 8 * (jm & 1);
@@ -363,8 +417,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
               uint32_t r0, r1, r2, r3;
               ldsm_x4_t(sV + vtok * 128 + ((chunk ^ (vtok & 7)) << 4), r0, r1, r2, r3);
               uint32_t a[4];
-              cvt_fp8x4(__byte_perm(r0, 0, 0x3120), a[0], a[1]);
-              cvt_fp8x4(__byte_perm(r1, 0, 0x3120), a[2], a[3]);
+              cvt_b8x4<KVDT>(__byte_perm(r0, 0, 0x3120), a[0], a[1]);
+              cvt_b8x4<KVDT>(__byte_perm(r1, 0, 0x3120), a[2], a[3]);
               if (nv < SCKV_PAGE_TOKENS) {
                 a[0] = mask_pair(a[0], 2 * t, 2 * t + 1, nv);
                 a[1] = mask_pair(a[1], 2 * t, 2 * t + 1, nv);
@@ -373,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
               }
 #pragma unroll
               for (int nq = 0; nq < NQT; ++nq) mma16816<false>(acc[nq][2 * c2], a, pb[nq][0][0], pb[nq][0][1]);
-              cvt_fp8x4(__byte_perm(r2, 0, 0x3120), a[0], a[1]);
-              cvt_fp8x4(__byte_perm(r3, 0, 0x3120), a[2], a[3]);
+              cvt_b8x4<KVDT>(__byte_perm(r2, 0, 0x3120), a[0], a[1]);
+              cvt_b8x4<KVDT>(__byte_perm(r3, 0, 0x3120), a[2], a[3]);
               if (nv < SCKV_PAGE_TOKENS) {
                 a[0] = mask_pair(a[0], 2 * t, 2 * t + 1, nv);
                 a[1] = mask_pair(a[1], 2 * t, 2 * t + 1, nv);
@@ -432,9 +486,9 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
 #pragma unroll
       for (int mi = 0; mi < 8; ++mi) {
         // FP8: A row g <-> dim 16mi+2g, row g+8 <-> dim 16mi+2g+1
-        const int dA = kFP8 ? 16 * mi + 2 * g : 16 * mi + g;
-        const int dB = kFP8 ? dA + 1 : dA + 8;
-        const float vs = kFP8 ? vref : 1.f;
+        const int dA = kB8 ? 16 * mi + 2 * g : 16 * mi + g;
+        const int dB = kB8 ? dA + 1 : dA + 8;
+        const float vs = kB8 ? vref : 1.f;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int q = 8 * nq + 2 * t + c;
@@ -538,6 +592,12 @@ int launch_decode_mma(const sckv_pool* pool, int G, const DecodeParams& prm, cud
       // (Qwen3 FP8: 0.791 -> 0.746 ms per layer launch)
       return (H % 4 == 0) ? launch_mma_nq<SCKV_DTYPE_FP8_E4M3, 4, 3>(pool, G, prm, stream)
                           : launch_mma_nq<SCKV_DTYPE_FP8_E4M3, 2, 10>(pool, G, prm, stream);
+    case SCKV_DTYPE_INT8:
+      // per-token scales of the group's heads travel as two bulk copies
+      if (pool->scales == nullptr) return SCKV_ERR_UNSUPPORTED;
+      return (H % 4 == 0) ? launch_mma_nq<SCKV_DTYPE_INT8, 4, 3>(pool, G, prm, stream)
+                          : (H % 2 == 0) ? launch_mma_nq<SCKV_DTYPE_INT8, 2, 10>(pool, G, prm, stream)
+                                         : launch_mma_nq<SCKV_DTYPE_INT8, 1, 16>(pool, G, prm, stream);
     default:
       return SCKV_ERR_UNSUPPORTED;
   }

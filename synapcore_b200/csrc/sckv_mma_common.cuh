@@ -24,6 +24,10 @@ template <>
 struct MmaKV<SCKV_DTYPE_FP8_E4M3> {
   static constexpr int kEB = 1;
 };
+template <>
+struct MmaKV<SCKV_DTYPE_INT8> {
+  static constexpr int kEB = 1;
+};
 
 // Byte address of (row, byte) inside a 128-byte-swizzled 16 x 128 B box.
 __device__ __forceinline__ uint32_t swz(uint32_t box, int row, int byte) {
@@ -89,6 +93,29 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Four int8 codes -> two f16x2 (exact), same byte order as cvt_fp8x4. Each
+// byte, offset by 128, becomes the low byte of the f16 1024 + u (exponent
+// field 25, so the 10 mantissa bits count units); subtracting 1152 leaves the
+// code. (The bias-and-subtract construction of small integers in floating
+// point, applied to f16.)
+__device__ __forceinline__ void cvt_s8x4(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = x ^ 0x80808080u;
+  const uint32_t l = __byte_perm(u, 0x64646464u, 0x4140);
+  const uint32_t h = __byte_perm(u, 0x64646464u, 0x4342);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+  const __half2 lv = __hsub2(*reinterpret_cast<const __half2*>(&l), bias);
+  const __half2 hv = __hsub2(*reinterpret_cast<const __half2*>(&h), bias);
+  lo = *reinterpret_cast<const uint32_t*>(&lv);
+  hi = *reinterpret_cast<const uint32_t*>(&hv);
+}
+
+// One-byte codes -> two f16x2 in the byte order of cvt_fp8x4.
+template <int KVDT>
+__device__ __forceinline__ void cvt_b8x4(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  if (KVDT == SCKV_DTYPE_INT8) cvt_s8x4(x, lo, hi);
+  else cvt_fp8x4(x, lo, hi);
 }
 
 template <bool BF16>

@@ -65,6 +65,8 @@ def _make_case(cuda_device, kv_dtype, hq, hkv, ctx_lens, pool_pages, seed, layer
     ("int8", 8, 2, torch.float16),
     ("int8", 32, 4, torch.bfloat16),
     ("int8", 64, 8, torch.float32),
+    ("int8", 12, 3, torch.bfloat16),      # tensor cores, 1 kv head per stage
+    ("int8", 32, 2, torch.float16),       # G = 16: two q tiles
 ])
 @pytest.mark.parametrize("chunk_pages", [0, 3])
 def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages):
@@ -95,7 +97,8 @@ def test_decode_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt, chunk_pages)
     ("fp8_e4m3", 32, 8, torch.bfloat16),  # tensor cores, 4 kv heads per stage
     ("fp8_e4m3", 12, 6, torch.bfloat16),  # tensor cores, 2 kv heads per stage
     ("fp16", 8, 8, torch.float16),        # CUDA cores
-    ("int8", 16, 4, torch.float16),       # CUDA cores
+    ("int8", 16, 4, torch.float16),       # tensor cores, per-token scales, 4 kv heads per stage
+    ("int8", 16, 16, torch.float16),      # CUDA cores
 ])
 def test_decode_long_items_reuse_every_ring_slot_many_times(cuda_device, kv_dtype, hq, hkv, qdt):
     """One split per sequence and a few work items, so every CTA streams
@@ -182,3 +185,41 @@ def test_fp8_quantisation_error_bound(cuda_device):
               f"(oracle predicts {np.max(predicted) / scale:.4f})")
     pool8.close()
     poolb.close()
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 2)])
+def test_decode_int8_rows_spanning_many_orders_of_magnitude(cuda_device, hq, hkv):
+    """int8 pages whose per-token scales differ by up to ~1e5 inside one
+    sequence: the tensor-core kernel folds each V scale into P relative to a
+    reference it moves when a ratio passes 64 (accumulator rescaled)."""
+    from synapcore_b200.pool import KVPool
+
+    rng = np.random.default_rng(41)
+    D, P, layers = 128, 160, 1
+    pool = KVPool(layers, hkv, D, P, "int8", device=cuda_device)
+    ora = PagedPoolOracle(layers, hkv, D, P, "int8")
+    k = rng.standard_normal((P, layers, hkv, PAGE_TOKENS, D)).astype(np.float32)
+    v = rng.standard_normal((P, layers, hkv, PAGE_TOKENS, D)).astype(np.float32)
+    mag = 10.0 ** rng.uniform(-2.0, 3.0, size=(P, layers, hkv, PAGE_TOKENS, 1)).astype(np.float32)
+    v *= mag
+    k *= 10.0 ** rng.uniform(-1.0, 0.5, size=(P, layers, hkv, PAGE_TOKENS, 1)).astype(np.float32)
+    k_t, v_t = torch.from_numpy(k).half(), torch.from_numpy(v).half()
+    ids = np.arange(P, dtype=np.int32)
+    pool.write_pages(torch.from_numpy(ids).to(cuda_device), k_t.to(cuda_device), v_t.to(cuda_device))
+    ora.write_pages(ids, k_t.float().numpy(), v_t.float().numpy())
+    ctx = [1500, 37, 800]
+    mb = max((c + 15) // 16 for c in ctx)
+    bt = np.stack([rng.choice(P, size=mb, replace=False) for _ in ctx]).astype(np.int32)
+    q = rng.standard_normal((len(ctx), hq, D)).astype(np.float32)
+    for chunk in (0, mb):
+        out = pool.decode_attn(0, torch.from_numpy(q).half().to(cuda_device), torch.from_numpy(bt).to(cuda_device),
+                               torch.tensor(ctx, dtype=torch.int32, device=cuda_device), out_dtype=torch.float32,
+                               chunk_pages=chunk)
+        torch.cuda.synchronize()
+        pool.raise_on_status()
+        ref = ora.decode(0, torch.from_numpy(q).half().float().numpy(), bt, np.array(ctx))
+        got = out.cpu().numpy()
+        assert np.all(np.isfinite(got))
+        for b in range(len(ctx)):
+            assert _rel_err(got[b], ref[b]) <= TOL, (chunk, b, _rel_err(got[b], ref[b]))
+    pool.close()
