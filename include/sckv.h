@@ -193,13 +193,13 @@ SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_d
  * (models/adapters.py:1209-1229, mask at :1218-1224).
  * q/out : [n_tokens][num_q_heads][head_dim]; cu_q int32 [n_seqs+1];
  * start_pos int32 [n_seqs]; block_table [n_seqs][bt_stride] (device).
- * F16 / BF16 pools: tcgen05.mma with S and O accumulators in tensor memory
- * (persistent CTAs claiming work from a counter in the pool's control
- * words, so prefill calls on one pool must not overlap on the GPU);
- * FP8_E4M3 pools (even num_kv_heads): mma.m16n8k16 over TMA-staged pages.
- * fp32 accumulation. BF16 pools need bf16 queries; num_q_heads /
+ * All pool types: tcgen05.mma with S and O accumulators in tensor memory
+ * (persistent CTAs claiming work from a per-launch counter); FP8 and int8
+ * pages are decoded (times their scales) into f16 tiles in shared memory
+ * first. fp32 accumulation. BF16 pools need bf16 queries; num_q_heads /
  * num_kv_heads must be a power of two <= 16; otherwise SCKV_ERR_UNSUPPORTED.
- * SCKV_PREFILL_KERNEL=mma selects the mma.m16n8k16 kernel for F16 / BF16. */
+ * SCKV_PREFILL_KERNEL=mma selects the older mma.m16n8k16 kernel (F16, BF16,
+ * FP8 with even num_kv_heads). */
 SCKV_API int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q,
                       int q_dtype, int num_q_heads, int n_seqs, int n_tokens,
                       const int32_t* cu_q, const int32_t* start_pos,

@@ -477,9 +477,6 @@ extern "C" int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q, int 
   if (out_dtype != SCKV_DTYPE_F16 && out_dtype != SCKV_DTYPE_BF16 && out_dtype != SCKV_DTYPE_F32)
     return SCKV_ERR_INVALID_ARG;
   if (pool->kv_dtype == SCKV_DTYPE_BF16 && q_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
-  if (pool->kv_dtype == SCKV_DTYPE_INT8) return SCKV_ERR_UNSUPPORTED;
-  if (pool->kv_dtype == SCKV_DTYPE_FP8_E4M3 && (pool->num_kv_heads % 2 != 0 || pool->num_kv_heads > 32))
-    return SCKV_ERR_UNSUPPORTED;
   if ((int64_t)pool->num_layers * pool->max_pages > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
   int lg = 0;
   while ((1 << lg) < G) ++lg;
@@ -504,8 +501,8 @@ extern "C" int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q, int 
   prm.q_dtype = q_dtype;
   prm.out_dtype = out_dtype;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  // f16 / bf16 pools: the tensor-memory kernel (sckv_prefill_tc.cu) unless
-  // SCKV_PREFILL_KERNEL=mma asks for this one
+  // every pool type: the tensor-memory kernel (sckv_prefill_tc.cu) unless
+  // SCKV_PREFILL_KERNEL=mma asks for this one (f16 / bf16 / FP8)
   const char* env = getenv("SCKV_PREFILL_KERNEL");
   const bool forced = env != nullptr && strcmp(env, "mma") == 0;
   SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
@@ -515,6 +512,9 @@ extern "C" int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q, int 
                                      as_stream(stream));
     if (rc != SCKV_ERR_UNSUPPORTED) return rc;
   }
+  if (pool->kv_dtype == SCKV_DTYPE_INT8) return SCKV_ERR_UNSUPPORTED;
+  if (pool->kv_dtype == SCKV_DTYPE_FP8_E4M3 && (pool->num_kv_heads % 2 != 0 || pool->num_kv_heads > 32))
+    return SCKV_ERR_UNSUPPORTED;
   const int BQ = kRows >> lg;
   const int max_tiles = (n_tokens + BQ - 1) / BQ + n_seqs;  // upper bound on sum of ceil(T_s / BQ)
   cudaStream_t s = as_stream(stream);

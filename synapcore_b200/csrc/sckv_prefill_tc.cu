@@ -51,7 +51,6 @@ constexpr int kRowsTc = 128;                  // query rows per Q tile (UMMA M)
 constexpr int kQTiles = 2;                    // Q tiles per item, sharing every K/V tile
 constexpr int kKeysTc = 64;                   // keys per K/V tile (4 pages)
 constexpr int kPagesTc = kKeysTc / SCKV_PAGE_TOKENS;
-constexpr int kStagesTc = 4;
 constexpr int kThreadsTc = 512;  // 16 warps, roles below
 constexpr int kSoftmaxThreads = 128;  // per softmax warpgroup (one per Q tile)
 constexpr uint32_t kTmemCols = 512;
@@ -68,16 +67,28 @@ constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of a Q tile: 16
 constexpr int kQTileBytes = 2 * kQHalf;
 constexpr int kTileHalf = kKeysTc * 128;      // one 64-dim half of a K or V tile: 8 KiB
 constexpr int kSlotBytes = 2 * kTileHalf;     // a K (or V) tile: lo and hi halves
-constexpr int kOffK = kQTiles * kQTileBytes;  // K ring [kStagesTc]
-constexpr int kOffV = kOffK + kStagesTc * kSlotBytes;  // V ring [kStagesTc]
-constexpr int kOffBar = kOffV + kStagesTc * kSlotBytes;
-constexpr int kNumBars = 4 * kStagesTc + 4 + 4 + 4 + 2 + 3 + 4;
-constexpr int kOffItemRing = kOffBar + kNumBars * 8;  // int[4]
-constexpr int kOffTmemSlot = kOffItemRing + 16;
-constexpr int kOffAbort = kOffTmemSlot + 4;
-constexpr int kOffPartial = kOffTmemSlot + 16;
-constexpr int kOffTileCum = kOffPartial + kThreadsTc * 4;
-constexpr int kFixedSmem = 1024 + kOffTileCum;  // + 4 * (n_seqs + 1)
+// Shared-memory layout per pool type. One-byte pools (FP8, int8) stage each
+// page's codes by TMA and have the producer warps decode them into the f16
+// K / V rings (3 slots, to make room for the staging).
+template <int KVDT>
+struct TcCfg {
+  static constexpr bool kB8 = KVDT == SCKV_DTYPE_FP8_E4M3 || KVDT == SCKV_DTYPE_INT8;
+  static constexpr bool kBF16 = KVDT == SCKV_DTYPE_BF16;  // MMA type; f16 otherwise
+  static constexpr int kStages = kB8 ? 3 : 4;
+  static constexpr int kPageBox = SCKV_PAGE_TOKENS * 128;          // one page's codes: 16 rows x 128 B
+  static constexpr int kStageSlot = 2 * kPageBox;                  // a producer warp's two pages of a tile
+  static constexpr int kOffK = kQTiles * kQTileBytes;              // K ring [kStages]
+  static constexpr int kOffV = kOffK + kStages * kSlotBytes;       // V ring [kStages]
+  static constexpr int kOffStage = kOffV + kStages * kSlotBytes;   // [4 producer warps][2][kStageSlot]
+  static constexpr int kOffBar = kOffStage + (kB8 ? 4 * 2 * kStageSlot : 0);
+  static constexpr int kNumBars = 4 * kStages + 4 + 4 + 4 + 2 + 3 + 4 + (kB8 ? 8 : 0);
+  static constexpr int kOffItemRing = kOffBar + kNumBars * 8;      // int[4]
+  static constexpr int kOffTmemSlot = kOffItemRing + 16;
+  static constexpr int kOffAbort = kOffTmemSlot + 4;
+  static constexpr int kOffPartial = kOffTmemSlot + 16;
+  static constexpr int kOffTileCum = kOffPartial + kThreadsTc * 4;
+  static constexpr int kFixedSmem = 1024 + kOffTileCum;            // + 4 * (n_seqs + 1)
+};
 
 struct TcParams {
   const void* q;
@@ -98,6 +109,7 @@ struct TcParams {
   int q_dtype;
   int out_dtype;
   int q_tma;  // q arrives by TMA (its type is the MMA's)
+  const void* kv_scales;  // one-byte pools: FP8 fp32 [L][P][K|V][H], int8 fp16 [L][P][K|V][H][16]
   unsigned long long* next_item;  // work counter, zero at launch
   float scale_log2;
 };
@@ -196,10 +208,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 // numbered by one running counter (ring slot g % 4), and each softmax
 // warpgroup numbers its own S tiles by another (S / P buffer g & 1), which
 // fixes every barrier's phase.
-template <bool kBF16>
+template <int KVDT>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tmap,
                       const __grid_constant__ CUtensorMap qmap) {
+  using C = TcCfg<KVDT>;
+  constexpr bool kBF16 = C::kBF16;
+  constexpr int kStagesTc = C::kStages;
+  constexpr int kOffK = C::kOffK, kOffV = C::kOffV, kOffBar = C::kOffBar, kNumBars = C::kNumBars;
+  constexpr int kOffItemRing = C::kOffItemRing, kOffTmemSlot = C::kOffTmemSlot, kOffAbort = C::kOffAbort;
+  constexpr int kOffPartial = C::kOffPartial, kOffTileCum = C::kOffTileCum;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
@@ -225,6 +243,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   // S of item k, and S of item k past its second tile waits for the softmax
   // of item k), so a slot is never rewritten while unread.
   uint64_t* item_full = q_full + 3;
+  // one-byte pools: [producer warp role 2 kv + part][2] staged page codes landed (TMA)
+  uint64_t* stage_full = item_full + 4;
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + kOffItemRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + kOffAbort);
@@ -296,7 +316,147 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpK0 || warp == kWarpK1 || warp == kWarpV0 || warp == kWarpV1) {
+  if (C::kB8 && (warp == kWarpK0 || warp == kWarpK1 || warp == kWarpV0 || warp == kWarpV1)) {
+    // ------------------------------------------------------ producers, one-byte pools
+    // Each warp stages its two pages of a tile by TMA (two tiles ahead) and
+    // decodes them, all lanes, into the f16 ring in the UMMA K-major layout:
+    // lane (r, hf) turns token row r's dims 64 hf .. 64 hf + 63 into f16
+    // times the scale (FP8: the page-head's fp32 scale, applied in fp32;
+    // int8: the token's fp16 scale, one exact f16 product as the reference's
+    // dequantisation rounds it). The ring slot is full once both warps of a
+    // tile (K or V) arrived.
+    const int kv = (warp == kWarpV0 || warp == kWarpV1) ? 1 : 0;
+    const int part = (warp == kWarpK1 || warp == kWarpV1) ? 1 : 0;  // pages 2 part, 2 part + 1
+    const int role = 2 * kv + part;
+    const bool leader = warp == kWarpK0;
+    if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    const int64_t layer_base = (int64_t)p.layer * p.max_pages;
+    uint64_t* fulls = kv ? v_full : k_full;
+    uint64_t* empties = kv ? v_empty : k_empty;
+    uint64_t* sfull = stage_full + 2 * role;
+    uint8_t* stg = base + C::kOffStage + role * 2 * C::kStageSlot;
+    const int r = lane >> 1, hf = lane & 1;
+    float scl[2][2];  // [staging slot][page]: this lane's scale (int8: the fp16 value)
+    int g = 0;        // tiles of this warp's ring so far
+    uint32_t sg = 0;  // staged tiles issued
+    uint32_t sc = 0;  // staged tiles decoded
+    bool aborted = false;
+    for (int k = 0;; ++k) {
+      int item;
+      if (leader) {
+        int claimed = 0;
+        if (lane == 0) {
+          // an index >= n_items tells every role to stop
+          claimed = aborted ? n_items : (int)min((unsigned long long)n_items, atomicAdd(p.next_item, 1ULL));
+          item_ring[k & 3] = claimed;
+          mbar_arrive(&item_full[k & 3]);
+        }
+        item = __shfl_sync(0xffffffffu, claimed, 0);
+      } else {
+        const int ab = __shfl_sync(0xffffffffu, *abort_flag, 0);
+        if (aborted || ab || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
+          aborted = true;
+          break;
+        }
+        item = item_ring[k & 3];
+      }
+      if (item >= n_items) break;
+      const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
+      const int32_t* bt_row = p.block_table + (int64_t)it.seq * p.bt_stride;
+      auto issue = [&](int j) {
+        const int first = j * kPagesTc + 2 * part;
+        const int np = max(0, min(2, it.jlast + 1 - first));
+        const uint32_t sl = sg & 1;
+        int32_t pages[2] = {0, 0};
+        for (int i = 0; i < np; ++i) {
+          int32_t page = __ldg(bt_row + first + i);
+          if (page < 0 || page >= p.max_pages) {
+            if (lane == 0) sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_PREFILL);
+            page = 0;
+          }
+          pages[i] = page;
+          const int64_t sidx = ((layer_base + page) * 2 + kv) * p.hkv + it.h;
+          if (KVDT == SCKV_DTYPE_INT8)
+            scl[sl][i] = __half2float(__ldg(reinterpret_cast<const __half*>(p.kv_scales) + sidx * 16 + r));
+          else
+            scl[sl][i] = __ldg(reinterpret_cast<const float*>(p.kv_scales) + sidx);
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sfull[sl], (uint32_t)np * C::kPageBox);
+          for (int i = 0; i < np; ++i)
+            tma_load_5d(smem_u32(stg + sl * C::kStageSlot + i * C::kPageBox), &tmap, 0, 0, it.h, kv,
+                        (int)(layer_base + pages[i]), &sfull[sl]);
+        }
+        ++sg;
+      };
+      if (it.n_k > 0) issue(0);
+      if (it.n_k > 1) issue(1);
+      for (int j = 0; j < it.n_k; ++j) {
+        const int gt = g + j;
+        const int st = gt % kStagesTc;
+        if (gt >= kStagesTc && !warp_wait(&empties[st], ((gt / kStagesTc) - 1) & 1)) {
+          aborted = true;
+          break;
+        }
+        const uint32_t sl = sc & 1;
+        if (!warp_wait(&sfull[sl], (sc >> 1) & 1)) {
+          aborted = true;
+          break;
+        }
+        const int first = j * kPagesTc + 2 * part;
+        const int np = max(0, min(2, it.jlast + 1 - first));
+        uint8_t* slot = base + (kv ? kOffV : kOffK) + st * kSlotBytes;
+        for (int i = 0; i < np; ++i) {
+          const uint8_t* src = stg + sl * C::kStageSlot + i * C::kPageBox + r * 128;
+          uint8_t* dst = slot + hf * kTileHalf + (2 * part + i) * 2048 + r * 128;
+          const float sv = scl[sl][i];
+          const __half2 s2 = __float2half2_rn(sv);  // int8: the stored fp16 scale, exact
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            // 16 codes: dims 64 hf + 16 c .. + 15 (128-byte swizzle: chunk ^ row)
+            const uint4 w = *reinterpret_cast<const uint4*>(src + (((4 * hf + c) ^ (r & 7)) << 4));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+            uint32_t o[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t lo, hi;
+              cvt_b8x4<KVDT>(ws[q], lo, hi);
+              if (KVDT == SCKV_DTYPE_INT8) {
+                const __half2 a = __hmul2(*reinterpret_cast<const __half2*>(&lo), s2);
+                const __half2 b = __hmul2(*reinterpret_cast<const __half2*>(&hi), s2);
+                lo = *reinterpret_cast<const uint32_t*>(&a);
+                hi = *reinterpret_cast<const uint32_t*>(&b);
+              } else {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+                lo = pack2<false>(a.x * sv, a.y * sv);
+                hi = pack2<false>(b.x * sv, b.y * sv);
+              }
+              o[2 * q] = lo;
+              o[2 * q + 1] = hi;
+            }
+            *reinterpret_cast<uint4*>(dst + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+        // the decoded tile is read by the tensor cores (async proxy)
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&fulls[st]);
+        ++sc;
+        if (j + 2 < it.n_k) issue(j + 2);
+      }
+      if (aborted && !leader) break;
+      g += it.n_k;
+    }
+    if (aborted && lane == 0) {
+      if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
+      *abort_flag = 1;
+    }
+    // staged copies still in flight land before the CTA retires
+    if (lane == 0)
+      for (uint32_t t = sc; t < sg; ++t) mbar_wait_bounded(&sfull[t & 1], (t >> 1) & 1, SCKV_WAIT_LIMIT_NS);
+  } else if (warp == kWarpK0 || warp == kWarpK1 || warp == kWarpV0 || warp == kWarpV1) {
     // ------------------------------------------------------------ producers
     // one TMA issue holds its warp ~0.1 us, so K and V each get two warps,
     // each copying two of a tile's four pages
@@ -713,14 +873,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   }
 }
 
-template <bool kBF16>
+template <int KVDT>
 int launch_tc(const sckv_pool* pool, const TcParams& prm, int max_items, const CUtensorMap& qmap,
               cudaStream_t stream) {
-  auto kern = prefill_tc_kernel<kBF16>;
+  auto kern = prefill_tc_kernel<KVDT>;
   sckv_pool* mp = const_cast<sckv_pool*>(pool);  // the map is a cache inside the handle
   int rc = ensure_tmap(pool, 1, mp->tmap_kv2, &mp->tmap2_ready, 1);
   if (rc != SCKV_OK) return rc;
-  const int smem = kFixedSmem + 4 * (prm.n_seqs + 1);
+  const int smem = TcCfg<KVDT>::kFixedSmem + 4 * (prm.n_seqs + 1);
   if (smem > 227 * 1024) return SCKV_ERR_UNSUPPORTED;
   SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   SCKV_CUDA_CHECK(cudaMemsetAsync(prm.next_item, 0, sizeof(unsigned long long), stream));
@@ -743,8 +903,10 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
                       int n_tokens, const int32_t* cu_q, const int32_t* start_pos, const int32_t* block_table,
                       int64_t bt_stride, int max_blocks, float scale, void* out, int out_dtype, int lg_g,
                       cudaStream_t stream) {
-  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
   if (pool->head_dim != kHDim || n_seqs > 16384 || !(scale > 0.f)) return SCKV_ERR_UNSUPPORTED;
+  const bool byte_pool = pool->kv_dtype == SCKV_DTYPE_FP8_E4M3 || pool->kv_dtype == SCKV_DTYPE_INT8;
+  if (byte_pool && pool->scales == nullptr) return SCKV_ERR_UNSUPPORTED;
+  if (!byte_pool && pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
   // 16-byte vector loads of q and stores of out
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return SCKV_ERR_UNSUPPORTED;
   TcParams prm{};
@@ -767,6 +929,7 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
   prm.out_dtype = out_dtype;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.next_item = sckv_take_work_counter(pool);
+  prm.kv_scales = pool->scales;
   const int BQ = kRowsTc >> lg_g;
   const int BQ2 = kQTiles * BQ;
   const int64_t max_tiles = (int64_t)(n_tokens + BQ2 - 1) / BQ2 + n_seqs;  // >= sum of ceil(T_s / BQ2)
@@ -790,8 +953,13 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
         prm.q_tma = 1;
     }
   }
-  return pool->kv_dtype == SCKV_DTYPE_BF16 ? launch_tc<true>(pool, prm, (int)max_items, qmap, stream)
-                                           : launch_tc<false>(pool, prm, (int)max_items, qmap, stream);
+  switch (pool->kv_dtype) {
+    case SCKV_DTYPE_BF16: return launch_tc<SCKV_DTYPE_BF16>(pool, prm, (int)max_items, qmap, stream);
+    case SCKV_DTYPE_F16: return launch_tc<SCKV_DTYPE_F16>(pool, prm, (int)max_items, qmap, stream);
+    case SCKV_DTYPE_FP8_E4M3: return launch_tc<SCKV_DTYPE_FP8_E4M3>(pool, prm, (int)max_items, qmap, stream);
+    case SCKV_DTYPE_INT8: return launch_tc<SCKV_DTYPE_INT8>(pool, prm, (int)max_items, qmap, stream);
+    default: return SCKV_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace sckv_detail

@@ -249,8 +249,8 @@ class PagedKVCache:
         except N.SCKVError as e:
             if e.code != N.SCKV_ERR_UNSUPPORTED:
                 raise
-        # combinations the tensor-core prefill kernel does not build (int8
-        # pools, non-power-of-two groups): token t is a decode query of length
+        # combinations the tensor-core prefill kernel does not build
+        # (non-power-of-two groups, head_dim != 128): token t is a decode query of length
         # start+t+1 over the same row (block-table stride 0)
         bt = self.block_table[r:r + 1].expand(T, self.max_blocks)
         ctx = torch.arange(start + 1, start + T + 1, dtype=torch.int32, device=self.device)

@@ -46,7 +46,7 @@ def _case(dev, kv_dtype, hq, hkv, T, start, pool_pages=160, layers=2, seed=3, na
             if used:
                 k[perm[b, last], :, :, used:] = np.nan
                 v[perm[b, last], :, :, used:] = np.nan
-    src_t = torch.float16 if kv_dtype == "fp16" else torch.bfloat16
+    src_t = torch.float16 if kv_dtype in ("fp16", "int8") else torch.bfloat16
     k_t, v_t = torch.from_numpy(k).to(src_t), torch.from_numpy(v).to(src_t)
     ids = np.arange(pool_pages, dtype=np.int32)
     pool.write_pages(torch.from_numpy(ids).to(dev), k_t.to(dev), v_t.to(dev))
@@ -85,6 +85,10 @@ def _check(pool, ora, bt, cu, start, q_t, out_dtype=torch.float32):
     ("fp8_e4m3", 32, 4, torch.bfloat16),
     ("fp8_e4m3", 16, 2, torch.float16),
     ("fp8_e4m3", 8, 8, torch.float32),
+    ("int8", 16, 4, torch.float16),
+    ("int8", 32, 8, torch.bfloat16),
+    ("int8", 8, 8, torch.float32),
+    ("int8", 32, 2, torch.float16),
 ])
 def test_prefill_matches_oracle(cuda_device, kv_dtype, hq, hkv, qdt):
     T = [1, 5, 64, 130, 17, 16, 33]
@@ -113,14 +117,16 @@ def test_prefill_unsupported_and_bounds(cuda_device):
     from synapcore_b200 import _native as N
     from synapcore_b200.pool import KVPool
 
+    # three q heads per kv head: not a power of two
     pool = KVPool(1, 4, 128, 16, "int8", device=cuda_device)
-    q = torch.zeros(4, 8, 128, dtype=torch.float16, device=cuda_device)
+    q3 = torch.zeros(4, 12, 128, dtype=torch.float16, device=cuda_device)
     cu = torch.tensor([0, 4], dtype=torch.int32, device=cuda_device)
     st = torch.tensor([0], dtype=torch.int32, device=cuda_device)
     bt = torch.zeros(1, 2, dtype=torch.int32, device=cuda_device)
     with pytest.raises(N.SCKVError) as e:
-        pool.prefill_attn(0, q, cu, st, bt)
+        pool.prefill_attn(0, q3, cu, st, bt)
     assert e.value.code == N.SCKV_ERR_UNSUPPORTED
+    q = torch.zeros(4, 8, 128, dtype=torch.float16, device=cuda_device)
     # a sequence that would run past its block table is reported, not read
     pool = KVPool(1, 4, 128, 16, "fp16", device=cuda_device)
     st_bad = torch.tensor([30], dtype=torch.int32, device=cuda_device)
@@ -263,3 +269,15 @@ def test_prefill_launches_on_two_streams_share_one_pool(cuda_device):
     for layer, out in outs:
         got = out.float().cpu().numpy()
         assert _rel_err(got, refs[layer]) <= TOL, layer
+
+
+@pytest.mark.parametrize("kv_dtype", ["fp8_e4m3", "int8"])
+def test_one_byte_pools_prefill_long_prompts_with_prefix(cuda_device, kv_dtype):
+    """One-byte pools on the tensor-memory kernel: codes staged by TMA and
+    decoded into the f16 rings; prompts long enough that every producer
+    warp cycles its staging slots and the 3-slot rings many times, behind a
+    cached prefix (start > 0) and with ragged ends."""
+    T = [700, 1, 333]
+    start = [64, 500, 0]
+    pool, ora, bt, cu, st, q = _case(cuda_device, kv_dtype, 32, 8, T, start, pool_pages=200, layers=1)
+    _check(pool, ora, bt, cu, st, torch.from_numpy(q).to(torch.bfloat16))
