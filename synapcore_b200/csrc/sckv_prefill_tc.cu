@@ -897,8 +897,8 @@ int launch_tc(const sckv_pool* pool, const TcParams& prm, int max_items, const C
 
 namespace sckv_detail {
 
-// Tensor-memory prefill for f16 / bf16 pools. Returns SCKV_ERR_UNSUPPORTED
-// for combinations it does not build (the caller then uses prefill_kernel).
+// Tensor-memory prefill for every pool type. Returns SCKV_ERR_UNSUPPORTED
+// for combinations it does not build (the caller then tries prefill_kernel).
 int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads, int n_seqs,
                       int n_tokens, const int32_t* cu_q, const int32_t* start_pos, const int32_t* block_table,
                       int64_t bt_stride, int max_blocks, float scale, void* out, int out_dtype, int lg_g,
