@@ -56,8 +56,8 @@ struct QkvCfg {
   static constexpr int kOffW = kQkvTile;
   static constexpr int kOffLo = kQkvTile * (1 + kHeads);
   static constexpr int kBarOff = kStages * kStageBytes;
-  static constexpr int kBytes = 1024 + kBarOff + (2 * kStages + 1) * 8 + 16;
-  static constexpr uint32_t kTmemCols = kBN;
+  static constexpr int kBytes = 1024 + kBarOff + (2 * kStages + 5) * 8 + 16;
+  static constexpr uint32_t kTmemCols = 2 * kBN;  // double-buffered accumulator
 };
 
 struct QkvParams {
@@ -82,7 +82,10 @@ struct QkvParams {
   int layer;
   int q_out_dtype;
   int pool_dtype;
-  int k_steps_per_split;  // hidden steps of 64 per blockIdx.z
+  int k_steps_per_split;  // hidden steps of 64 per split
+  int n_groups;           // head groups (of kHeads heads) over q, k and v
+  int m_tiles;            // token tiles of 128
+  int n_tiles;            // n_groups * m_tiles * splits
   int hd_total;           // (hq + 2 hkv) * 128 output columns
   float eps;
 };
@@ -221,6 +224,32 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
   for (int i = 0; i < 4; ++i) sckv_store_from_float(out, dst + lane + 32 * i, out_dtype, y[i]);
 }
 
+// Geometry of work tile t: tiles run head group fastest, then token tile,
+// then hidden split, so CTAs working at the same time share the x tile.
+struct QkvTile {
+  int kind, head0, kind_heads, m0, z, s0, nk;
+};
+
+template <int kHeads>
+__device__ __forceinline__ QkvTile qkv_tile(const QkvParams& p, int t) {
+  QkvTile q;
+  const int gq = (p.hq + kHeads - 1) / kHeads, gk = (p.hkv + kHeads - 1) / kHeads;
+  const int gx = t % p.n_groups;
+  const int rest = t / p.n_groups;
+  q.m0 = (rest % p.m_tiles) * kQkvBM;
+  q.z = rest / p.m_tiles;
+  q.kind = gx < gq ? 0 : (gx < gq + gk ? 1 : 2);  // q, k, v
+  q.head0 = (gx - (q.kind == 0 ? 0 : (q.kind == 1 ? gq : gq + gk))) * kHeads;
+  q.kind_heads = q.kind == 0 ? p.hq : p.hkv;
+  const int nk_all = (p.hidden + kQkvBK - 1) / kQkvBK;
+  q.s0 = q.z * p.k_steps_per_split;
+  q.nk = min(nk_all - q.s0, p.k_steps_per_split);
+  return q;
+}
+
+// Persistent: one CTA per SM walks tiles blockIdx.x, + gridDim.x, ...; the
+// accumulator is double-buffered in tensor memory (2 x 128 kHeads columns),
+// so the MMAs of a CTA's next tile run while its epilogue drains the last.
 template <bool kBF16, bool kSplit, int kHeads>
 __global__ void __launch_bounds__(kQkvThreads, 1)
     qkv_append_kernel(const QkvParams p, const __grid_constant__ CUtensorMap xmap,
@@ -232,29 +261,25 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(base + SM::kBarOff);  // [S] stage landed (TMA)
   uint64_t* empty = full + kQkvStages;                               // [S] stage read by its MMAs (commit)
-  uint64_t* acc_full = empty + kQkvStages;                           // every MMA finished (commit)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + kQkvStages;                           // [2] a tile's MMAs finished (commit)
+  uint64_t* acc_empty = acc_full + 2;                                // [2] its epilogue read it (128 threads)
+  uint64_t* mma_done = acc_empty + 2;                                // every MMA issued finished (drain)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // output head group: groups of q heads, then of k heads, then of v heads
-  const int gq = (p.hq + kHeads - 1) / kHeads, gk = (p.hkv + kHeads - 1) / kHeads;
-  const int kind = blockIdx.x < gq ? 0 : (blockIdx.x < gq + gk ? 1 : 2);  // q, k, v
-  const int head0 = (blockIdx.x - (kind == 0 ? 0 : (kind == 1 ? gq : gq + gk))) * kHeads;
-  const int kind_heads = kind == 0 ? p.hq : p.hkv;
-  const int m0 = blockIdx.y * kQkvBM;
-  // hidden steps s0 .. s0 + nk - 1 of 64 (all of them unless split over blockIdx.z)
-  const int nk_all = (p.hidden + kQkvBK - 1) / kQkvBK;
-  const int s0 = blockIdx.z * p.k_steps_per_split;
-  const int nk = min(nk_all - s0, p.k_steps_per_split);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQkvStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -267,168 +292,201 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const CUtensorMap* wmap = kind == 0 ? &wqmap : (kind == 1 ? &wkmap : &wvmap);
-      const int row0 = head0 * kHead;  // rows past the last head read as zeros
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap)) : "memory");
-      int issued = 0;
-      for (int s = 0; s < nk; ++s) {
-        const int st = s % kQkvStages;
-        if (s >= kQkvStages) {
-          if (*abort_flag || !mbar_wait_bounded(&empty[st], ((s / kQkvStages) - 1) & 1, SCKV_WAIT_LIMIT_NS)) {
-            if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_QKV);
-            *abort_flag = 1;
-            break;
+      uint32_t gcount = 0;  // stages issued by this CTA
+      bool aborted = false;
+      for (int t = blockIdx.x; t < p.n_tiles && !aborted; t += gridDim.x) {
+        const QkvTile tl = qkv_tile<kHeads>(p, t);
+        const CUtensorMap* wmap = tl.kind == 0 ? &wqmap : (tl.kind == 1 ? &wkmap : &wvmap);
+        const int row0 = tl.head0 * kHead;  // rows past the last head read as zeros
+        for (int s = 0; s < tl.nk; ++s) {
+          const uint32_t st = gcount % kQkvStages;
+          if (gcount >= kQkvStages) {
+            if (*abort_flag ||
+                !mbar_wait_bounded(&empty[st], ((gcount / kQkvStages) - 1) & 1, SCKV_WAIT_LIMIT_NS)) {
+              if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_QKV);
+              *abort_flag = 1;
+              aborted = true;
+              break;
+            }
           }
+          const uint32_t stage = smem_u32(base + st * SM::kStageBytes);
+          mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
+          const int kx = (tl.s0 + s) * kQkvBK;
+          tma_load_2d(stage, &xmap, kx, tl.m0, &full[st]);
+          tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
+          if (kSplit) tma_load_2d(stage + SM::kOffLo, &xlomap, kx, tl.m0, &full[st]);
+          ++gcount;
         }
-        const uint32_t stage = smem_u32(base + st * SM::kStageBytes);
-        mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
-        const int kx = (s0 + s) * kQkvBK;
-        tma_load_2d(stage, &xmap, kx, m0, &full[st]);
-        tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
-        if (kSplit) tma_load_2d(stage + SM::kOffLo, &xlomap, kx, m0, &full[st]);
-        ++issued;
       }
       // copies still in flight land before the CTA may exit
-      for (int k = issued > kQkvStages ? issued - kQkvStages : 0; k < issued; ++k)
+      for (uint32_t k = gcount > kQkvStages ? gcount - kQkvStages : 0; k < gcount; ++k)
         mbar_wait_bounded(&full[k % kQkvStages], (k / kQkvStages) & 1, SCKV_WAIT_LIMIT_NS);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t kIdesc = instr_desc_f16(kBF16, SM::kBN, false);
     bool ok = true;
-    for (int s = 0; s < nk; ++s) {
-      const int st = s % kQkvStages;
-      if (*abort_flag || !warp_wait(&full[st], (s / kQkvStages) & 1)) {
+    uint32_t gcount = 0;  // stages consumed
+    int lt = 0;           // tiles of this CTA
+    for (int t = blockIdx.x; t < p.n_tiles && ok; t += gridDim.x, ++lt) {
+      const QkvTile tl = qkv_tile<kHeads>(p, t);
+      const int buf = lt & 1;
+      // the buffer's previous tile (lt - 2) has been read by the epilogue
+      if (lt >= 2 && (*abort_flag || !warp_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (lane == 0) {
-        const uint32_t a = smem_u32(base + st * SM::kStageBytes);
-        const uint32_t b = a + SM::kOffW;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          // A = x rows (tokens), B = W rows (output dims), both K-major:
-          // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
-          const uint64_t bdesc = smem_desc_sw128(b + kk * 32, 16, 1024);
-          umma_ss(tmem, smem_desc_sw128(a + kk * 32, 16, 1024), bdesc, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
-          if (kSplit) umma_ss(tmem, smem_desc_sw128(a + SM::kOffLo + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
+      const uint32_t acc = tmem + (uint32_t)(buf * SM::kBN);
+      for (int s = 0; s < tl.nk; ++s) {
+        const uint32_t st = gcount % kQkvStages;
+        if (*abort_flag || !warp_wait(&full[st], (gcount / kQkvStages) & 1)) {
+          ok = false;
+          break;
         }
-        umma_commit(&empty[st]);
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a = smem_u32(base + st * SM::kStageBytes);
+          const uint32_t b = a + SM::kOffW;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // A = x rows (tokens), B = W rows (output dims), both K-major:
+            // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
+            const uint64_t bdesc = smem_desc_sw128(b + kk * 32, 16, 1024);
+            umma_ss(acc, smem_desc_sw128(a + kk * 32, 16, 1024), bdesc, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+            if (kSplit) umma_ss(acc, smem_desc_sw128(a + SM::kOffLo + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
+          }
+          umma_commit(&empty[st]);
+        }
+        __syncwarp();
+        ++gcount;
       }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&acc_full[buf]);
       __syncwarp();
     }
     if (!ok) {
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_QKV);
       if (lane == 0) *abort_flag = 1;
     }
-    // fires once every MMA issued above has finished (at once if none was)
-    if (lane == 0) umma_commit(acc_full);
+    // every MMA issued above has finished before the tensor memory is freed
+    if (lane == 0) umma_commit(mma_done);
     __syncwarp();
-    warp_wait(acc_full, 0);
+    warp_wait(mma_done, 0);
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lanes 32 quad .. 32 quad + 31
-    const int t = m0 + quad * 32 + lane;
-    const bool ready = warp_wait(acc_full, 0);
-    tc_fence_after();
-    // warp-uniform: the tensor-memory loads below are warp-wide
-    const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
-    if (ready && !aborted && p.partial != nullptr) {
-      // split-K: raw fp32 sums of this split; qkv_finish_kernel adds the
-      // splits and applies the norm, rotation and stores
+    int lt = 0;
+    for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
+      const QkvTile tl = qkv_tile<kHeads>(p, t);
+      const int buf = lt & 1;
+      const int tok = tl.m0 + quad * 32 + lane;
+      const bool ready = warp_wait(&acc_full[buf], (lt >> 1) & 1);
+      tc_fence_after();
+      // warp-uniform: the tensor-memory loads below are warp-wide
+      const int aborted = __shfl_sync(0xffffffffu, *abort_flag, 0);
+      if (!ready || aborted) break;
+      const uint32_t acc = tmem + (uint32_t)(buf * SM::kBN) + ((uint32_t)(quad * 32) << 16);
+      if (p.partial != nullptr) {
+        // split-K: raw fp32 sums of this split; qkv_finish_kernel adds the
+        // splits and applies the norm, rotation and stores
 #pragma unroll 1
-      for (int hh = 0; hh < kHeads; ++hh) {
-        const int head = head0 + hh;
-        if (head >= kind_heads) break;  // warp-uniform
-        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(hh * kHead);
-        const int col0 = (kind == 0 ? 0 : (kind == 1 ? p.hq : p.hq + p.hkv) * kHead) + head * kHead;
-        float* dst = p.partial + ((int64_t)blockIdx.z * p.n_tok + t) * p.hd_total + col0;
+        for (int hh = 0; hh < kHeads; ++hh) {
+          const int head = tl.head0 + hh;
+          if (head >= tl.kind_heads) break;  // warp-uniform
+          const uint32_t trow = acc + (uint32_t)(hh * kHead);
+          const int col0 = (tl.kind == 0 ? 0 : (tl.kind == 1 ? p.hq : p.hq + p.hkv) * kHead) + head * kHead;
+          float* dst = p.partial + ((int64_t)tl.z * p.n_tok + tok) * p.hd_total + col0;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(trow + c * 32, r);
-          tc_wait_ld();
-          if (t < p.n_tok) {
-            float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                  __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-          }
-        }
-      }
-    } else if (ready && !aborted) {
-      const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
-      const bool live = t < p.n_tok;
-      // the token's page slab (k and v tiles); q rows go to q_out
-      int pos = 0;
-      const int64_t slot_row = (live && kind > 0) ? token_slab(p, t, &pos, head0 == 0) : -1;
-#pragma unroll 1
-      for (int hh = 0; hh < kHeads; ++hh) {
-        const int head = head0 + hh;
-        if (head >= kind_heads) break;  // warp-uniform
-        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(hh * kHead);
-        // every lane reads the tensor memory (the loads are warp-wide); rows
-        // past the last token are computed and dropped
-        float inv = 1.f;
-        if (nw != nullptr) {
-          float ss = 0.f;
-#pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
             tmem_ld32(trow + c * 32, r);
             tc_wait_ld();
+            if (tok < p.n_tok) {
+              float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                    __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            }
+          }
+        }
+      } else {
+        const __half* nw = tl.kind == 0 ? p.q_norm_w : (tl.kind == 1 ? p.k_norm_w : nullptr);
+        const bool live = tok < p.n_tok;
+        // the token's page slab (k and v tiles); q rows go to q_out
+        int pos = 0;
+        const int64_t slot_row = (live && tl.kind > 0) ? token_slab(p, tok, &pos, tl.head0 == 0) : -1;
+#pragma unroll 1
+        for (int hh = 0; hh < kHeads; ++hh) {
+          const int head = tl.head0 + hh;
+          if (head >= tl.kind_heads) break;  // warp-uniform
+          const uint32_t trow = acc + (uint32_t)(hh * kHead);
+          // every lane reads the tensor memory (the loads are warp-wide); rows
+          // past the last token are computed and dropped
+          float inv = 1.f;
+          if (nw != nullptr) {
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(trow + c * 32, r);
+              tc_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float x = __uint_as_float(r[i]);
+                ss = __fmaf_rn(x, x, ss);
+              }
+            }
+            inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHead), p.eps)));
+          }
+          int64_t dst = -1;
+          void* out = p.q_out;
+          int out_dtype = p.q_out_dtype;
+          if (live && tl.kind == 0) {
+            dst = ((int64_t)tok * p.hq + head) * kHead;
+          } else if (slot_row >= 0) {
+            // data layout [L][P][K|V][H][16][D]
+            dst = (((slot_row * 2 + (tl.kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) *
+                  kHead;
+            out = p.pool_data;
+            out_dtype = p.pool_dtype;
+          }
+#pragma unroll 1
+          for (int hf = 0; hf < 2; ++hf) {
+            // dims d = 32 hf + i and their rotation partners d + 64
+            uint32_t r1[32], r2[32];
+            tmem_ld32(trow + hf * 32, r1);
+            tmem_ld32(trow + 64 + hf * 32, r2);
+            tc_wait_ld();
+            if (dst < 0) continue;
+            float y1[32], y2[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float x = __uint_as_float(r[i]);
-              ss = __fmaf_rn(x, x, ss);
+              const int d = hf * 32 + i;
+              float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
+              if (nw != nullptr) {
+                x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
+                x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
+              }
+              if (tl.kind < 2) {
+                const float2 cs = __ldg(p.rope_cs + (int64_t)tok * kRopePairs + d);
+                y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+                y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+              } else {
+                y1[i] = x1;
+                y2[i] = x2;
+              }
             }
+            store32(out, dst + hf * 32, out_dtype, y1);
+            store32(out, dst + 64 + hf * 32, out_dtype, y2);
           }
-          inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHead), p.eps)));
-        }
-        int64_t dst = -1;
-        void* out = p.q_out;
-        int out_dtype = p.q_out_dtype;
-        if (live && kind == 0) {
-          dst = ((int64_t)t * p.hq + head) * kHead;
-        } else if (slot_row >= 0) {
-          // data layout [L][P][K|V][H][16][D]
-          dst = (((slot_row * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kHead;
-          out = p.pool_data;
-          out_dtype = p.pool_dtype;
-        }
-#pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          // dims d = 32 hf + i and their rotation partners d + 64
-          uint32_t r1[32], r2[32];
-          tmem_ld32(trow + hf * 32, r1);
-          tmem_ld32(trow + 64 + hf * 32, r2);
-          tc_wait_ld();
-          if (dst < 0) continue;
-          float y1[32], y2[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int d = hf * 32 + i;
-            float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
-            if (nw != nullptr) {
-              x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
-              x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
-            }
-            if (kind < 2) {
-              const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + d);
-              y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-              y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-            } else {
-              y1[i] = x1;
-              y2[i] = x2;
-            }
-          }
-          store32(out, dst + hf * 32, out_dtype, y1);
-          store32(out, dst + 64 + hf * 32, out_dtype, y2);
         }
       }
+      // the accumulator buffer may take the tile after next
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
@@ -455,14 +513,21 @@ int encode_rows(CUtensorMap* map, const void* ptr, int rows, int hidden, bool bf
 }
 
 template <bool kBF16, bool kSplit, int kHeads>
-int launch_qkv(const QkvParams& prm, const CUtensorMap (&maps)[5], int n_groups, int m_tiles, cudaStream_t stream,
-               int k_splits = 1) {
+int launch_qkv(const QkvParams& prm_in, const CUtensorMap (&maps)[5], int n_groups, int m_tiles, int num_sms,
+               cudaStream_t stream, int k_splits = 1) {
   auto kern = qkv_append_kernel<kBF16, kSplit, kHeads>;
   constexpr int smem = QkvCfg<kSplit, kHeads>::kBytes;
   static_assert(smem <= 227 * 1024, "shared memory");
+  QkvParams prm = prm_in;
+  prm.n_groups = n_groups;
+  prm.m_tiles = m_tiles;
+  const int64_t n_tiles = (int64_t)n_groups * m_tiles * k_splits;
+  if (n_tiles > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
+  prm.n_tiles = (int)n_tiles;
   SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kern<<<dim3(n_groups, m_tiles, k_splits), kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3],
-                                                                         maps[4]);
+  // persistent: one CTA per SM (the shared memory allows no second)
+  const int grid = (int)(n_tiles < num_sms ? n_tiles : num_sms);
+  kern<<<grid, kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3], maps[4]);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
@@ -600,11 +665,12 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
                                                          (size_t)n_tokens * kRopePairs * sizeof(float2))
                              : nullptr;
   const int mt = (int)m_tiles;
+  const int sms = pool->num_sms;
   if (k_splits > 1) {
-    rc = x_lo ? (bf16 ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, s, k_splits)
-                      : launch_qkv<false, true, 1>(prm, maps, n_groups, mt, s, k_splits))
-              : (bf16 ? launch_qkv<true, false, 1>(prm, maps, n_groups, mt, s, k_splits)
-                      : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, s, k_splits));
+    rc = x_lo ? (bf16 ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
+                      : launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits))
+              : (bf16 ? launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
+                      : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits));
     if (rc != SCKV_OK) return rc;
     const int64_t warps = (int64_t)n_tokens * n_heads;
     qkv_finish_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(prm, k_splits);
@@ -613,10 +679,14 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   }
   if (heads == 2) {
     if (bf16)
-      return x_lo ? launch_qkv<true, true, 2>(prm, maps, n_groups, mt, s) : launch_qkv<true, false, 2>(prm, maps, n_groups, mt, s);
-    return x_lo ? launch_qkv<false, true, 2>(prm, maps, n_groups, mt, s) : launch_qkv<false, false, 2>(prm, maps, n_groups, mt, s);
+      return x_lo ? launch_qkv<true, true, 2>(prm, maps, n_groups, mt, sms, s)
+                  : launch_qkv<true, false, 2>(prm, maps, n_groups, mt, sms, s);
+    return x_lo ? launch_qkv<false, true, 2>(prm, maps, n_groups, mt, sms, s)
+                : launch_qkv<false, false, 2>(prm, maps, n_groups, mt, sms, s);
   }
   if (bf16)
-    return x_lo ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, s) : launch_qkv<true, false, 1>(prm, maps, n_groups, mt, s);
-  return x_lo ? launch_qkv<false, true, 1>(prm, maps, n_groups, mt, s) : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, s);
+    return x_lo ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s)
+                : launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s);
+  return x_lo ? launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s)
+              : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s);
 }
