@@ -93,6 +93,14 @@ WORKLOADS = {
     "olmoe-mix-small": dict(kind="mix", model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128,
                             kv="fp16", qdt=torch.float16, batch=32, ctx=(16, 8192), new_per_step=8,
                             prompt=(64, 2048), fork_frac=0.25, prefix=1024, pool_pages=9000, evict_at=0.9),
+    # prompt passes alone: causal prefill attention over whole prompts whose
+    # K/V are already in the pages (one sckv_prefill_attn per layer)
+    "qwen3-prefill": dict(kind="prefill", model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128,
+                          kv="bf16", qdt=torch.bfloat16, batch=16, prompt=2048),
+    "qwen3-fp8-prefill": dict(kind="prefill", model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128,
+                              kv="fp8_e4m3", qdt=torch.bfloat16, batch=16, prompt=2048),
+    "qwen3-int8-prefill": dict(kind="prefill", model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128,
+                               kv="int8", qdt=torch.bfloat16, batch=16, prompt=2048),
     # the attention input either side of the cache: q/k/v projections of
     # the hidden states (bf16 activations and weights), per-head QK-norm,
     # RoPE and the K/V append, fused in one launch per layer (sckv_qkv_append)
@@ -558,6 +566,153 @@ def bench_ours(args, w_full, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+    pool.close()
+    return res
+
+
+# ----------------------------------------------------------------------------- prompt passes
+def prefill_flops(w) -> int:
+    """Causal attention flops of one layer over the step's prompts: query t
+    of a T-token prompt sees t + 1 keys (2 matmuls x 2 flops per MAC)."""
+    T = w["prompt"]
+    return w["batch"] * 4 * w["hq"] * w["d"] * (T * (T + 1) // 2)
+
+
+def bench_prefill(args, w, world, rank, local):
+    """One step = sckv_prefill_attn for every layer over `batch` prompts of
+    `prompt` tokens whose K/V already fill their pages."""
+    from synapcore_b200.pool import KVPool
+
+    dev = torch.device("cuda", local)
+    L, hq, hkv, d, B, T = w["layers"], w["hq"], w["hkv"], w["d"], w["batch"], w["prompt"]
+    mb = (T + PAGE - 1) // PAGE
+    P = B * mb
+    pool = KVPool(L, hkv, d, P, w["kv"], device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    view = pool.pool_view()
+    for l in range(L):
+        if w["kv"] == "fp8_e4m3":
+            codes = torch.randint(0, 0x7F, view[l].shape, dtype=torch.uint8, device=dev, generator=g)
+            codes |= torch.randint(0, 2, view[l].shape, dtype=torch.uint8, device=dev, generator=g) << 7
+            view[l].copy_(codes)
+        elif w["kv"] == "int8":
+            view[l].copy_(torch.randint(-127, 128, view[l].shape, dtype=torch.int8, device=dev, generator=g))
+        else:
+            view[l].normal_(generator=g)
+    if w["kv"] == "fp8_e4m3":
+        pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
+    elif w["kv"] == "int8":
+        pool.scale_view().uniform_(1.5 / 127, 12.0 / 127, generator=g)
+    perm = torch.randperm(P, generator=g, device=dev).to(torch.int32)
+    bt = perm.view(B, mb)
+    cu = torch.arange(0, B * T + 1, T, dtype=torch.int32, device=dev)
+    start = torch.zeros(B, dtype=torch.int32, device=dev)
+    # one query tensor serves every layer (268 MB >> L2 at the default size)
+    q = torch.randn(B * T, hq, d, device=dev, generator=g).to(w["qdt"])
+    out = torch.empty_like(q)
+
+    def step(qs, outs, ev=None):
+        for l in range(L):
+            if ev is not None:
+                ev.append(torch.cuda.Event(enable_timing=True))
+                ev[-1].record()
+            pool.prefill_attn(l, qs, cu, start, bt, out=outs)
+            if ev is not None:
+                ev.append(torch.cuda.Event(enable_timing=True))
+                ev[-1].record()
+
+    from synapcore_b200 import _native as N
+
+    n0 = N.launch_count()
+    step(q, out)
+    launches_per_step = N.launch_count() - n0
+    for _ in range(args.warmup):
+        step(q, out)
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(q, out)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    ev = []
+    step(q, out, ev)
+    torch.cuda.synchronize()
+    launch_ms = max_over_ranks(float(np.mean([ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)])), world)
+    pool.raise_on_status()
+
+    # e2e: each step copies the queries in from pinned host memory and reads
+    # the last layer's output back
+    h_q = q.cpu().pin_memory()
+    h_o = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q = torch.empty_like(q)
+    step(d_q, out)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    f0.record()
+    for _ in range(args.steps):
+        d_q.copy_(h_q, non_blocking=True)
+        step(d_q, out)
+        h_o.copy_(out, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    pool.raise_on_status()
+
+    flops = prefill_flops(w)
+    peak, peak_kind = 1590.0, "fallback"
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        try:
+            peak, peak_kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    value = world * L * flops / (ms_total * 1e-3 / args.steps) / 1e12
+    e2e_value = world * L * flops / (e2e_ms * 1e-3 / args.steps) / 1e12
+    achieved = flops / (launch_ms * 1e-3) / 1e12
+    res = {
+        "metric": "causal prefill attention TFLOP/s (counting the causal half)",
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_total / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w["kv"],
+        "data": "synthetic (seeded codes / N(0,1) KV pages, random block-table permutation, N(0,1) queries)",
+        "tok_per_s": round(world * B * T / (ms_total * 1e-3 / args.steps), 1),
+        "config": {
+            "workload": f"{args.workload}: {w['model']} {L} layers, {hq}q/{hkv}kv heads x d{d}, {w['kv']} KV, "
+                        f"{B} prompts x {T} tokens per GPU, one sckv_prefill_attn per layer",
+            "global_batch": world * B, "seq_len": T, "parallelism": f"sequence-sharded x{world}",
+            "l2": "each layer's K/V (%.2f GB) read by every head group; > L2 for 16-bit pools"
+                  % (B * T * hkv * d * 2 * kv_bytes_per_elem(w["kv"]) / 1e9),
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h_q.numel() * 2),
+                "d2h_bytes_per_step": int(h_o.numel() * 2)},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "prefill_tc_kernel (tcgen05) per layer launch", "flops_per_launch": int(flops),
+                     "avg_launch_ms": round(launch_ms, 4)},
+        "clocks": clocks,
+    }
     pool.close()
     return res
 
@@ -1227,6 +1382,8 @@ def main():
             res = bench_mix(args, w, world, rank, local)
         elif w.get("kind") == "qkv":
             res = bench_qkv(args, w, world, rank, local)
+        elif w.get("kind") == "prefill":
+            res = bench_prefill(args, w, world, rank, local)
         else:
             res = bench_ours(args, w, world, rank, local)
         if rank == 0 and res is not None:
