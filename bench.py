@@ -93,6 +93,11 @@ WORKLOADS = {
     "olmoe-mix-small": dict(kind="mix", model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128,
                             kv="fp16", qdt=torch.float16, batch=32, ctx=(16, 8192), new_per_step=8,
                             prompt=(64, 2048), fork_frac=0.25, prefix=1024, pool_pages=9000, evict_at=0.9),
+    # the paging kernels at OLMoE scale (config 1's append + gather, sized up):
+    # per step append 64 sequences x 64 new tokens into all 16 layers, gather
+    # 256 random all-layer pages into contiguous K/V, copy 256 pages (CoW)
+    "olmoe-paging": dict(kind="paging", model="OLMoE-1B-7B attention", layers=16, hkv=16, d=128, kv="fp16",
+                         batch=64, new_tokens=64, gather_pages=256, copy_pages=256, pool_pages=8192),
     # prompt passes alone: causal prefill attention over whole prompts whose
     # K/V are already in the pages (one sckv_prefill_attn per layer)
     "qwen3-prefill": dict(kind="prefill", model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128,
@@ -568,6 +573,181 @@ def bench_ours(args, w_full, world, rank, local):
         res["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
     pool.close()
     return res
+
+
+# ----------------------------------------------------------------------------- paging kernels
+def bench_paging(args, w, world, rank, local):
+    """One step = one append of `new_tokens` per sequence into every layer
+    (sckv_append), one gather of `gather_pages` random pages into contiguous
+    K / V (sckv_gather) and one copy of `copy_pages` pages (sckv_copy_pages)."""
+    from synapcore_b200 import _native as N
+    from synapcore_b200.pool import KVPool
+
+    dev = torch.device("cuda", local)
+    L, H, d, B, T, P = w["layers"], w["hkv"], w["d"], w["batch"], w["new_tokens"], w["pool_pages"]
+    eb = kv_bytes_per_elem(w["kv"])
+    pool = KVPool(L, H, d, P, w["kv"], device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    view = pool.pool_view()
+    for l in range(L):
+        view[l].normal_(generator=g)
+    mb = (T + PAGE - 1) // PAGE
+    perm = torch.randperm(P, generator=g, device=dev).to(torch.int32)
+    bt = perm[: B * mb].view(B, mb).contiguous()
+    cu = torch.arange(0, B * T + 1, T, dtype=torch.int32, device=dev)
+    start = torch.zeros(B, dtype=torch.int32, device=dev)
+    kn = torch.randn(L, B * T, H, d, device=dev, generator=g).half()
+    vn = torch.randn(L, B * T, H, d, device=dev, generator=g).half()
+    gids = perm[B * mb: B * mb + w["gather_pages"]].contiguous()
+    c0 = B * mb + w["gather_pages"]
+    src = perm[c0: c0 + w["copy_pages"]].contiguous()
+    dst = perm[c0 + w["copy_pages"]: c0 + 2 * w["copy_pages"]].contiguous()
+    nt = w["gather_pages"] * PAGE
+    gk = torch.empty(L, H, nt, d, dtype=torch.float16, device=dev)
+    gv = torch.empty_like(gk)
+    page_bytes = 2 * L * H * PAGE * d * eb
+    bytes_append = L * B * T * H * d * 2 * (2 + eb) + B * mb * 4  # read fp16 source, write pool, block table
+    bytes_gather = w["gather_pages"] * page_bytes + L * H * nt * d * 2 * 2
+    bytes_copy = 2 * w["copy_pages"] * page_bytes
+    kernels = [("append", bytes_append), ("gather", bytes_gather), ("copy", bytes_copy)]
+
+    def step(ev=None):
+        def mark():
+            if ev is not None:
+                ev.append(torch.cuda.Event(enable_timing=True))
+                ev[-1].record()
+        mark()
+        pool.append(kn, vn, cu, start, bt)
+        mark()
+        pool.gather(gids, out=(gk, gv))
+        mark()
+        pool.copy_pages(src, dst)
+        mark()
+
+    n0 = N.launch_count()
+    step()
+    launches_per_step = N.launch_count() - n0
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    per = {k: [] for k, _ in kernels}
+    for _ in range(args.steps):
+        ev = []
+        step(ev)
+        torch.cuda.synchronize()
+        for i, (k, _) in enumerate(kernels):
+            per[k].append(ev[i].elapsed_time(ev[i + 1]))
+    pool.raise_on_status()
+    peak, peak_kind = measured_peak_gbs()
+    sub = {}
+    for k, b in kernels:
+        ms = max_over_ranks(float(np.mean(per[k])), world)
+        sub[k] = {"bytes_per_launch": int(b), "avg_launch_ms": round(ms, 4),
+                  "achieved": round(b / (ms * 1e-3) / 1e9, 1), "frac": round(b / (ms * 1e-3) / 1e9 / peak, 4)}
+
+    # e2e: new K/V rows from pinned host memory each step, gathered K/V read back
+    h_k, h_v = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    h_gk = torch.empty(gk.shape, dtype=gk.dtype).pin_memory()
+    h_gv = torch.empty(gv.shape, dtype=gv.dtype).pin_memory()
+    d_k, d_v = torch.empty_like(kn), torch.empty_like(vn)
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        pool.append(d_k, d_v, cu, start, bt)
+        pool.gather(gids, out=(gk, gv))
+        pool.copy_pages(src, dst)
+        h_gk.copy_(gk, non_blocking=True)
+        h_gv.copy_(gv, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    pool.raise_on_status()
+
+    step_bytes_all = sum(b for _, b in kernels)
+    value = world * step_bytes_all / (ms_total * 1e-3 / args.steps) / 1e9
+    e2e_value = world * step_bytes_all / (e2e_ms * 1e-3 / args.steps) / 1e9
+    top = max(sub, key=lambda k: sub[k]["avg_launch_ms"])
+    res = {
+        "metric": "paging kernels GB/s (append + gather + CoW page copy)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_total / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w["kv"],
+        "data": "synthetic (seeded N(0,1) pages and new rows, random page ids)",
+        "config": {
+            "workload": f"{args.workload}: {w['model']} {L} layers x {H} kv heads x d{d}, {w['kv']} pages of 16 "
+                        f"tokens; per step append {B} x {T} tokens into all layers, gather {w['gather_pages']} "
+                        f"pages, copy {w['copy_pages']} pages; pool {P} pages",
+            "global_batch": world * B, "seq_len": T, "parallelism": f"sequence-sharded x{world}",
+            "l2": "each kernel moves >= 1 GB per launch (>> L2)",
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(2 * h_k.numel() * 2), "d2h_bytes_per_step": int(2 * h_gk.numel() * 2)},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "roofline": {"bound": "hbm", "achieved": sub[top]["achieved"], "peak": peak, "unit": "GB/s",
+                     "frac": sub[top]["frac"], "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"{top} (the step's longest launch)", "bytes_per_launch": sub[top]["bytes_per_launch"],
+                     "avg_launch_ms": sub[top]["avg_launch_ms"]},
+        "kernels": sub,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_gather(w, budget_s=args.cpu_seconds)
+    pool.close()
+    return res
+
+
+def cpu_baseline_gather(w, budget_s: float = 15.0):
+    """The reference's page-by-page NumPy gather (oracle restatement of
+    gather_contiguous_kv_numpy, native/native_engine.py:403-419) of 32 pages."""
+    from oracle.kv_oracle import ArenaOracle
+
+    L, H, d = w["layers"], w["hkv"], w["d"]
+    n = 32
+    ar = ArenaOracle(n, L, H, d, "fp16")
+    rng = np.random.default_rng(0)
+    ar.k[:] = rng.standard_normal(ar.k.shape).astype(np.float16)
+    ar.v[:] = rng.standard_normal(ar.v.shape).astype(np.float16)
+    ids = list(rng.permutation(n))
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        ar.gather_contiguous_kv_numpy(ids)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    page_bytes = 2 * L * H * PAGE * d * 2
+    gbs = reps * 2 * n * page_bytes / el / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
+            or (os.cpu_count() or 1), "kind": "port",
+            "sample": f"gather of {n} fp16 pages ({n * page_bytes / 1e6:.0f} MB), {reps} reps in {el:.1f}s"}
 
 
 # ----------------------------------------------------------------------------- prompt passes
@@ -1384,6 +1564,8 @@ def main():
             res = bench_qkv(args, w, world, rank, local)
         elif w.get("kind") == "prefill":
             res = bench_prefill(args, w, world, rank, local)
+        elif w.get("kind") == "paging":
+            res = bench_paging(args, w, world, rank, local)
         else:
             res = bench_ours(args, w, world, rank, local)
         if rank == 0 and res is not None:

@@ -101,29 +101,39 @@ __device__ __forceinline__ int64_t resolve_page(const Geo& g, const int32_t* bt,
 }
 
 // ---------------------------------------------------------------------------
-// Append, 16-bit pools: one thread per 8-element chunk of a (layer, token, kv, head) row.
+// Append, 16-bit pools: one block per new token. Thread 0 resolves the
+// token's sequence, position and page once; the block then copies the
+// token's rows of every layer, K and V and head in 16-byte chunks (the H
+// rows of one (layer, K|V) are contiguous in the source, 16-token-strided
+// in the page).
 // ---------------------------------------------------------------------------
-__global__ void append16_kernel(Geo g, int layer0, int n_layers, const void* k_new, const void* v_new,
-                                int src_dtype, int n_seqs, int n_tokens, const int32_t* cu,
-                                const int32_t* start_pos, const int32_t* bt, int64_t stride,
-                                int max_blocks) {
-  const int cpr = g.D / 8;  // chunks per row
-  const int64_t total = (int64_t)n_layers * n_tokens * 2 * g.H * cpr;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int c = (int)(i % cpr);
-    int64_t r = i / cpr;
-    int h = (int)(r % g.H); r /= g.H;
-    int kv = (int)(r % 2); r /= 2;
-    int t = (int)(r % n_tokens);
-    int l = (int)(r / n_tokens);
-    int b = sckv_find_seq(cu, n_seqs, t);
-    int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
-    int64_t page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
-    if (page < 0) continue;
+__global__ void __launch_bounds__(256) append16_kernel(Geo g, int layer0, int n_layers, const void* k_new,
+                                                       const void* v_new, int src_dtype, int n_seqs, int n_tokens,
+                                                       const int32_t* cu, const int32_t* start_pos, const int32_t* bt,
+                                                       int64_t stride, int max_blocks) {
+  __shared__ int64_t s_page;
+  __shared__ int s_slot;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const int b = sckv_find_seq(cu, n_seqs, t);
+    const int pos = __ldg(start_pos + b) + (t - __ldg(cu + b));
+    s_page = resolve_page(g, bt, stride, max_blocks, b, pos, KID_APPEND);
+    s_slot = pos % SCKV_PAGE_TOKENS;
+  }
+  __syncthreads();
+  const int64_t page = s_page;
+  if (page < 0) return;
+  const int slot = s_slot;
+  const int cpr = g.D / 8;           // 16-byte chunks per row
+  const int per_pair = g.H * cpr;    // chunks of one (layer, K|V): H rows
+  const int total = n_layers * 2 * per_pair;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int pair = i / per_pair, j = i - pair * per_pair;
+    const int l = pair >> 1, kv = pair & 1;
+    const int h = j / cpr, c = j - h * cpr;
     const void* src = kv ? v_new : k_new;
-    int64_t sidx = (((int64_t)l * n_tokens + t) * g.H + h) * g.D + c * 8;
-    int64_t didx = row_off(g, layer0 + l, page, kv, h, pos % SCKV_PAGE_TOKENS) + c * 8;
+    const int64_t sidx = (((int64_t)l * n_tokens + t) * g.H) * g.D + (int64_t)j * 8;
+    const int64_t didx = row_off(g, layer0 + l, page, kv, h, slot) + c * 8;
     if (src_dtype == g.dtype) {
       *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.data) + didx) =
           *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + sidx);
@@ -408,22 +418,30 @@ __global__ void write_pages_quantized_kernel(Geo g, const int32_t* ids, int n, c
 // Gather: out[l][h][t][D] = pool[layer0+l][ids[t/16]][kv][h][t%16][:] (dequantised).
 // Thread per 8-element chunk.
 // ---------------------------------------------------------------------------
-__global__ void gather_kernel(Geo g, int layer0, int n_layers, const int32_t* ids, int n_pages,
-                              int n_tokens, void* out_k, void* out_v, int out_dtype) {
+__global__ void __launch_bounds__(256) gather_kernel(Geo g, int layer0, int n_layers, const int32_t* ids,
+                                                     int n_pages, int n_tokens, void* out_k, void* out_v,
+                                                     int out_dtype) {
+  // one block per (page of the list, layer): the page's slab of that layer
+  // ([K|V][H][16][D], contiguous) goes to rows 16 i .. 16 i + 15 of every
+  // (K|V, head) plane of the output
+  const int i = blockIdx.x / n_layers;
+  const int l = blockIdx.x - i * n_layers;
+  const int32_t page = __ldg(ids + i);
+  if (page < 0 || page >= g.P) {
+    if (threadIdx.x == 0) sckv_report(g.status, SCKV_ERR_BOUNDS, page, KID_GATHER);
+    return;
+  }
   const int cpr = g.D / 8;
-  const int64_t total = (int64_t)2 * n_layers * g.H * n_tokens * cpr;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = i;
-    int c = (int)(r % cpr); r /= cpr;
-    int t = (int)(r % n_tokens); r /= n_tokens;
-    int h = (int)(r % g.H); r /= g.H;
-    int l = (int)(r % n_layers);
-    int kv = (int)(r / n_layers);
-    int32_t page = __ldg(ids + t / SCKV_PAGE_TOKENS);
-    if (page < 0 || page >= g.P) { sckv_report(g.status, SCKV_ERR_BOUNDS, page, KID_GATHER); continue; }
-    const int slot = t % SCKV_PAGE_TOKENS;
-    const int64_t sidx = row_off(g, layer0 + l, page, kv, h, slot) + c * 8;
+  const int per_head = SCKV_PAGE_TOKENS * cpr;  // chunks of one (K|V, head): 16 rows
+  const int total = 2 * g.H * per_head;
+  const int64_t slab = row_off(g, layer0 + l, page, 0, 0, 0);
+  for (int j = threadIdx.x; j < total; j += blockDim.x) {
+    const int kh = j / per_head, r = j - kh * per_head;
+    const int kv = kh / g.H, h = kh - kv * g.H;
+    const int slot = r / cpr, c = r - slot * cpr;
+    const int t = i * SCKV_PAGE_TOKENS + slot;
+    if (t >= n_tokens) continue;
+    const int64_t sidx = slab + (int64_t)j * 8;
     const int64_t didx = (((int64_t)l * g.H + h) * n_tokens + t) * g.D + c * 8;
     void* out = kv ? out_v : out_k;
     if ((g.dtype == SCKV_DTYPE_F16 || g.dtype == SCKV_DTYPE_BF16) && out_dtype == g.dtype) {
@@ -439,13 +457,13 @@ __global__ void gather_kernel(Geo g, int layer0, int n_layers, const int32_t* id
       uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(g.data) + sidx);
       const int8_t* cb = reinterpret_cast<const int8_t*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __half2float(__float2half_rn(static_cast<float>(cb[j]) * sf));
+      for (int q = 0; q < 8; ++q) v[q] = __half2float(__float2half_rn(static_cast<float>(cb[q]) * sf));
     } else {  // fp8
       const float sf = reinterpret_cast<const float*>(g.scales)[fp8_scale_idx(g, layer0 + l, page, kv, h)];
       uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(g.data) + sidx);
       const uint8_t* cb = reinterpret_cast<const uint8_t*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = sckv_fp8_to_float(cb[j]) * sf;
+      for (int q = 0; q < 8; ++q) v[q] = sckv_fp8_to_float(cb[q]) * sf;
     }
     if (out_dtype == SCKV_DTYPE_F32) {
       float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + didx);
@@ -460,36 +478,32 @@ __global__ void gather_kernel(Geo g, int layer0, int n_layers, const int32_t* id
 // ---------------------------------------------------------------------------
 // Copy-on-write page copy: every layer's slab (and scales) src -> dst.
 // ---------------------------------------------------------------------------
-__global__ void copy_pages_kernel(Geo g, const int32_t* src_ids, const int32_t* dst_ids, int n) {
+__global__ void __launch_bounds__(256) copy_pages_kernel(Geo g, const int32_t* src_ids, const int32_t* dst_ids,
+                                                         int n) {
+  // one block per (page pair, layer): the layer's contiguous slab, then its scales
+  const int pi = blockIdx.x / g.L;
+  const int l = blockIdx.x - pi * g.L;
+  const int32_t s = __ldg(src_ids + pi), d = __ldg(dst_ids + pi);
+  if (s < 0 || s >= g.P || d < 0 || d >= g.P) {
+    if (threadIdx.x == 0) sckv_report(g.status, SCKV_ERR_BOUNDS, (s < 0 || s >= g.P) ? s : d, KID_COPY);
+    return;
+  }
   const int64_t slab_bytes = 2LL * g.H * SCKV_PAGE_TOKENS * g.D * (g.dtype <= SCKV_DTYPE_BF16 ? 2 : 1);
-  const int64_t vec_per_slab = slab_bytes / 16;
-  const int64_t total = (int64_t)n * g.L * vec_per_slab;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t v = i % vec_per_slab;
-    int64_t r = i / vec_per_slab;
-    int l = (int)(r % g.L);
-    int pi = (int)(r / g.L);
-    int32_t s = __ldg(src_ids + pi), d = __ldg(dst_ids + pi);
-    if (s < 0 || s >= g.P || d < 0 || d >= g.P) {
-      sckv_report(g.status, SCKV_ERR_BOUNDS, (s < 0 || s >= g.P) ? s : d, KID_COPY);
-      continue;
-    }
-    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(g.data) + ((int64_t)l * g.P + s) * slab_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.data) + ((int64_t)l * g.P + d) * slab_bytes);
-    dst[v] = src[v];
-    if (v == 0 && g.scales != nullptr) {
-      if (g.dtype == SCKV_DTYPE_INT8) {
-        const int64_t per = 2LL * g.H * SCKV_PAGE_TOKENS;
-        const __half* ss = reinterpret_cast<const __half*>(g.scales) + ((int64_t)l * g.P + s) * per;
-        __half* ds = reinterpret_cast<__half*>(g.scales) + ((int64_t)l * g.P + d) * per;
-        for (int64_t k = 0; k < per; ++k) ds[k] = ss[k];
-      } else {
-        const int64_t per = 2LL * g.H;
-        const float* ss = reinterpret_cast<const float*>(g.scales) + ((int64_t)l * g.P + s) * per;
-        float* ds = reinterpret_cast<float*>(g.scales) + ((int64_t)l * g.P + d) * per;
-        for (int64_t k = 0; k < per; ++k) ds[k] = ss[k];
-      }
+  const int vec_per_slab = (int)(slab_bytes / 16);
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(g.data) + ((int64_t)l * g.P + s) * slab_bytes);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.data) + ((int64_t)l * g.P + d) * slab_bytes);
+  for (int v = threadIdx.x; v < vec_per_slab; v += blockDim.x) dst[v] = src[v];
+  if (g.scales != nullptr) {
+    if (g.dtype == SCKV_DTYPE_INT8) {
+      const int per = 2 * g.H * SCKV_PAGE_TOKENS;
+      const __half* ss = reinterpret_cast<const __half*>(g.scales) + ((int64_t)l * g.P + s) * per;
+      __half* ds = reinterpret_cast<__half*>(g.scales) + ((int64_t)l * g.P + d) * per;
+      for (int k = threadIdx.x; k < per; k += blockDim.x) ds[k] = ss[k];
+    } else {
+      const int per = 2 * g.H;
+      const float* ss = reinterpret_cast<const float*>(g.scales) + ((int64_t)l * g.P + s) * per;
+      float* ds = reinterpret_cast<float*>(g.scales) + ((int64_t)l * g.P + d) * per;
+      for (int k = threadIdx.x; k < per; k += blockDim.x) ds[k] = ss[k];
     }
   }
 }
@@ -631,8 +645,8 @@ extern "C" int sckv_append(sckv_pool* p, int layer0, int n_layers, const void* k
   cudaStream_t s = as_stream(stream);
   SCKV_CUDA_CHECK(cudaSetDevice(p->device));
   if (p->kv_dtype == SCKV_DTYPE_F16 || p->kv_dtype == SCKV_DTYPE_BF16) {
-    int64_t work = (int64_t)n_layers * n_tokens * 2 * p->num_kv_heads * (p->head_dim / 8);
-    append16_kernel<<<grid_for(p, work, 256), 256, 0, s>>>(g, layer0, n_layers, k_new, v_new, src_dtype, n_seqs,
+    // one block per new token
+    append16_kernel<<<n_tokens, 256, 0, s>>>(g, layer0, n_layers, k_new, v_new, src_dtype, n_seqs,
                                                            n_tokens, cu_tokens, start_pos, block_table, bt_stride,
                                                            max_blocks);
   } else if (p->kv_dtype == SCKV_DTYPE_INT8) {
@@ -702,9 +716,11 @@ extern "C" int sckv_gather(sckv_pool* p, int layer0, int n_layers, const int32_t
   if ((reinterpret_cast<uintptr_t>(out_k) | reinterpret_cast<uintptr_t>(out_v)) & 15) return SCKV_ERR_ALIGNMENT;
   Geo g = geo_of(p);
   SCKV_CUDA_CHECK(cudaSetDevice(p->device));
-  int64_t work = (int64_t)2 * n_layers * p->num_kv_heads * n_tokens * (p->head_dim / 8);
-  gather_kernel<<<grid_for(p, work, 256), 256, 0, as_stream(stream)>>>(g, layer0, n_layers, ids, n_pages, n_tokens,
-                                                                       out_k, out_v, out_dtype);
+  // one block per (listed page holding gathered tokens, layer)
+  const int64_t blocks = (int64_t)((n_tokens + SCKV_PAGE_TOKENS - 1) / SCKV_PAGE_TOKENS) * n_layers;
+  if (blocks > INT32_MAX) return SCKV_ERR_INVALID_ARG;
+  gather_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(g, layer0, n_layers, ids, n_pages, n_tokens, out_k,
+                                                                 out_v, out_dtype);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
@@ -715,9 +731,10 @@ extern "C" int sckv_copy_pages(sckv_pool* p, const int32_t* src_ids, const int32
   if (!src_ids || !dst_ids) return SCKV_ERR_INVALID_ARG;
   Geo g = geo_of(p);
   SCKV_CUDA_CHECK(cudaSetDevice(p->device));
-  const int64_t slab_bytes = sckv_slab_elems(p) * sckv_elem_bytes(p->kv_dtype);
-  int64_t work = (int64_t)n * p->num_layers * (slab_bytes / 16);
-  copy_pages_kernel<<<grid_for(p, work, 256), 256, 0, as_stream(stream)>>>(g, src_ids, dst_ids, n);
+  // one block per (page pair, layer)
+  const int64_t blocks = (int64_t)n * p->num_layers;
+  if (blocks > INT32_MAX) return SCKV_ERR_INVALID_ARG;
+  copy_pages_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(g, src_ids, dst_ids, n);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
