@@ -893,6 +893,8 @@ def bench_prefill(args, w, world, rank, local):
                      "avg_launch_ms": round(launch_ms, 4)},
         "clocks": clocks,
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_prefill(w, budget_s=args.cpu_seconds)
     pool.close()
     return res
 
@@ -1495,20 +1497,61 @@ def cpu_baseline(w, budget_s: float = 15.0):
                       f"{w['batch'] * gbs * 1e9 / (w['layers'] * attn_bytes_per_launch(w, [T] * w['batch'])):.3f}"}
 
 
+def cpu_baseline_prefill(w, budget_s: float = 15.0):
+    """The reference's NumPy causal prompt pass (oracle restatement of
+    models/adapters.py:1209-1229 with its -1e9 mask) on one layer of one
+    256-token prompt, repeated for ~budget_s."""
+    from oracle.kv_oracle import sdpa_prefill
+
+    rng = np.random.default_rng(0)
+    T, hq, hkv, d = 256, w["hq"], w["hkv"], w["d"]
+    q = rng.standard_normal((T, hq, d)).astype(np.float32)
+    k = rng.standard_normal((hkv, T, d)).astype(np.float16)
+    v = rng.standard_normal((hkv, T, d)).astype(np.float16)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        sdpa_prefill(q, k, v, 0)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    tflops = reps * 4 * hq * d * (T * (T + 1) // 2) / el / 1e12
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
+            or (os.cpu_count() or 1), "kind": "port",
+            "sample": f"1 layer x one {T}-token prompt, {reps} reps in {el:.1f}s"}
+
+
 def bench_reference(args, w, world, rank):
     if rank != 0:
         return None
     steps = []
-    qkv = w.get("kind") == "qkv"
+    kind = w.get("kind")
+    qkv = kind == "qkv"
+    budget = args.cpu_seconds / max(1, args.steps)
     for i in range(args.warmup + args.steps):
         if qkv:
-            r = cpu_baseline_qkv(w, w["tokens_per_seq"] > 1, budget_s=args.cpu_seconds / max(1, args.steps))
+            r = cpu_baseline_qkv(w, w["tokens_per_seq"] > 1, budget_s=budget)
+        elif kind == "prefill":
+            r = cpu_baseline_prefill(w, budget_s=budget)
+        elif kind == "paging":
+            r = cpu_baseline_gather(w, budget_s=budget)
         else:
-            r = cpu_baseline(w, budget_s=args.cpu_seconds / max(1, args.steps))
+            r = cpu_baseline(w, budget_s=budget)
         if i >= args.warmup:
             steps.append(r["value"])
     val = float(np.mean(steps))
     cores = os.cpu_count() or 1
+    if kind in ("prefill", "paging"):
+        return {"metric": ("causal prefill attention TFLOP/s (counting the causal half)" if kind == "prefill"
+                           else "paging kernels GB/s (append + gather + CoW page copy)"),
+                "impl": "reference", "value": round(val, 6), "unit": r["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": w["kv"], "data": "synthetic (seeded)",
+                "config": {"workload": f"{args.workload}: reference NumPy path on a bounded host sample",
+                           "parallelism": "host cores"},
+                "cpu_baseline": {"value": round(val, 6), "unit": r["unit"], "cores": cores, "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": round(val, 6), "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if qkv:
         return {"metric": ("fused q/k/v projection + QK-norm + RoPE + KV append " +
                            ("TFLOP/s" if w["tokens_per_seq"] > 1 else "GB/s (weights + activations)")),
