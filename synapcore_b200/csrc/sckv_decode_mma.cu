@@ -204,6 +204,32 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         qf[nq][s][1] = pack2<kBF16>(v2, v3);
       }
     }
+    // int8: K codes enter the score MMAs offset by +1152 (cvt_b8x4_biased),
+    // so a score row carries 1152 * sum_d q[d] extra, removed per page below
+    // (one page's 128-dim dot product: no precision issue). V codes stay
+    // exact: an offset there would grow with the context inside the
+    // tensor-core accumulator.
+    float qcorr[NQT][2];
+#pragma unroll
+    for (int nq = 0; nq < NQT; ++nq) {
+      qcorr[nq][0] = qcorr[nq][1] = 0.f;
+      if (kINT8) {
+        float part = 0.f;  // this lane's 32 dims of q row 8 nq + g, as the MMA sees them (f16)
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+#pragma unroll
+          for (int r2 = 0; r2 < 2; ++r2) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qf[nq][s][r2]));
+            part += f.x + f.y;
+          }
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        // score columns of this lane are q rows 2t and 2t + 1 (held by lanes 4 (2t + c))
+#pragma unroll
+        for (int c = 0; c < 2; ++c) qcorr[nq][c] = 1152.f * __shfl_sync(0xffffffffu, part, 4 * (2 * t + c));
+      }
+    }
     float acc[NQT][8][4];
     float m[NQT][2], l[NQT][2];
 #pragma unroll
@@ -262,12 +288,12 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
               uint32_t w0, w1, w2, w3;
               ldsm_x4(sK + row * 128 + ((chunk ^ (row & 7)) << 4), w0, w1, w2, w3);
               uint32_t a[4];
-              cvt_b8x4<KVDT>(w0, a[0], a[2]);
-              cvt_b8x4<KVDT>(w1, a[1], a[3]);
+              cvt_b8x4_biased<KVDT>(w0, a[0], a[2]);
+              cvt_b8x4_biased<KVDT>(w1, a[1], a[3]);
 #pragma unroll
               for (int nq = 0; nq < NQT; ++nq) mma16816<false>(sc[nq], a, qf[nq][2 * c2][0], qf[nq][2 * c2][1]);
-              cvt_b8x4<KVDT>(w2, a[0], a[2]);
-              cvt_b8x4<KVDT>(w3, a[1], a[3]);
+              cvt_b8x4_biased<KVDT>(w2, a[0], a[2]);
+              cvt_b8x4_biased<KVDT>(w3, a[1], a[3]);
 #pragma unroll
               for (int nq = 0; nq < NQT; ++nq)
                 mma16816<false>(sc2[nq], a, qf[nq][2 * c2 + 1][0], qf[nq][2 * c2 + 1][1]);
@@ -301,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         for (int nq = 0; nq < NQT; ++nq) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const float sA = (g < nv) ? (sc[nq][c] + sc2[nq][c]) * sscaleA : -INFINITY;
-            const float sB = (g + 8 < nv) ? (sc[nq][2 + c] + sc2[nq][2 + c]) * sscaleB : -INFINITY;
+            const float sA = (g < nv) ? (sc[nq][c] + sc2[nq][c] - qcorr[nq][c]) * sscaleA : -INFINITY;
+            const float sB = (g + 8 < nv) ? (sc[nq][2 + c] + sc2[nq][2 + c] - qcorr[nq][c]) * sscaleB : -INFINITY;
             sv[nq][c] = sA;
             sv[nq][2 + c] = sB;
             grow |= (fmaxf(sA, sB) > m[nq][c] + 8.f);

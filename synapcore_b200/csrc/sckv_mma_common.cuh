@@ -118,6 +118,20 @@ __device__ __forceinline__ void cvt_b8x4(uint32_t x, uint32_t& lo, uint32_t& hi)
   else cvt_fp8x4(x, lo, hi);
 }
 
+// As cvt_b8x4, but int8 codes come out offset by +1152 (the f16 1024 + u
+// before the subtraction): for callers that remove the offset from whole
+// dot products instead of from every code.
+template <int KVDT>
+__device__ __forceinline__ void cvt_b8x4_biased(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  if (KVDT == SCKV_DTYPE_INT8) {
+    const uint32_t u = x ^ 0x80808080u;
+    lo = __byte_perm(u, 0x64646464u, 0x4140);
+    hi = __byte_perm(u, 0x64646464u, 0x4342);
+  } else {
+    cvt_fp8x4(x, lo, hi);
+  }
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if (BF16) {
