@@ -64,6 +64,11 @@ WORKLOADS = {
                         qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
     "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                             qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
+    # config 2 with the reference arena's int8 mode, and with FP8 pages
+    "olmoe-int8": dict(model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="int8",
+                       qdt=torch.float16, batch=64, ctx=4096, pool_pages=18750),
+    "olmoe-fp8": dict(model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="fp8_e4m3",
+                      qdt=torch.float16, batch=64, ctx=4096, pool_pages=18750),
     # config 4 with the reference arena's int8 mode (per-token fp16 scales)
     "qwen3-int8": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="int8",
                        qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
@@ -564,7 +569,8 @@ def bench_ours(args, w_full, world, rank, local):
         "gpu_launches": int(args.steps * L * 3),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": ("decode_mma_kernel" if w["hq"] // w["hkv"] >= 2 else "decode_kernel")
+                     "kernel": ("decode_mma_kernel" if (w["hq"] // w["hkv"] >= 2 or kv_bytes_per_elem(w["kv"]) == 1)
+                                else "decode_kernel")
                                + " (+combine) per layer launch",
                      "bytes_per_launch": int(avg_launch_bytes), "avg_launch_ms": round(attn_avg_ms, 4)},
         "clocks": clocks,

@@ -494,6 +494,10 @@ bool use_tensor_core_path(const sckv_pool* pool, int G, int q_dtype) {
   if (pool->kv_dtype == SCKV_DTYPE_BF16 && q_dtype != SCKV_DTYPE_BF16) return false;
   if (G > 16) return false;
   if (forced >= 0) return forced == 1;
+  // one-byte pages: decoding the codes costs the same per page whatever G
+  // is, and the tensor-core kernel does it with fewer instructions than the
+  // CUDA-core one, so it takes MHA pools too
+  if (pool->kv_dtype == SCKV_DTYPE_INT8 || pool->kv_dtype == SCKV_DTYPE_FP8_E4M3) return true;
   return G >= 2;
 }
 
