@@ -356,6 +356,12 @@ SCKV_API int sckv_alloc_state(const sckv_pool* pool, int64_t out[5], void* strea
 SCKV_API int sckv_get_status(const sckv_pool* pool, int32_t out[4], void* stream);
 SCKV_API int sckv_clear_status(sckv_pool* pool, void* stream);
 
+/* Failure-path self test: one kernel waits (bounded, limit_us <= 2 s) on a
+ * barrier nothing completes, gives up and records SCKV_ERR_TIMEOUT (detail
+ * -1) in the status word, exactly as a stalled pipeline kernel would; the
+ * context stays usable. No counterpart in the reference. */
+SCKV_API int sckv_selftest_wait_timeout(sckv_pool* pool, unsigned limit_us, void* stream);
+
 /* ========================================================================== */
 /* KV prefix hash table (host, C++)                                            */
 /* ========================================================================== */

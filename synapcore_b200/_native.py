@@ -100,6 +100,7 @@ _SIGNATURES = [
     ("sckv_alloc_state", c_int, [c_void_p, POINTER(c_int64), c_void_p]),
     ("sckv_get_status", c_int, [c_void_p, POINTER(c_int32), c_void_p]),
     ("sckv_clear_status", c_int, [c_void_p, c_void_p]),
+    ("sckv_selftest_wait_timeout", c_int, [c_void_p, ctypes.c_uint, c_void_p]),
     ("sckv_kv_lookup", c_int, [c_void_p, c_void_p, POINTER(c_uint32)]),
     ("sckv_kv_insert", c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_double, c_void_p, POINTER(c_uint64)]),
     ("sckv_version", ctypes.c_char_p, []),

@@ -29,6 +29,7 @@ enum SckvKernelId : int32_t {
   KID_RESERVE = 12,
   KID_PREFILL = 13,
   KID_QKV = 14,
+  KID_SELFTEST = 15,
 };
 
 // Allocator control words (int64, device).

@@ -170,6 +170,33 @@ extern "C" int sckv_clear_status(sckv_pool* p, void* stream) {
   return SCKV_OK;
 }
 
+namespace {
+
+// Waits on an mbarrier nothing ever arrives on, with the bounded wait every
+// pipeline kernel uses: it gives up after limit_ns and records
+// SCKV_ERR_TIMEOUT (detail -1) in the pool's status word, as a stalled
+// pipeline would.
+__global__ void selftest_wait_kernel(int32_t* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_bounded(&bar, 0, limit_ns))
+    sckv_report(status, SCKV_ERR_TIMEOUT, -1, KID_SELFTEST);
+}
+
+}  // namespace
+
+extern "C" int sckv_selftest_wait_timeout(sckv_pool* p, unsigned limit_us, void* stream) {
+  if (p == nullptr || limit_us == 0 || limit_us > 2000000u) return SCKV_ERR_INVALID_ARG;
+  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(p->status, (uint64_t)limit_us * 1000ull);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
 extern "C" const char* sckv_version(void) { return "sckv 0.1.0 sm_100a"; }
 
 extern "C" const char* sckv_last_error(void) { return sckv_error_buffer(); }

@@ -538,6 +538,12 @@ class KVPool:
         N.check(self.lib.sckv_get_status(self.handle, arr, _stream_ptr(stream)), "sckv_get_status")
         return int(arr[0]), int(arr[1]), int(arr[2]), int(arr[3])
 
+    def selftest_wait_timeout(self, limit_us: int = 20000, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Launch a kernel whose bounded wait runs out (nothing completes its
+        barrier): afterwards status() reads SCKV_ERR_TIMEOUT, detail -1."""
+        N.check(self.lib.sckv_selftest_wait_timeout(self.handle, int(limit_us), _stream_ptr(stream)),
+                "sckv_selftest_wait_timeout")
+
     def clear_status(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         N.check(self.lib.sckv_clear_status(self.handle, _stream_ptr(stream)), "sckv_clear_status")
 

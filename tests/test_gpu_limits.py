@@ -93,3 +93,45 @@ def test_prefill_fills_block_table_to_the_last_slot(cuda_device):
     assert _rel(got.cpu().numpy(), ref) <= TOL
     assert sorted(cache.page_ids("s")) == list(range(mb))
     cache.check()
+
+
+def test_bounded_wait_runs_out_reports_timeout_and_context_survives(cuda_device):
+    """A kernel whose barrier nothing completes gives up after its limit and
+    reports SCKV_ERR_TIMEOUT through the status word; the context keeps
+    working (a decode afterwards matches the oracle)."""
+    import time
+
+    import numpy as np
+    import torch
+
+    from oracle.kv_oracle import PagedPoolOracle
+    from synapcore_b200 import _native as N
+    from synapcore_b200.pool import KVPool
+
+    pool = KVPool(1, 2, 128, 8, "fp16", device=cuda_device)
+    t0 = time.perf_counter()
+    pool.selftest_wait_timeout(20000)  # 20 ms
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    code, detail, kernel, count = pool.status()
+    assert code == N.SCKV_ERR_TIMEOUT and detail == -1 and count == 1
+    assert 0.015 <= dt < 2.0
+    with pytest.raises(N.SCKVError):
+        pool.raise_on_status()
+    pool.clear_status()
+    assert pool.status()[0] == 0
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((8, 1, 2, 16, 128)).astype(np.float16)
+    v = rng.standard_normal((8, 1, 2, 16, 128)).astype(np.float16)
+    ids = np.arange(8, dtype=np.int32)
+    pool.write_pages(torch.from_numpy(ids).to(cuda_device), torch.from_numpy(k).to(cuda_device),
+                     torch.from_numpy(v).to(cuda_device))
+    ora = PagedPoolOracle(1, 2, 128, 8, "fp16")
+    ora.write_pages(ids, k.astype(np.float32), v.astype(np.float32))
+    q = rng.standard_normal((1, 8, 128)).astype(np.float16)
+    bt = ids.reshape(1, 8)
+    out = pool.decode_attn(0, torch.from_numpy(q).to(cuda_device), torch.from_numpy(bt).to(cuda_device),
+                           torch.tensor([100], dtype=torch.int32, device=cuda_device), out_dtype=torch.float32)
+    ref = ora.decode(0, q.astype(np.float32), bt, np.array([100]))
+    assert float(np.max(np.abs(out.cpu().numpy() - ref)) / np.max(np.abs(ref))) <= 2e-3
+    pool.close()
