@@ -66,7 +66,9 @@ struct QkvParams {
   int32_t* status;
   const __half* q_norm_w;  // [128] or null
   const __half* k_norm_w;  // [128] or null
-  const float2* rope_cs;   // [n_tok][64] (cos, sin)
+  const float2* rope_cs;   // [n_tok][64] (cos, sin); null when split (the finish kernel computes them)
+  const float* inv_freq;   // [64]
+  float rope_scaling;
   float* partial;          // split-K: [k_splits][n_tok][hd_total] fp32 sums, else null
   const int32_t* cu;
   const int32_t* start_pos;
@@ -198,11 +200,16 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
   }
   float y[4] = {x[0], x[1], x[2], x[3]};
   if (kind < 2) {
+    // cos / sin of this token's position, the operations of rope_table_kernel
+    const int b = sckv_find_seq(p.cu, p.n_seqs, t);
+    const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
+    const float fpos = __fdiv_rn((float)pos, p.rope_scaling);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const float2 cs = __ldg(p.rope_cs + (int64_t)t * kRopePairs + lane + 32 * i);
-      y[i] = __fsub_rn(__fmul_rn(x[i], cs.x), __fmul_rn(x[i + 2], cs.y));
-      y[i + 2] = __fadd_rn(__fmul_rn(x[i + 2], cs.x), __fmul_rn(x[i], cs.y));
+      float sn, cn;
+      sincosf(__fmul_rn(fpos, __ldg(p.inv_freq + lane + 32 * i)), &sn, &cn);
+      y[i] = __fsub_rn(__fmul_rn(x[i], cn), __fmul_rn(x[i + 2], sn));
+      y[i + 2] = __fadd_rn(__fmul_rn(x[i + 2], cn), __fmul_rn(x[i], sn));
     }
   }
   int64_t dst;
@@ -541,6 +548,8 @@ int qkv_steps_per_split(int64_t n_tokens, int64_t n_heads, int hidden, int num_s
   const int nk = (hidden + kQkvBK - 1) / kQkvBK;
   const int64_t ctas = ((n_tokens + kQkvBM - 1) / kQkvBM) * n_heads;
   if (ctas * 2 > num_sms || nk < 8) return nk;
+  // about one tile per SM (two per SM measured slower: the finishing pass
+  // then reads twice the partial sums)
   int64_t ks = num_sms / ctas;
   ks = ks < 2 ? 2 : (ks > 8 ? 8 : ks);
   if (ks > nk / 4) ks = nk / 4;
@@ -632,10 +641,14 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   cudaStream_t s = as_stream(stream);
   SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
   float2* cs = reinterpret_cast<float2*>(workspace);
-  const int64_t n_cs = (int64_t)n_tokens * kRopePairs;
-  rope_table_kernel<<<(unsigned)((n_cs + 255) / 256), 256, 0, s>>>(inv_freq, rope_scaling, n_seqs, n_tokens,
-                                                                     cu_tokens, start_pos, cs);
-  SCKV_LAUNCH_CHECK();
+  if (k_splits == 1) {
+    // the fused epilogue reads a per-token cos / sin table; the split-K
+    // finish kernel computes its own
+    const int64_t n_cs = (int64_t)n_tokens * kRopePairs;
+    rope_table_kernel<<<(unsigned)((n_cs + 255) / 256), 256, 0, s>>>(inv_freq, rope_scaling, n_seqs, n_tokens,
+                                                                       cu_tokens, start_pos, cs);
+    SCKV_LAUNCH_CHECK();
+  }
 
   QkvParams prm{};
   prm.q_out = q_out;
@@ -643,7 +656,9 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.status = pool->status;
   prm.q_norm_w = q_norm_len ? reinterpret_cast<const __half*>(q_norm_w) : nullptr;
   prm.k_norm_w = k_norm_len ? reinterpret_cast<const __half*>(k_norm_w) : nullptr;
-  prm.rope_cs = cs;
+  prm.rope_cs = k_splits == 1 ? cs : nullptr;
+  prm.inv_freq = inv_freq;
+  prm.rope_scaling = rope_scaling;
   prm.cu = cu_tokens;
   prm.start_pos = start_pos;
   prm.bt = block_table;
