@@ -103,6 +103,10 @@ WORKLOADS = {
     # 256 random all-layer pages into contiguous K/V, copy 256 pages (CoW)
     "olmoe-paging": dict(kind="paging", model="OLMoE-1B-7B attention", layers=16, hkv=16, d=128, kv="fp16",
                          batch=64, new_tokens=64, gather_pages=256, copy_pages=256, pool_pages=8192),
+    # the same launches on a 2 GB pool, for profiler captures
+    "olmoe-paging-small": dict(kind="paging", model="OLMoE-1B-7B attention", layers=16, hkv=16, d=128,
+                               kv="fp16", batch=64, new_tokens=64, gather_pages=256, copy_pages=128,
+                               pool_pages=1024),
     # prompt passes alone: causal prefill attention over whole prompts whose
     # K/V are already in the pages (one sckv_prefill_attn per layer)
     "qwen3-prefill": dict(kind="prefill", model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128,
