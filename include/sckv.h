@@ -175,9 +175,13 @@ SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
  * chunk_pages : pages per split (split-K unit); <= 0 picks one. A fixed
  *               value makes each sequence's result independent of the batch.
  * workspace   : device scratch of sckv_decode_workspace_bytes bytes.
- * Pool dtypes F16, BF16, FP8_E4M3 (per-page-head scale) and INT8
- * (per-token fp16 scales, num_q_heads / num_kv_heads in {1, 2, 4, 8});
- * accumulation is fp32. */
+ * Pool dtypes F16, BF16 (bf16 queries for the tensor-core kernel),
+ * FP8_E4M3 (per-page-head scale) and INT8 (per-token fp16 scales);
+ * num_q_heads / num_kv_heads <= 16. Kernel choice: tensor cores (mma.sync,
+ * TMA page boxes) for FP8 / INT8 pools and for G = num_q_heads /
+ * num_kv_heads >= 2; CUDA cores for 16-bit MHA pools.
+ * SCKV_DECODE_KERNEL=simt|mma overrides (the CUDA-core kernel takes INT8
+ * only with G in {1, 2, 4, 8}). Accumulation is fp32. */
 SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype,
                      int num_q_heads, const int32_t* block_table,
                      int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
