@@ -122,6 +122,12 @@ WORKLOADS = {
                       kv="bf16", batch=128, tokens_per_seq=1, ctx=16384),
     "qwen3-qkv-prefill": dict(kind="qkv", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
                               kv="bf16", batch=8, tokens_per_seq=1024, ctx=0),
+    # the other side: o_proj of the fp32 attention output with fp16 weights
+    # (models/adapters.py:1231), one sckv_o_proj per layer
+    "qwen3-oproj": dict(kind="oproj", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
+                        kv="fp16", batch=128, tokens_per_seq=1, ctx=0),
+    "qwen3-oproj-prefill": dict(kind="oproj", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8,
+                                d=128, kv="fp16", batch=8, tokens_per_seq=1024, ctx=0),
 }
 
 
@@ -911,11 +917,18 @@ def bench_prefill(args, w, world, rank, local):
 
 # ----------------------------------------------------------------------------- fused attention input
 def qkv_flops(w, n_tok: int) -> int:
+    if w["kind"] == "oproj":
+        return 2 * n_tok * w["hq"] * w["d"] * w["hidden"]
     return 2 * n_tok * w["hidden"] * (w["hq"] + 2 * w["hkv"]) * w["d"]
 
 
 def qkv_bytes(w, n_tok: int) -> int:
-    """Algorithmic bytes of one layer launch: weights + x read, q_out + K/V rows written (bf16)."""
+    """Algorithmic bytes of one layer launch: weights + x read, q_out + K/V
+    rows written (bf16); for o_proj the fp16 weights, the fp32 attention
+    output read and the fp32 result written."""
+    if w["kind"] == "oproj":
+        fin = w["hq"] * w["d"]
+        return 2 * fin * w["hidden"] + 4 * n_tok * fin + 4 * n_tok * w["hidden"]
     hd = (w["hq"] + 2 * w["hkv"]) * w["d"]
     return 2 * (hd * w["hidden"] + n_tok * w["hidden"] + n_tok * hd)
 
@@ -932,29 +945,42 @@ def bench_qkv(args, w, world, rank, local):
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     scale = hidden ** -0.5
-    wq = [torch.randn(hq * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
-    wk = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
-    wv = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
-    qn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
-    kn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
-    x = torch.randn(L, n_tok, hidden, device=dev, generator=g).to(torch.bfloat16)
+    oproj = w["kind"] == "oproj"
     ctx0 = w["ctx"]
-    mb = (ctx0 + tps + PAGE - 1) // PAGE
-    # only the pages the new tokens land in exist; earlier blocks are never touched
-    b0 = ctx0 // PAGE
-    nb = mb - b0
-    pool = KVPool(L, H, d, B * nb, w["kv"], device=dev)
-    bt = torch.zeros(B, mb, dtype=torch.int32, device=dev)
-    bt[:, b0:] = torch.arange(B * nb, dtype=torch.int32, device=dev).view(B, nb)
-    cu = torch.arange(0, n_tok + 1, tps, dtype=torch.int32, device=dev)
-    start = torch.full((B,), ctx0, dtype=torch.int32, device=dev)
-    inv = rope_inv_freq(1e6, d, dev)
-    q_out = torch.empty(L, n_tok, hq, d, dtype=torch.bfloat16, device=dev)
+    if oproj:
+        # fp32 attention outputs (as the reference's attn_out) and fp16 weights
+        fin = hq * d
+        wo = [torch.randn(hidden, fin, device=dev, generator=g).mul_(fin ** -0.5).half() for _ in range(L)]
+        x = torch.randn(L, n_tok, fin, device=dev, generator=g)
+        q_out = torch.empty(L, n_tok, hidden, dtype=torch.float32, device=dev)
+        pool = KVPool(1, H, d, 4, w["kv"], device=dev)
 
-    def step(xs, outs):
-        for l in range(L):
-            pool.qkv_append(l, xs[l], wq[l], wk[l], wv[l], cu, start, bt, inv, q_norm_w=qn, k_norm_w=kn,
-                            q_out=outs[l])
+        def step(xs, outs):
+            for l in range(L):
+                pool.o_proj(xs[l], wo[l], out=outs[l])
+    else:
+        wq = [torch.randn(hq * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+        wk = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+        wv = [torch.randn(H * d, hidden, device=dev, generator=g).mul_(scale).to(torch.bfloat16) for _ in range(L)]
+        qn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+        kn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+        x = torch.randn(L, n_tok, hidden, device=dev, generator=g).to(torch.bfloat16)
+        mb = (ctx0 + tps + PAGE - 1) // PAGE
+        # only the pages the new tokens land in exist; earlier blocks are never touched
+        b0 = ctx0 // PAGE
+        nb = mb - b0
+        pool = KVPool(L, H, d, B * nb, w["kv"], device=dev)
+        bt = torch.zeros(B, mb, dtype=torch.int32, device=dev)
+        bt[:, b0:] = torch.arange(B * nb, dtype=torch.int32, device=dev).view(B, nb)
+        cu = torch.arange(0, n_tok + 1, tps, dtype=torch.int32, device=dev)
+        start = torch.full((B,), ctx0, dtype=torch.int32, device=dev)
+        inv = rope_inv_freq(1e6, d, dev)
+        q_out = torch.empty(L, n_tok, hq, d, dtype=torch.bfloat16, device=dev)
+
+        def step(xs, outs):
+            for l in range(L):
+                pool.qkv_append(l, xs[l], wq[l], wk[l], wv[l], cu, start, bt, inv, q_norm_w=qn, k_norm_w=kn,
+                                q_out=outs[l])
 
     # a step is launch-bound at decode sizes (host work per call ~ the
     # kernel's time), so each step is replayed from a CUDA graph, as a
@@ -1067,7 +1093,8 @@ def bench_qkv(args, w, world, rank, local):
     e2e_value = world * L * per_launch / (e2e_ms * 1e-3 / args.steps)
     achieved = per_launch / (launch_ms * 1e-3)
     res = {
-        "metric": ("fused q/k/v projection + QK-norm + RoPE + KV append " +
+        "metric": (("attention output projection (o_proj) " if oproj else
+                    "fused q/k/v projection + QK-norm + RoPE + KV append ") +
                    ("TFLOP/s" if prefill else "GB/s (weights + activations)")),
         "value": round(value, 2),
         "unit": unit,
@@ -1078,26 +1105,33 @@ def bench_qkv(args, w, world, rank, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) hidden states, N(0,1/hidden) weights)",
+        "dtype": "fp32 x fp16 (hi + lo)" if oproj else "bf16",
+        "data": ("synthetic (seeded N(0,1) fp32 attention outputs, N(0,1/in) fp16 weights)" if oproj else
+                 "synthetic (seeded N(0,1) hidden states, N(0,1/hidden) weights)"),
         "tok_per_s": round(world * n_tok / (ms_step * 1e-3), 1),
         "config": {
-            "workload": f"{args.workload}: {w['model']} {L} layers, hidden {hidden}, {hq}q/{H}kv heads x d{d}, "
-                        f"per-head QK-norm, RoPE, bf16 pool; {B} sequences x {tps} new token(s) at position "
-                        f"{ctx0} per step, one sckv_qkv_append per layer",
+            "workload": (f"{args.workload}: {w['model']} {L} layers, o_proj [{hq * d} -> {hidden}] fp16 weights, "
+                         f"fp32 attention output of {B} sequences x {tps} token(s) per step, one sckv_o_proj per "
+                         f"layer (fp32 result)" if oproj else
+                         f"{args.workload}: {w['model']} {L} layers, hidden {hidden}, {hq}q/{H}kv heads x d{d}, "
+                         f"per-head QK-norm, RoPE, bf16 pool; {B} sequences x {tps} new token(s) at position "
+                         f"{ctx0} per step, one sckv_qkv_append per layer"),
             "global_batch": world * n_tok,
             "seq_len": tps,
             "parallelism": f"sequence-sharded x{world}",
             "l2": "weights of all layers (%.1f GB) >> L2; each layer's weights are read once per step"
-                  % (L * 2 * (hq + 2 * H) * d * hidden / 1e9),
+                  % (L * 2 * (hq * d * hidden if oproj else (hq + 2 * H) * d * hidden) / 1e9),
         },
-        "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": int(h_x.numel() * 2),
-                "d2h_bytes_per_step": int(h_q[0].numel() * 2)},
+        "e2e": {"value": round(e2e_value, 2), "unit": unit,
+                "h2d_bytes_per_step": int(h_x.numel() * h_x.element_size()),
+                "d2h_bytes_per_step": int(h_q[0].numel() * h_q[0].element_size())},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor" if prefill else "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": unit, "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "qkv_append_kernel + rope_table_kernel (+ qkv_finish_kernel when the hidden dim is "
-                               "split) per layer (CUDA-graph replay, step time / layers)",
+                     "kernel": ("split_hi_lo_kernel + qkv_append_kernel (plain mode) (+ qkv_finish_kernel when "
+                                "in_features is split) per layer (CUDA-graph replay, step time / layers)" if oproj
+                                else "qkv_append_kernel + rope_table_kernel (+ qkv_finish_kernel when the hidden "
+                                     "dim is split) per layer (CUDA-graph replay, step time / layers)"),
                      ("flops_per_launch" if prefill else "bytes_per_launch"): int(flops if prefill else nbytes),
                      "avg_launch_ms": round(launch_ms, 4)},
         "clocks": clocks,
@@ -1111,10 +1145,28 @@ def bench_qkv(args, w, world, rank, local):
 def cpu_baseline_qkv(w, prefill: bool, budget_s: float = 15.0):
     """The reference's NumPy projections + QK-norm + RoPE (oracle restatement of
     models/adapters.py:1167-1194) on one layer x 32 tokens, repeated for ~budget_s."""
-    from oracle.kv_oracle import qk_norm_rope, qkv_project, rope_inv_freq
+    from oracle.kv_oracle import o_project, qk_norm_rope, qkv_project, rope_inv_freq
 
     rng = np.random.default_rng(0)
     n, hidden, hq, H, d = 32, w["hidden"], w["hq"], w["hkv"], w["d"]
+    if w["kind"] == "oproj":
+        # the reference's o_proj (models/adapters.py:1231): fp32 attn_out @ fp16 weights widened to fp32
+        a = rng.standard_normal((n, hq * d)).astype(np.float32)
+        wo = (rng.standard_normal((hidden, hq * d)) * (hq * d) ** -0.5).astype(np.float16)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            o_project(a, wo)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 1000:
+                break
+        if prefill:
+            val, unit = reps * qkv_flops(w, n) / el / 1e12, "TFLOP/s"
+        else:
+            val, unit = reps * qkv_bytes(w, n) / el / 1e9, "GB/s"
+        return {"value": round(val, 5), "unit": unit, "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)
+                or (os.cpu_count() or 1), "kind": "port",
+                "sample": f"1 layer x {n} tokens (fp32 attention output, fp16 weights), {reps} reps in {el:.1f}s"}
     x = rng.standard_normal((n, hidden)).astype(np.float32)
     wq = (rng.standard_normal((hq * d, hidden)) * hidden ** -0.5).astype(np.float16)
     wk = (rng.standard_normal((H * d, hidden)) * hidden ** -0.5).astype(np.float16)
@@ -1536,7 +1588,7 @@ def bench_reference(args, w, world, rank):
         return None
     steps = []
     kind = w.get("kind")
-    qkv = kind == "qkv"
+    qkv = kind in ("qkv", "oproj")
     budget = args.cpu_seconds / max(1, args.steps)
     for i in range(args.warmup + args.steps):
         if qkv:
@@ -1563,12 +1615,14 @@ def bench_reference(args, w, world, rank):
                                  "sample": r["sample"]},
                 "e2e": {"value": round(val, 6), "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if qkv:
-        return {"metric": ("fused q/k/v projection + QK-norm + RoPE + KV append " +
+        return {"metric": (("attention output projection (o_proj) " if kind == "oproj" else
+                            "fused q/k/v projection + QK-norm + RoPE + KV append ") +
                            ("TFLOP/s" if w["tokens_per_seq"] > 1 else "GB/s (weights + activations)")),
                 "impl": "reference", "value": round(val, 5), "unit": r["unit"], "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-                "config": {"workload": f"{args.workload}: reference NumPy projections + QK-norm + RoPE on a "
+                "config": {"workload": f"{args.workload}: reference NumPy "
+                                       f"{'o_proj' if kind == 'oproj' else 'projections + QK-norm + RoPE'} on a "
                                        f"bounded host sample", "parallelism": "host cores"},
                 "cpu_baseline": {"value": round(val, 5), "unit": r["unit"], "cores": cores, "kind": "port",
                                  "sample": r["sample"]},
@@ -1613,7 +1667,7 @@ def main():
             res = bench_reference(args, w, world, rank)
         elif w.get("kind") == "mix":
             res = bench_mix(args, w, world, rank, local)
-        elif w.get("kind") == "qkv":
+        elif w.get("kind") in ("qkv", "oproj"):
             res = bench_qkv(args, w, world, rank, local)
         elif w.get("kind") == "prefill":
             res = bench_prefill(args, w, world, rank, local)

@@ -272,6 +272,31 @@ SCKV_API size_t sckv_qkv_workspace_bytes(const sckv_pool* pool, int n_tokens,
 SCKV_API int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo,
                      int dtype, void* stream);
 
+/* Output projection after attention: out = x @ w_o^T, the last step of
+ * ModularAttentionEngine.forward_numpy (models/adapters.py:1231, attn_out
+ * fp32 times the fp16 o_proj weights, fp32 result). The plain mode of the
+ * sckv_qkv_append kernel (tcgen05, fp32 accumulation).
+ * x : [n_tokens][in_features] in x_dtype (F16 or BF16, the weights' type);
+ *     x_lo (optional) as in sckv_qkv_append: an fp32 attention output split
+ *     by sckv_split_hi_lo keeps fp32 accuracy.
+ * w_o [out_features][in_features] row-major; out [n_tokens][out_features]
+ * in out_dtype (F32, F16 or BF16).
+ * out_features % 128 == 0 and in_features % 8 == 0, else
+ * SCKV_ERR_UNSUPPORTED. workspace: >= sckv_o_proj_workspace_bytes(...)
+ * (fp32 partial sums when few token tiles make the kernel split
+ * in_features across CTAs; 0 bytes otherwise, and workspace may be NULL).
+ * x, x_lo, w_o, out and workspace 16-byte aligned. Failures inside the
+ * kernel are recorded in the pool's status word (kernel id 14). */
+SCKV_API int sckv_o_proj(sckv_pool* pool, const void* x, const void* x_lo,
+                     int x_dtype, int n_tokens, int in_features,
+                     const void* w_o, int out_features, void* out,
+                     int out_dtype, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Workspace sckv_o_proj needs for this call shape (0 on bad arguments). */
+SCKV_API size_t sckv_o_proj_workspace_bytes(const sckv_pool* pool,
+                     int n_tokens, int in_features, int out_features);
+
 /* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
 #define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)
 

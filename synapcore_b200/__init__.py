@@ -7,6 +7,7 @@ sm_100a CUDA kernels in libsckv.so through its C ABI (include/sckv.h).
 """
 from ._native import SCKVBoundsError, SCKVError, SCKVPoolExhausted
 from .arena import PagedKVArena
+from .attention_layer import PagedAttentionLayer
 from .kv_index import KVPrefixIndex
 from .paged_cache import DecodeStepGraph, PagedKVCache
 from .pool import KVPool, rope_inv_freq
@@ -22,6 +23,7 @@ __all__ = [
     "PrefixPageIndex",
     "KVPrefixIndex",
     "NativeKVPrefixCache",
+    "PagedAttentionLayer",
     "PagedKVArena",
     "PagedKVStats",
     "SCKVBoundsError",

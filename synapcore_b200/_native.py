@@ -83,6 +83,10 @@ _SIGNATURES = [
       c_int, c_void_p, c_size_t, c_void_p]),
     ("sckv_split_hi_lo", c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_qkv_workspace_bytes", c_size_t, [c_void_p, c_int, c_int, c_int]),
+    ("sckv_o_proj", c_int,
+     [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_size_t,
+      c_void_p]),
+    ("sckv_o_proj_workspace_bytes", c_size_t, [c_void_p, c_int, c_int, c_int]),
     ("sckv_prefill_attn", c_int,
      [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float,
       c_void_p, c_int, c_void_p]),

@@ -27,6 +27,12 @@
 //              the stores (q_out row, or the K / V row of the token's page).
 // The epilogue follows the reference's fp32 operation order with IEEE
 // operations; the projection sums in fp32 in the tensor core's order.
+//
+// The same kernel in its plain mode is the output projection after
+// attention, attn_out @ W_o^T with fp16 weights (models/adapters.py:1231):
+// 128-column output tiles take the place of the heads, and the epilogue
+// stores the fp32 sums (or their 16-bit rounding) with no norm, rotation or
+// page append.
 #include <cuda.h>
 #include <math.h>
 
@@ -89,6 +95,7 @@ struct QkvParams {
   int m_tiles;            // token tiles of 128
   int n_tiles;            // n_groups * m_tiles * splits
   int hd_total;           // (hq + 2 hkv) * 128 output columns
+  int plain;              // plain projection (o_proj): no norm, rotation or append
   float eps;
 };
 
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
     for (int i = 0; i < 4; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), __half2float(__ldg(nw + lane + 32 * i)));
   }
   float y[4] = {x[0], x[1], x[2], x[3]};
-  if (kind < 2) {
+  if (kind < 2 && !p.plain) {
     // cos / sin of this token's position, the operations of rope_table_kernel
     const int b = sckv_find_seq(p.cu, p.n_seqs, t);
     const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
@@ -477,7 +484,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
                 x1 = __fmul_rn(__fmul_rn(x1, inv), __half2float(__ldg(nw + d)));
                 x2 = __fmul_rn(__fmul_rn(x2, inv), __half2float(__ldg(nw + d + kRopePairs)));
               }
-              if (tl.kind < 2) {
+              if (tl.kind < 2 && !p.plain) {
                 const float2 cs = __ldg(p.rope_cs + (int64_t)tok * kRopePairs + d);
                 y1[i] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
                 y2[i] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
@@ -563,6 +570,44 @@ size_t qkv_workspace_bytes(int64_t n_tokens, int64_t n_heads, int hidden, int nu
   size_t b = (size_t)n_tokens * kRopePairs * sizeof(float2);
   if (ks > 1) b += (size_t)ks * n_tokens * n_heads * kHead * sizeof(float);
   return b;
+}
+
+size_t oproj_workspace_bytes(int64_t n_tokens, int in_features, int out_features, int num_sms) {
+  const int64_t n_out = out_features / kHead;
+  if (n_out <= 0) return 0;
+  const int per = qkv_steps_per_split(n_tokens, n_out, in_features, num_sms);
+  const int nk = (in_features + kQkvBK - 1) / kQkvBK;
+  const int64_t ks = (nk + per - 1) / per;
+  return ks > 1 ? (size_t)ks * n_tokens * out_features * sizeof(float) : 0;
+}
+
+// The projection launch (and, split over the hidden dim, the finishing
+// pass) for the fused q / k / v kernel and the plain output projection.
+int launch_projection(const QkvParams& prm, const CUtensorMap (&maps)[5], bool bf16, bool has_lo, int k_splits,
+                      int heads, int n_groups, int mt, int sms, cudaStream_t s) {
+  if (k_splits > 1) {
+    const int rc = has_lo ? (bf16 ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
+                                  : launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits))
+                          : (bf16 ? launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
+                                  : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits));
+    if (rc != SCKV_OK) return rc;
+    const int64_t warps = (int64_t)prm.n_tok * (prm.hq + 2 * prm.hkv);
+    qkv_finish_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(prm, k_splits);
+    SCKV_LAUNCH_CHECK();
+    return SCKV_OK;
+  }
+  if (heads == 2) {
+    if (bf16)
+      return has_lo ? launch_qkv<true, true, 2>(prm, maps, n_groups, mt, sms, s)
+                    : launch_qkv<true, false, 2>(prm, maps, n_groups, mt, sms, s);
+    return has_lo ? launch_qkv<false, true, 2>(prm, maps, n_groups, mt, sms, s)
+                  : launch_qkv<false, false, 2>(prm, maps, n_groups, mt, sms, s);
+  }
+  if (bf16)
+    return has_lo ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s)
+                  : launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s);
+  return has_lo ? launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s)
+                : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s);
 }
 
 }  // namespace
@@ -679,29 +724,67 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.partial = k_splits > 1 ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
                                                          (size_t)n_tokens * kRopePairs * sizeof(float2))
                              : nullptr;
-  const int mt = (int)m_tiles;
-  const int sms = pool->num_sms;
-  if (k_splits > 1) {
-    rc = x_lo ? (bf16 ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
-                      : launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s, k_splits))
-              : (bf16 ? launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits)
-                      : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits));
-    if (rc != SCKV_OK) return rc;
-    const int64_t warps = (int64_t)n_tokens * n_heads;
-    qkv_finish_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(prm, k_splits);
-    SCKV_LAUNCH_CHECK();
-    return SCKV_OK;
-  }
-  if (heads == 2) {
-    if (bf16)
-      return x_lo ? launch_qkv<true, true, 2>(prm, maps, n_groups, mt, sms, s)
-                  : launch_qkv<true, false, 2>(prm, maps, n_groups, mt, sms, s);
-    return x_lo ? launch_qkv<false, true, 2>(prm, maps, n_groups, mt, sms, s)
-                : launch_qkv<false, false, 2>(prm, maps, n_groups, mt, sms, s);
-  }
-  if (bf16)
-    return x_lo ? launch_qkv<true, true, 1>(prm, maps, n_groups, mt, sms, s)
-                : launch_qkv<true, false, 1>(prm, maps, n_groups, mt, sms, s);
-  return x_lo ? launch_qkv<false, true, 1>(prm, maps, n_groups, mt, sms, s)
-              : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s);
+  return launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
+                           pool->num_sms, s);
+}
+
+extern "C" size_t sckv_o_proj_workspace_bytes(const sckv_pool* pool, int n_tokens, int in_features,
+                                              int out_features) {
+  if (pool == nullptr || n_tokens < 0 || in_features <= 0 || out_features <= 0) return 0;
+  return oproj_workspace_bytes(n_tokens, in_features, out_features, pool->num_sms);
+}
+
+extern "C" int sckv_o_proj(sckv_pool* pool, const void* x, const void* x_lo, int x_dtype, int n_tokens,
+                           int in_features, const void* w_o, int out_features, void* out, int out_dtype,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (pool == nullptr || n_tokens < 0 || in_features <= 0 || out_features <= 0) return SCKV_ERR_INVALID_ARG;
+  if (x_dtype != SCKV_DTYPE_F16 && x_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
+  if (out_dtype != SCKV_DTYPE_F32 && out_dtype != SCKV_DTYPE_F16 && out_dtype != SCKV_DTYPE_BF16)
+    return SCKV_ERR_INVALID_ARG;
+  // 128-column output tiles are stored whole; 16-byte row pitch for the tensor maps
+  if (out_features % kHead != 0 || in_features % 8 != 0) return SCKV_ERR_UNSUPPORTED;
+  if (n_tokens == 0) return SCKV_OK;
+  if (!x || !w_o || !out) return SCKV_ERR_INVALID_ARG;
+  const size_t need = oproj_workspace_bytes(n_tokens, in_features, out_features, pool->num_sms);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return SCKV_ERR_INVALID_ARG;
+  if (!aligned16(x) || (x_lo && !aligned16(x_lo)) || !aligned16(w_o) || !aligned16(out) ||
+      (need > 0 && !aligned16(workspace)))
+    return SCKV_ERR_ALIGNMENT;
+  const int64_t m_tiles = ((int64_t)n_tokens + kQkvBM - 1) / kQkvBM;
+  if (m_tiles > 65535) return SCKV_ERR_UNSUPPORTED;
+  const int n_out = out_features / kHead;  // 128-column output tiles ("heads" of the fused kernel)
+
+  const int64_t groups2 = (n_out + 1) / 2;
+  const int per_split = qkv_steps_per_split(n_tokens, n_out, in_features, pool->num_sms);
+  const int nk = (in_features + kQkvBK - 1) / kQkvBK;
+  const int k_splits = (nk + per_split - 1) / per_split;
+  const int heads = (k_splits == 1 && groups2 * m_tiles >= pool->num_sms) ? 2 : 1;
+  const int n_groups = heads == 2 ? (int)groups2 : n_out;
+
+  const bool bf16 = x_dtype == SCKV_DTYPE_BF16;
+  CUtensorMap maps[5];
+  int rc = encode_rows(&maps[0], x, n_tokens, in_features, bf16, kQkvBM);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[1], x_lo ? x_lo : x, n_tokens, in_features, bf16, kQkvBM);
+  if (rc == SCKV_OK) rc = encode_rows(&maps[2], w_o, out_features, in_features, bf16, heads * kHead);
+  if (rc != SCKV_OK) return rc;
+  maps[3] = maps[2];  // no k / v tiles in a plain projection
+  maps[4] = maps[2];
+  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+
+  QkvParams prm{};
+  prm.q_out = out;
+  prm.status = pool->status;
+  prm.n_tok = n_tokens;
+  prm.hidden = in_features;
+  prm.hq = n_out;
+  prm.hkv = 0;
+  prm.q_out_dtype = out_dtype;
+  prm.pool_dtype = pool->kv_dtype;
+  prm.plain = 1;
+  prm.rope_scaling = 1.f;
+  prm.k_steps_per_split = per_split;
+  prm.hd_total = out_features;
+  prm.partial = k_splits > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
+  return launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
+                           pool->num_sms, as_stream(stream));
 }

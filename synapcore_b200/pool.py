@@ -323,6 +323,54 @@ class KVPool:
                     t.record_stream(stream)
         return q_out
 
+    def o_proj(self, x: torch.Tensor, w_o: torch.Tensor, out: Optional[torch.Tensor] = None,
+               out_dtype: torch.dtype = torch.float32, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Output projection after attention, x [n_tokens, in_features] @
+        w_o^T with w_o [out_features, in_features] (float16 or bfloat16),
+        on the tensor cores; returns [n_tokens, out_features] in out_dtype.
+        An fp32 x (the attention output) is split into hi + lo parts of the
+        weights' type, as in qkv_append; a 16-bit x must have the weights'
+        type. Needs out_features % 128 == 0 and in_features % 8 == 0."""
+        if x.dim() == 3:
+            x = x.reshape(x.shape[0], -1)
+        x = x.contiguous()
+        w_o = w_o.contiguous()
+        nt, fin = x.shape
+        wdt = w_o.dtype
+        if wdt not in (torch.float16, torch.bfloat16):
+            raise TypeError("w_o must be float16 or bfloat16")
+        if w_o.dim() != 2 or w_o.shape[1] != fin:
+            raise ValueError("w_o must be [out_features, in_features]")
+        fout = w_o.shape[0]
+        _need(x, "x", self.device)
+        _need(w_o, "w_o", self.device)
+        if out is None:
+            out = torch.empty((nt, fout), dtype=out_dtype, device=self.device)
+        else:
+            _need(out, "out", self.device)
+            if tuple(out.shape) != (nt, fout):
+                raise ValueError("out must be [n_tokens, out_features]")
+        x_lo = None
+        if x.dtype == torch.float32:
+            hi = torch.empty((nt, fin), dtype=wdt, device=self.device)
+            x_lo = torch.empty_like(hi)
+            N.check(self.lib.sckv_split_hi_lo(x.data_ptr(), x.numel(), hi.data_ptr(), x_lo.data_ptr(),
+                                              torch_dtype_code(wdt), _stream_ptr(stream)), "sckv_split_hi_lo")
+            x = hi
+        elif x.dtype != wdt:
+            raise TypeError("a 16-bit x must have the weights' dtype")
+        ws_bytes = int(self.lib.sckv_o_proj_workspace_bytes(self.handle, nt, fin, fout))
+        ws = torch.empty(max(16, ws_bytes) // 4 + 4, dtype=torch.float32, device=self.device)
+        N.check(self.lib.sckv_o_proj(self.handle, x.data_ptr(), _ptr(x_lo), torch_dtype_code(x.dtype), nt, fin,
+                                     w_o.data_ptr(), fout, out.data_ptr(), torch_dtype_code(out.dtype), ws.data_ptr(),
+                                     ws.numel() * 4, _stream_ptr(stream)),
+                "sckv_o_proj")
+        if stream is not None:
+            for t in (ws, x_lo, x if x_lo is not None else None):
+                if t is not None:
+                    t.record_stream(stream)
+        return out
+
     def write_pages(self, page_ids: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor,
                     stream: Optional[torch.cuda.Stream] = None) -> None:
         """k_src, v_src: [n, L, H, 16, D] float16 / bfloat16 / float32."""

@@ -308,6 +308,44 @@ def qk_rope_cases(ad, arrays):
     return out
 
 
+def attention_layer_cases(ad, arrays):
+    """A whole attention layer through ModularAttentionEngine.forward_numpy
+    (models/adapters.py:1148-1231): q/k/v projections with random fp16
+    weights, QK-norm (per head, whole width, or none) with the adapter's
+    eps, RoPE from the cached prefix's length, the fp16 cache concat, causal
+    SDPA (none for one token) and o_proj. Records the layer output and the
+    cache entries the call appended; the inputs come from seeds
+    (attn_layer_inputs.py, which the tests use too) and are recorded as
+    digests."""
+    sys.path.insert(0, str(OUT))
+    from attn_layer_inputs import ATTN_LAYER_CASES, attn_layer_inputs  # noqa: E402
+
+    adapters = {"qwen2_moe": ad.QwenMoEAdapter, "olmoe": ad.OLMoEAdapter, "mixtral": ad.MixtralAdapter}
+    out = []
+    for name, kind, hq, hkv, prefix, T, norm, theta, seed in ATTN_LAYER_CASES:
+        d = 128
+        hidden = hq * d
+        cfg = {"model_type": kind, "num_hidden_layers": 1, "num_experts": 8, "num_experts_per_tok": 2,
+               "hidden_size": hidden, "intermediate_size": hidden * 2, "moe_intermediate_size": hidden * 2,
+               "num_attention_heads": hq, "num_key_value_heads": hkv, "vocab_size": 32000,
+               "rms_norm_eps": 1e-6, "rope_theta": theta, "use_qk_norm": norm is not None}
+        eng = ad.ModularAttentionEngine(adapters[kind](cfg).spec)
+        inp = attn_layer_inputs(hq, hkv, prefix, T, norm, seed)
+        kk = [inp["pk"][None].copy() if prefix else None]
+        vv = [inp["pv"][None].copy() if prefix else None]
+        y = eng.forward_numpy(inp["x"][None], inp["wq"], inp["wk"], inp["wv"], inp["wo"], q_norm_w_fp16=inp["qn"],
+                              k_norm_w_fp16=inp["kn"], kv_cache_k=kk, kv_cache_v=vv, layer_idx=0,
+                              pos_offset=prefix)
+        arrays[f"attn_layer_{name}_out"] = y[0].astype(np.float32)
+        arrays[f"attn_layer_{name}_k_new"] = kk[0][0][:, prefix:]
+        arrays[f"attn_layer_{name}_v_new"] = vv[0][0][:, prefix:]
+        out.append({"name": name, "adapter": kind, "hq": hq, "hkv": hkv, "prefix": prefix, "T": T, "norm": norm,
+                    "theta": theta, "seed": seed, "eps": float(eng.rms_eps),
+                    "has_qk_norm": bool(eng.has_qk_norm), "scale": float(eng.scale),
+                    "inputs_sha256": {k: sha(v) for k, v in inp.items() if v is not None}})
+    return out
+
+
 def scheduler_runs(ne, ad, arrays):
     """The reference ContinuousBatchScheduler (engine/scheduler.py) over a
     stub of the reference engine carrying the seeded weights of
@@ -402,6 +440,7 @@ def main():
         "sdpa": sdpa_cases(ad, arrays),
         "scheduler": scheduler_runs(ne, ad, arrays),
         "qk_rope": qk_rope_cases(ad, arrays),
+        "attention_layer": attention_layer_cases(ad, arrays),
         "chain_hash": [ne.chain_merkle_prefix_hash(GOLDEN_SEED_ROOT, list(range(16))),
                        ne.chain_merkle_prefix_hash("00" * 32, [0] * 16),
                        ne.chain_merkle_prefix_hash("ff" * 32, [4294967295] * 16)],
