@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <atomic>
+#include <utility>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -266,6 +267,32 @@ inline int sckv_record_error(const char* file, int line, const char* what, const
 inline std::atomic<unsigned long long>& sckv_launch_counter() {
   static std::atomic<unsigned long long> n{0};
   return n;
+}
+
+// Programmatic dependent launch. A kernel launched with sckv_launch_pdl may
+// start while the kernel before it in the stream is still running (once
+// that one has called pdl_trigger or finished); it must call pdl_wait before
+// it reads anything an earlier kernel wrote, which waits for the earlier
+// kernel to complete and its memory to be visible. Kernels call pdl_trigger
+// after their own pdl_wait, so a dependent never starts before the kernel
+// two places back has completed.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t sckv_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 #define SCKV_LAUNCH_CHECK()                                                              \

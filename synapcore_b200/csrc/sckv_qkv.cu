@@ -72,10 +72,10 @@ struct QkvParams {
   int32_t* status;
   const __half* q_norm_w;  // [128] or null
   const __half* k_norm_w;  // [128] or null
-  const float2* rope_cs;   // [n_tok][64] (cos, sin); null when split (the finish kernel computes them)
+  const float2* rope_cs;   // [n_tok][64] (cos, sin); split: written by the projection kernel itself
   const float* inv_freq;   // [64]
   float rope_scaling;
-  float* partial;          // split-K: [k_splits][n_tok][hd_total] fp32 sums, else null
+  float* partial;          // split-K: fp32 sums per (tile, split), layout of split_part_index, else null
   const int32_t* cu;
   const int32_t* start_pos;
   const int32_t* bt;
@@ -95,6 +95,8 @@ struct QkvParams {
   int m_tiles;            // token tiles of 128
   int n_tiles;            // n_groups * m_tiles * splits
   int hd_total;           // (hq + 2 hkv) * 128 output columns
+  int k_splits;           // splits of the hidden dim (1: none)
+  int2* tok_meta;         // split: per token (position, page of its K/V slot or -1), written by the projection
   int plain;              // plain projection (o_proj): no norm, rotation or append
   float eps;
 };
@@ -102,10 +104,7 @@ struct QkvParams {
 // Destination page row of token t (k / v): the slab (layer, page) of its
 // block, or -1 (out-of-range position or page, reported once per token by
 // the caller's choice of `report`).
-__device__ __forceinline__ int64_t token_slab(const QkvParams& p, int t, int* pos_out, bool report) {
-  const int b = sckv_find_seq(p.cu, p.n_seqs, t);
-  const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
-  *pos_out = pos;
+__device__ __forceinline__ int64_t slab_at(const QkvParams& p, int b, int pos, bool report) {
   const int blk = pos / SCKV_PAGE_TOKENS;
   if (pos < 0 || blk >= p.max_blocks) {
     if (report) sckv_report(p.status, SCKV_ERR_BOUNDS, pos < 0 ? pos : blk, KID_QKV);
@@ -119,11 +118,20 @@ __device__ __forceinline__ int64_t token_slab(const QkvParams& p, int t, int* po
   return (int64_t)p.layer * p.max_pages + page;
 }
 
+__device__ __forceinline__ int64_t token_slab(const QkvParams& p, int t, int* pos_out, bool report) {
+  const int b = sckv_find_seq(p.cu, p.n_seqs, t);
+  const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
+  *pos_out = pos;
+  return slab_at(p, b, pos, report);
+}
+
 // cos / sin of every (token, frequency) pair: position start_pos[b] + i
 // divided by rope_scaling, times inv_freq[j], as sckv_append_rope computes
 // them (apply_rope_f32, models/adapters.py:1134-1146).
 __global__ void rope_table_kernel(const float* inv_freq, float rope_scaling, int n_seqs, int n_tok,
                                   const int32_t* cu, const int32_t* start_pos, float2* cs) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)n_tok * kRopePairs) return;
   const int t = (int)(idx / kRopePairs), j = (int)(idx % kRopePairs);
@@ -139,6 +147,8 @@ __global__ void rope_table_kernel(const float* inv_freq, float rope_scaling, int
 // fp32 x -> hi = round(x), lo = round(x - hi) in the MMA's 16-bit type, so
 // hi . W + lo . W carries x to ~2^-22 relative (W is exact in that type).
 __global__ void split_hi_lo_kernel(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, int bf16) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = x[i];
     if (bf16) {
@@ -176,11 +186,50 @@ __device__ __forceinline__ void store32(void* dst, int64_t idx, int dtype, const
   }
 }
 
+// Split-K partial sums: per (head tile g = head + heads x token tile, split
+// z) a 128-row x 128-column fp32 tile stored as [16 column octets][128
+// rows][8]: the epilogue thread of row r writes its octets as 32-byte runs
+// that sit side by side across the warp, and the finishing warp of a row
+// reads each octet as two lanes' float4s, one full sector. Index of the
+// first float of (g, z, octet, row).
+__device__ __forceinline__ int64_t split_part_index(int64_t g, int ks, int z, int octet, int row) {
+  return (((g * ks + z) * 16 + octet) * 128 + row) * 8;
+}
+
+// Split over the hidden dim: while its MMAs run, the projection kernel's
+// epilogue warps look up every token's sequence, position and K/V page and
+// its cos / sin row (the operations of rope_table_kernel), so the finishing
+// kernel's loads are all independent. e = epilogue thread (0..127). A
+// token whose slot is out of range is reported here, once.
+__device__ __forceinline__ void token_meta(const QkvParams& p, int e) {
+  float2* cs = const_cast<float2*>(p.rope_cs);
+  for (int t = blockIdx.x * 128 + e; t < p.n_tok; t += gridDim.x * 128) {
+    const int b = sckv_find_seq(p.cu, p.n_seqs, t);
+    const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
+    const int64_t slab = slab_at(p, b, pos, true);
+    p.tok_meta[t] = make_int2(pos, slab < 0 ? -1 : (int)(slab - (int64_t)p.layer * p.max_pages));
+    const float fpos = __fdiv_rn((float)pos, p.rope_scaling);
+    float4* d = reinterpret_cast<float4*>(cs + (int64_t)t * kRopePairs);
+#pragma unroll 4
+    for (int j = 0; j < kRopePairs; j += 2) {
+      float s0, c0, s1, c1;
+      sincosf(__fmul_rn(fpos, __ldg(p.inv_freq + j)), &s0, &c0);
+      sincosf(__fmul_rn(fpos, __ldg(p.inv_freq + j + 1)), &s1, &c1);
+      d[j >> 1] = make_float4(c0, s0, c1, s1);
+    }
+  }
+}
+
 // Split-K finish: one warp per (token, output head) adds the splits' fp32
-// sums, then applies the per-head RMSNorm, the rotation and the stores of
-// the fused epilogue. Lane i holds dims i, i + 32, i + 64, i + 96, so both
-// rotation pairs (i, i + 64) and (i + 32, i + 96) stay in the lane.
-__global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int k_splits) {
+// sums in split order, then applies the per-head RMSNorm, the rotation and
+// the stores of the fused epilogue (plain mode: the stores only). Lane l
+// holds dims 4l .. 4l + 3, so the rotation partner (d + 64) of lane l < 16
+// is lane l + 16. Every load (partial sums, the token's position and page,
+// its cos / sin) is independent of the others; 40 registers keep the grid
+// of a 128-token decode batch in one wave.
+__global__ void __launch_bounds__(256, 6) qkv_finish_kernel(const QkvParams p, int k_splits) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int n_heads = p.hq + 2 * p.hkv;
@@ -188,11 +237,40 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
   const int t = (int)(wid / n_heads), hidx = (int)(wid % n_heads);
   const int kind = hidx < p.hq ? 0 : (hidx < p.hq + p.hkv ? 1 : 2);
   const int head = kind == 0 ? hidx : (kind == 1 ? hidx - p.hq : hidx - p.hq - p.hkv);
-  float x[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int z = 0; z < k_splits; ++z) {
-    const float* src = p.partial + ((int64_t)z * p.n_tok + t) * p.hd_total + (int64_t)hidx * kHead;
+  const int64_t g = (int64_t)(t / kQkvBM) * n_heads + hidx;
+  const float4* src = reinterpret_cast<const float4*>(p.partial + split_part_index(g, k_splits, 0, lane >> 1,
+                                                                                    t % kQkvBM)) + (lane & 1);
+  constexpr int64_t kSplitStride = 16 * 128 * 8 / 4;  // float4s between one split's tile and the next
+  float4 v[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = __fadd_rn(x[i], __ldg(src + lane + 32 * i));
+  for (int i = 0; i < 4; ++i)
+    if (i < k_splits) v[i] = __ldcg(src + i * kSplitStride);
+  int2 meta = make_int2(0, 0);  // (position, page)
+  float4 cs0 = make_float4(1.f, 0.f, 1.f, 0.f), cs1 = cs0;
+  if (!p.plain) {
+    meta = __ldg(p.tok_meta + t);
+    if (kind < 2) {
+      // (cos, sin) of dims 4l .. 4l + 3 (mod 64)
+      const float4* c4 = reinterpret_cast<const float4*>(p.rope_cs + (int64_t)t * kRopePairs + ((4 * lane) & 63));
+      cs0 = __ldg(c4);
+      cs1 = __ldg(c4 + 1);
+    }
+  }
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int z0 = 0; z0 < k_splits; z0 += 4) {
+    if (z0 > 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (z0 + i < k_splits) v[i] = __ldcg(src + (z0 + i) * kSplitStride);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (z0 + i < k_splits) {
+        x[0] = __fadd_rn(x[0], v[i].x);
+        x[1] = __fadd_rn(x[1], v[i].y);
+        x[2] = __fadd_rn(x[2], v[i].z);
+        x[3] = __fadd_rn(x[3], v[i].w);
+      }
   }
   const __half* nw = kind == 0 ? p.q_norm_w : (kind == 1 ? p.k_norm_w : nullptr);
   if (nw != nullptr) {
@@ -203,20 +281,17 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
     for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
     const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHead), p.eps)));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), __half2float(__ldg(nw + lane + 32 * i)));
+    for (int i = 0; i < 4; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), __half2float(__ldg(nw + 4 * lane + i)));
   }
   float y[4] = {x[0], x[1], x[2], x[3]};
   if (kind < 2 && !p.plain) {
-    // cos / sin of this token's position, the operations of rope_table_kernel
-    const int b = sckv_find_seq(p.cu, p.n_seqs, t);
-    const int pos = __ldg(p.start_pos + b) + (t - __ldg(p.cu + b));
-    const float fpos = __fdiv_rn((float)pos, p.rope_scaling);
+    const bool first = lane < 16;  // dims 4l.. in the first half; the partner lane holds d + 64
+    const float cn[4] = {cs0.x, cs0.z, cs1.x, cs1.z}, sn[4] = {cs0.y, cs0.w, cs1.y, cs1.w};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      float sn, cn;
-      sincosf(__fmul_rn(fpos, __ldg(p.inv_freq + lane + 32 * i)), &sn, &cn);
-      y[i] = __fsub_rn(__fmul_rn(x[i], cn), __fmul_rn(x[i + 2], sn));
-      y[i + 2] = __fadd_rn(__fmul_rn(x[i + 2], cn), __fmul_rn(x[i], sn));
+    for (int i = 0; i < 4; ++i) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[i], 16);
+      y[i] = first ? __fsub_rn(__fmul_rn(x[i], cn[i]), __fmul_rn(other, sn[i]))
+                   : __fadd_rn(__fmul_rn(x[i], cn[i]), __fmul_rn(other, sn[i]));
     }
   }
   int64_t dst;
@@ -227,15 +302,22 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvParams p, int 
     out = p.q_out;
     out_dtype = p.q_out_dtype;
   } else {
-    int pos = 0;
-    const int64_t slab = token_slab(p, t, &pos, lane == 0 && head == 0);
-    if (slab < 0) return;
-    dst = (((slab * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) * kHead;
+    if (meta.y < 0) return;  // reported by token_meta
+    const int64_t slab = (int64_t)p.layer * p.max_pages + meta.y;
+    dst = (((slab * 2 + (kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + meta.x % SCKV_PAGE_TOKENS) * kHead;
     out = p.pool_data;
     out_dtype = p.pool_dtype;
   }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) sckv_store_from_float(out, dst + lane + 32 * i, out_dtype, y[i]);
+  dst += 4 * lane;
+  if (out_dtype == SCKV_DTYPE_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + dst) = make_float4(y[0], y[1], y[2], y[3]);
+  } else if (out_dtype == SCKV_DTYPE_BF16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + dst) =
+        make_uint2(pack2<true>(y[0], y[1]), pack2<true>(y[2], y[3]));
+  } else {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + dst) =
+        make_uint2(pack2<false>(y[0], y[1]), pack2<false>(y[2], y[3]));
+  }
 }
 
 // Geometry of work tile t: tiles run head group fastest, then token tile,
@@ -302,6 +384,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the set-up above may overlap the previous kernel; the inputs may not
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -396,6 +481,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       const QkvTile tl = qkv_tile<kHeads>(p, t);
       const int buf = lt & 1;
       const int tok = tl.m0 + quad * 32 + lane;
+      // split: per-token lookups for the finishing kernel, while the MMAs run
+      if (p.partial != nullptr && lt == 0 && !p.plain) token_meta(p, threadIdx.x - 64);
       const bool ready = warp_wait(&acc_full[buf], (lt >> 1) & 1);
       tc_fence_after();
       // warp-uniform: the tensor-memory loads below are warp-wide
@@ -403,27 +490,25 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       if (!ready || aborted) break;
       const uint32_t acc = tmem + (uint32_t)(buf * SM::kBN) + ((uint32_t)(quad * 32) << 16);
       if (p.partial != nullptr) {
-        // split-K: raw fp32 sums of this split; qkv_finish_kernel adds the
-        // splits and applies the norm, rotation and stores
+        // split-K: raw fp32 sums of this split (rows past the last token
+        // too); qkv_finish_kernel adds the splits and applies the norm,
+        // rotation and stores
+        const int n_heads = p.hq + 2 * p.hkv;
+        const int hidx = (tl.kind == 0 ? 0 : (tl.kind == 1 ? p.hq : p.hq + p.hkv)) + tl.head0;
+        const int64_t g = (int64_t)(tl.m0 / kQkvBM) * n_heads + hidx;
+        const int row = quad * 32 + lane;
 #pragma unroll 1
-        for (int hh = 0; hh < kHeads; ++hh) {
-          const int head = tl.head0 + hh;
-          if (head >= tl.kind_heads) break;  // warp-uniform
-          const uint32_t trow = acc + (uint32_t)(hh * kHead);
-          const int col0 = (tl.kind == 0 ? 0 : (tl.kind == 1 ? p.hq : p.hq + p.hkv) * kHead) + head * kHead;
-          float* dst = p.partial + ((int64_t)tl.z * p.n_tok + tok) * p.hd_total + col0;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(trow + c * 32, r);
-            tc_wait_ld();
-            if (tok < p.n_tok) {
-              float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + c * 32, r);
+          tc_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                    __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-            }
+          for (int q = 0; q < 4; ++q) {
+            float4* d4 = reinterpret_cast<float4*>(p.partial + split_part_index(g, p.k_splits, tl.z, c * 4 + q, row));
+            d4[0] = make_float4(__uint_as_float(r[8 * q]), __uint_as_float(r[8 * q + 1]),
+                                __uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+            d4[1] = make_float4(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]),
+                                __uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
           }
         }
       } else {
@@ -541,7 +626,8 @@ int launch_qkv(const QkvParams& prm_in, const CUtensorMap (&maps)[5], int n_grou
   SCKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   // persistent: one CTA per SM (the shared memory allows no second)
   const int grid = (int)(n_tiles < num_sms ? n_tiles : num_sms);
-  kern<<<grid, kQkvThreads, smem, stream>>>(prm, maps[0], maps[1], maps[2], maps[3], maps[4]);
+  SCKV_CUDA_CHECK(sckv_launch_pdl(kern, dim3(grid), dim3(kQkvThreads), smem, stream, prm, maps[0], maps[1],
+                                  maps[2], maps[3], maps[4]));
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
@@ -563,13 +649,19 @@ int qkv_steps_per_split(int64_t n_tokens, int64_t n_heads, int hidden, int num_s
   return (int)((nk + ks - 1) / ks);
 }
 
+// Split-K partial sums: a 128 x 128 fp32 tile per (output tile, token tile, split).
+size_t split_part_bytes(int64_t n_tokens, int64_t n_tiles_out, int64_t ks) {
+  if (ks <= 1) return 0;
+  return (size_t)ks * n_tiles_out * ((n_tokens + kQkvBM - 1) / kQkvBM) * kQkvBM * kHead * sizeof(float);
+}
+
+// The cos / sin table, then (split) the partial sums and the per-token lookups.
 size_t qkv_workspace_bytes(int64_t n_tokens, int64_t n_heads, int hidden, int num_sms) {
   const int per = qkv_steps_per_split(n_tokens, n_heads, hidden, num_sms);
   const int nk = (hidden + kQkvBK - 1) / kQkvBK;
   const int64_t ks = (nk + per - 1) / per;
-  size_t b = (size_t)n_tokens * kRopePairs * sizeof(float2);
-  if (ks > 1) b += (size_t)ks * n_tokens * n_heads * kHead * sizeof(float);
-  return b;
+  return (size_t)n_tokens * kRopePairs * sizeof(float2) + split_part_bytes(n_tokens, n_heads, ks) +
+         (ks > 1 ? (size_t)n_tokens * sizeof(int2) : 0);
 }
 
 size_t oproj_workspace_bytes(int64_t n_tokens, int in_features, int out_features, int num_sms) {
@@ -577,8 +669,7 @@ size_t oproj_workspace_bytes(int64_t n_tokens, int in_features, int out_features
   if (n_out <= 0) return 0;
   const int per = qkv_steps_per_split(n_tokens, n_out, in_features, num_sms);
   const int nk = (in_features + kQkvBK - 1) / kQkvBK;
-  const int64_t ks = (nk + per - 1) / per;
-  return ks > 1 ? (size_t)ks * n_tokens * out_features * sizeof(float) : 0;
+  return split_part_bytes(n_tokens, n_out, (nk + per - 1) / per);
 }
 
 // The projection launch (and, split over the hidden dim, the finishing
@@ -592,7 +683,8 @@ int launch_projection(const QkvParams& prm, const CUtensorMap (&maps)[5], bool b
                                   : launch_qkv<false, false, 1>(prm, maps, n_groups, mt, sms, s, k_splits));
     if (rc != SCKV_OK) return rc;
     const int64_t warps = (int64_t)prm.n_tok * (prm.hq + 2 * prm.hkv);
-    qkv_finish_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(prm, k_splits);
+    SCKV_CUDA_CHECK(sckv_launch_pdl(qkv_finish_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, prm,
+                                    k_splits));
     SCKV_LAUNCH_CHECK();
     return SCKV_OK;
   }
@@ -622,8 +714,9 @@ extern "C" int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo, i
   if (dtype != SCKV_DTYPE_F16 && dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
   const int64_t blocks = (n + 255) / 256;
-  split_hi_lo_kernel<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, as_stream(stream)>>>(
-      x, n, reinterpret_cast<uint16_t*>(hi), reinterpret_cast<uint16_t*>(lo), dtype == SCKV_DTYPE_BF16);
+  SCKV_CUDA_CHECK(sckv_launch_pdl(split_hi_lo_kernel, dim3((unsigned)(blocks < 4096 ? blocks : 4096)), dim3(256), 0,
+                                  as_stream(stream), x, n, reinterpret_cast<uint16_t*>(hi),
+                                  reinterpret_cast<uint16_t*>(lo), (int)(dtype == SCKV_DTYPE_BF16)));
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }
@@ -687,11 +780,11 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
   float2* cs = reinterpret_cast<float2*>(workspace);
   if (k_splits == 1) {
-    // the fused epilogue reads a per-token cos / sin table; the split-K
-    // finish kernel computes its own
+    // the fused epilogue reads a per-token cos / sin table (split over the
+    // hidden dim, the projection kernel fills it while its MMAs run)
     const int64_t n_cs = (int64_t)n_tokens * kRopePairs;
-    rope_table_kernel<<<(unsigned)((n_cs + 255) / 256), 256, 0, s>>>(inv_freq, rope_scaling, n_seqs, n_tokens,
-                                                                       cu_tokens, start_pos, cs);
+    SCKV_CUDA_CHECK(sckv_launch_pdl(rope_table_kernel, dim3((unsigned)((n_cs + 255) / 256)), dim3(256), 0, s,
+                                    inv_freq, rope_scaling, n_seqs, n_tokens, cu_tokens, start_pos, cs));
     SCKV_LAUNCH_CHECK();
   }
 
@@ -701,7 +794,7 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.status = pool->status;
   prm.q_norm_w = q_norm_len ? reinterpret_cast<const __half*>(q_norm_w) : nullptr;
   prm.k_norm_w = k_norm_len ? reinterpret_cast<const __half*>(k_norm_w) : nullptr;
-  prm.rope_cs = k_splits == 1 ? cs : nullptr;
+  prm.rope_cs = cs;
   prm.inv_freq = inv_freq;
   prm.rope_scaling = rope_scaling;
   prm.cu = cu_tokens;
@@ -721,9 +814,12 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.eps = eps;
   prm.k_steps_per_split = per_split;
   prm.hd_total = (int)(n_heads * kHead);
-  prm.partial = k_splits > 1 ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
-                                                         (size_t)n_tokens * kRopePairs * sizeof(float2))
-                             : nullptr;
+  prm.k_splits = k_splits;
+  if (k_splits > 1) {
+    char* w = reinterpret_cast<char*>(workspace) + (size_t)n_tokens * kRopePairs * sizeof(float2);
+    prm.partial = reinterpret_cast<float*>(w);
+    prm.tok_meta = reinterpret_cast<int2*>(w + split_part_bytes(n_tokens, n_heads, k_splits));
+  }
   return launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
                            pool->num_sms, s);
 }
@@ -784,6 +880,7 @@ extern "C" int sckv_o_proj(sckv_pool* pool, const void* x, const void* x_lo, int
   prm.rope_scaling = 1.f;
   prm.k_steps_per_split = per_split;
   prm.hd_total = out_features;
+  prm.k_splits = k_splits;
   prm.partial = k_splits > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
   return launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
                            pool->num_sms, as_stream(stream));
