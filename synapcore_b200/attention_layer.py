@@ -4,8 +4,8 @@ ModularAttentionEngine.forward_numpy (models/adapters.py:1148-1231).
 The reference runs, per request and layer: q/k/v = x @ W^T with fp16
 weights (:1167-1169), optional QK-norm (:1171-1185), RoPE from the
 request's position (:1191-1192), the fp16 KV concat (:1194-1207), causal
-SDPA in fp32 (:1209-1229) and o_proj (:1231). Here one call covers every
-sequence of a batch in three launches groups:
+SDPA in fp32 (:1209-1229) and o_proj (:1231). Here a decode call covers
+every row of a batch and a prefill call one prompt, in three steps:
 
 - `sckv_qkv_append`: projections, per-head QK-norm, RoPE and the K/V page
   append fused in one tcgen05 kernel (whole-width norms take the unfused
