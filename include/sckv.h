@@ -248,9 +248,12 @@ SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
  * q_norm_len / k_norm_len: 0 or 128 (per-head fp16 weights); whole-width
  * norms return SCKV_ERR_UNSUPPORTED (use the projections + sckv_append_rope).
  * workspace: >= sckv_qkv_workspace_bytes(...) bytes: the per-token cos / sin
- * table, plus fp32 partial sums when few token tiles make the kernel split
- * the hidden dim across CTAs (a second, finishing launch then applies the
- * norm, rotation and stores).
+ * table, plus fp32 partial sums and per-token (position, page) entries when
+ * few token tiles make the kernel split the hidden dim across CTAs (a
+ * second, finishing launch then applies the norm, rotation and stores).
+ * The launches use programmatic dependent launch: each may start its set-up
+ * while the kernel before it in the stream finishes, and reads nothing
+ * before that kernel has completed.
  * hidden % 8 == 0; x, x_lo, weights, q_out and workspace 16-byte aligned. */
 SCKV_API int sckv_qkv_append(sckv_pool* pool, int layer, const void* x,
                      const void* x_lo, int x_dtype, int n_tokens, int hidden,
