@@ -22,7 +22,7 @@ a decode step reserves its token's pages on the device at layer 0.
 """
 from __future__ import annotations
 
-from typing import Hashable, Optional
+from typing import Hashable, Optional, Sequence
 
 import torch
 
@@ -65,6 +65,43 @@ class PagedAttentionLayer:
         if layer == c.num_layers - 1:
             c.lengths[r] += T
             c.ctx_lens[r] = c.lengths[r]
+        return out
+
+    def prefill_batch(self, layer: int, seq_ids: Sequence[Hashable], x: torch.Tensor, cu_tokens: Sequence[int],
+                      w_q: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor, w_o: torch.Tensor,
+                      q_norm_w: Optional[torch.Tensor] = None, k_norm_w: Optional[torch.Tensor] = None,
+                      out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Prompts of several sequences in one set of launches (the
+        scheduler's admitted prompts of a step): sequence i's new tokens are
+        rows cu_tokens[i] .. cu_tokens[i+1]-1 of x [total, hidden] (host
+        offsets), at positions length..length+T_i-1. The sequences must sit on
+        consecutive cache rows (e.g. added one after another). Returns the
+        layer output [total, hidden_out]."""
+        c = self.cache
+        seq_ids = list(seq_ids)
+        n = len(seq_ids)
+        cu = [int(v) for v in cu_tokens]
+        if len(cu) != n + 1 or cu[0] != 0 or any(b < a for a, b in zip(cu, cu[1:])):
+            raise ValueError("cu_tokens must be n+1 non-decreasing offsets from 0")
+        if x.shape[0] < cu[-1]:
+            raise ValueError("x has fewer rows than cu_tokens[-1]")
+        r0 = c._consecutive_rows(seq_ids)
+        T = [cu[i + 1] - cu[i] for i in range(n)]
+        starts = [c.lengths[r0 + i] for i in range(n)]
+        if layer == 0:
+            c._grow_rows(r0, T)
+        meta = to_device(cu + starts, torch.int32, c.device)
+        cu_d, st_d = meta[:n + 1], meta[n + 1:]
+        bt = c.block_table[r0:r0 + n]
+        q = self.pool.qkv_append(layer, x[:cu[-1]], w_q, w_k, w_v, cu_d, st_d, bt, self.inv_freq, self.rope_scaling,
+                                 q_norm_w, k_norm_w, self.rms_eps, q_out_dtype=torch.float32,
+                                 max_blocks=c.max_blocks)
+        attn = c.prefill_attention_batch(layer, seq_ids, q, cu_d, st_d, scale=self.scale, out_dtype=torch.float32)
+        out = self.pool.o_proj(attn, w_o, out_dtype=out_dtype)
+        if layer == c.num_layers - 1:
+            for i in range(n):
+                c.lengths[r0 + i] += T[i]
+            c.ctx_lens[r0:r0 + n].copy_(to_device(c.lengths[r0:r0 + n], torch.int32, c.device))
         return out
 
     def decode(self, layer: int, x: torch.Tensor, n_rows: int, w_q: torch.Tensor, w_k: torch.Tensor,

@@ -141,6 +141,56 @@ def test_layer_batched_prompts_then_decode_steps_match_oracle(cuda_device):
     print("worst relative error", worst)
 
 
+def test_layer_prompt_batch_matches_oracle(cuda_device):
+    """Several prompts (one of them empty) through one prefill_batch call per
+    layer, then a decode step: every output against the oracle's
+    forward_numpy composition over that sequence's own history."""
+    from synapcore_b200 import PagedAttentionLayer, PagedKVCache
+
+    dev = cuda_device
+    hq, hkv, L = 8, 2, 2
+    hidden = hq * D
+    eps, theta = 1e-6, 10000.0
+    rng = np.random.default_rng(17)
+    sd = 1.0 / np.sqrt(hidden)
+    W = [[(rng.standard_normal(sh) * sd).astype(np.float16)
+          for sh in ((hq * D, hidden), (hkv * D, hidden), (hkv * D, hidden), (hidden, hq * D))] for _ in range(L)]
+    NW = [[rng.uniform(0.5, 1.5, D).astype(np.float16) for _ in range(2)] for _ in range(L)]
+    Wd = [[_dev(w, dev) for w in ws] for ws in W]
+    NWd = [[_dev(w, dev) for w in ws] for ws in NW]
+    cache = PagedKVCache(L, hkv, D, max_pages=128, max_seqs=8, max_blocks_per_seq=32, kv_dtype="fp16", device=dev)
+    layer = PagedAttentionLayer(cache, hq, rope_theta=theta, rms_eps=eps)
+    prompts = [70, 0, 200, 17]
+    cu = np.concatenate([[0], np.cumsum(prompts)]).tolist()
+    for b in range(len(prompts)):
+        cache.add_sequence(b)
+    hist_k = [[None] * L for _ in prompts]
+    hist_v = [[None] * L for _ in prompts]
+    for l in range(L):
+        x = rng.standard_normal((cu[-1], hidden)).astype(np.float32)
+        out = layer.prefill_batch(l, range(len(prompts)), _dev(x, dev), cu, *Wd[l], q_norm_w=NWd[l][0],
+                                  k_norm_w=NWd[l][1]).cpu().numpy()
+        for b, T in enumerate(prompts):
+            if T == 0:
+                continue
+            ref, hist_k[b][l], hist_v[b][l] = O.attention_layer(x[cu[b]:cu[b + 1]], *W[l], hq, hkv, hist_k[b][l],
+                                                                hist_v[b][l], NW[l][0], NW[l][1], eps, theta)
+            assert _rel_err(out[cu[b]:cu[b + 1]], ref) <= ATTN_TOL, (l, b)
+    for b, T in enumerate(prompts):
+        assert cache.length(b) == T
+    # the empty prompt's sequence decodes from position 0
+    n = len(prompts)
+    for l in range(L):
+        x = rng.standard_normal((n, hidden)).astype(np.float32)
+        out = layer.decode(l, _dev(x, dev), n, *Wd[l], q_norm_w=NWd[l][0], k_norm_w=NWd[l][1]).cpu().numpy()
+        for b in range(n):
+            ref, hist_k[b][l], hist_v[b][l] = O.attention_layer(x[b:b + 1], *W[l], hq, hkv, hist_k[b][l],
+                                                                hist_v[b][l], NW[l][0], NW[l][1], eps, theta)
+            assert _rel_err(out[b:b + 1], ref) <= ATTN_TOL, (l, b)
+    torch.cuda.synchronize()
+    cache.pool.raise_on_status()
+
+
 @pytest.mark.parametrize("n_tok,fin,fout,x_kind,wdt,out_dtype", [
     (1, 512, 1024, "f32", torch.float16, torch.float32),        # decode size: split over in_features
     (128, 4096, 4096, "f32", torch.float16, torch.float32),     # Qwen3-8B decode batch, 4-way split
