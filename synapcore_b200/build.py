@@ -76,7 +76,9 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         if ptxas_verbose and src.suffix == ".cu":
             cmd += ["-Xptxas", "-v"]
         if src.suffix == ".cpp":
-            cmd = [nvcc, "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+            # host-only C++: no device code, so no target architecture to warn about
+            cmd = [nvcc, "-O3", "-std=c++17", "-Wno-deprecated-gpu-targets", "-Xcompiler", "-fPIC",
+                   "-Xcompiler", "-fvisibility=hidden",
                    "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)

@@ -252,7 +252,8 @@ inline int sckv_record_error(const char* file, int line, const char* what, const
   const char* base = file;
   for (const char* c = file; *c; ++c)
     if (*c == '/') base = c + 1;
-  snprintf(sckv_error_buffer(), 256, "%s:%d %s: %s", base, line, what, err);
+  // bounded fields: the message fits the 256-byte buffer
+  snprintf(sckv_error_buffer(), 256, "%.64s:%d %.96s: %.64s", base, line, what, err);
   return SCKV_ERR_CUDA;
 }
 
