@@ -225,8 +225,17 @@ def measured_peak_gbs():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(workload: str):
-    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+def profiled_traffic(workload: str, part: str = ""):
+    """DRAM bytes (read + write) per launch of the dominant kernel from the
+    committed ncu summaries: a `traffic_bytes_per_launch[<workload>]:` (or
+    `[<workload>:<part>]`) line in any profiles/*.md, else the plain
+    `traffic_bytes_per_launch:` line of profiles/decode_attn_<workload>.md."""
+    key = f"{workload}:{part}" if part else workload
+    pat = re.compile(r"traffic_bytes_per_launch\[" + re.escape(key) + r"\]:\s*([0-9.eE+]+)")
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        m = pat.search(f.read_text())
+        if m:
+            return float(m.group(1))
     f = REPO / "profiles" / f"decode_attn_{workload}.md"
     if not f.exists():
         return None
@@ -728,7 +737,8 @@ def bench_paging(args, w, world, rank, local):
                 "h2d_bytes_per_step": int(2 * h_k.numel() * 2), "d2h_bytes_per_step": int(2 * h_gk.numel() * 2)},
         "gpu_launches": int(launches_per_step * args.steps),
         "roofline": {"bound": "hbm", "achieved": sub[top]["achieved"], "peak": peak, "unit": "GB/s",
-                     "frac": sub[top]["frac"], "traffic": None, "peak_kind": peak_kind,
+                     "frac": sub[top]["frac"], "traffic": profiled_traffic(args.workload, top),
+                     "peak_kind": peak_kind,
                      "kernel": f"{top} (the step's longest launch)", "bytes_per_launch": sub[top]["bytes_per_launch"],
                      "avg_launch_ms": sub[top]["avg_launch_ms"]},
         "kernels": sub,
@@ -904,7 +914,8 @@ def bench_prefill(args, w, world, rank, local):
                 "d2h_bytes_per_step": int(h_o.numel() * 2)},
         "gpu_launches": int(launches_per_step * args.steps),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
+                     "peak_kind": peak_kind,
                      "kernel": "prefill_tc_kernel (tcgen05) per layer launch", "flops_per_launch": int(flops),
                      "avg_launch_ms": round(launch_ms, 4)},
         "clocks": clocks,
@@ -1127,7 +1138,8 @@ def bench_qkv(args, w, world, rank, local):
                 "d2h_bytes_per_step": int(h_q[0].numel() * h_q[0].element_size())},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor" if prefill else "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
+                     "peak_kind": peak_kind,
                      "kernel": ("split_hi_lo_kernel + qkv_append_kernel (plain mode) (+ qkv_finish_kernel when "
                                 "in_features is split) per layer (CUDA-graph replay, step time / layers)" if oproj
                                 else "qkv_append_kernel + rope_table_kernel (+ qkv_finish_kernel when the hidden "
