@@ -16,7 +16,9 @@ every row of a batch and a prefill call one prompt, in three steps:
   attention output entering as a 16-bit hi + lo pair so the products keep
   fp32 accuracy.
 
-Page bookkeeping follows `PagedKVCache`: pages for a prompt are reserved
+The pool is fp16 or bf16 (the fused append writes 16-bit rows; int8 and
+FP8 pools take their K/V through `KVPool.append`). Page bookkeeping follows
+`PagedKVCache`: pages for a prompt are reserved
 when layer 0 runs and the sequence's length advances after the last layer;
 a decode step reserves its token's pages on the device at layer 0.
 """
@@ -33,6 +35,11 @@ from .pool import rope_inv_freq, to_device
 class PagedAttentionLayer:
     def __init__(self, cache: PagedKVCache, num_q_heads: int, rope_theta: float = 10000.0,
                  rope_scaling: float = 1.0, rms_eps: float = 1e-6, scale: Optional[float] = None):
+        if cache.pool.kv_dtype not in ("fp16", "bf16"):
+            # the fused projection + norm + rotation + append writes 16-bit
+            # rows; one-byte pools take their K/V through KVPool.append
+            raise ValueError("PagedAttentionLayer needs an fp16 or bf16 pool "
+                             f"(got {cache.pool.kv_dtype!r})")
         if num_q_heads % cache.num_kv_heads != 0:
             raise ValueError("num_q_heads must be a multiple of the cache's kv heads "
                              "(models/adapters.py:1107-1111)")
