@@ -220,13 +220,16 @@ def o_project(attn_f32: np.ndarray, w_o: np.ndarray) -> np.ndarray:
 def attention_layer(x_f32: np.ndarray, w_q: np.ndarray, w_k: np.ndarray, w_v: np.ndarray, w_o: np.ndarray,
                     hq: int, hkv: int, prev_k: Optional[np.ndarray], prev_v: Optional[np.ndarray],
                     q_w: Optional[np.ndarray] = None, k_w: Optional[np.ndarray] = None, eps: float = 1e-6,
-                    theta: float = 10000.0, scaling: float = 1.0, scale: Optional[float] = None
-                    ) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+                    theta: float = 10000.0, scaling: float = 1.0, scale: Optional[float] = None,
+                    int8_cache: bool = False) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
     """ModularAttentionEngine.forward_numpy (models/adapters.py:1148-1231) for
     one sequence, composed from the steps above: projections (:1167-1169),
     QK-norm + RoPE from position len(prev) (:1171-1192), the fp16 cache
     concat (:1194-1207), causal SDPA (:1209-1229, no mask for one token) and
     o_proj (:1231). x [T, hidden]; prev_k / prev_v [Hkv, P, D] fp16 or None.
+    int8_cache: the new K / V rows go through the arena's int8 mode (quantised
+    per row as quantize_kv_int8, read back as dequantize_kv_int8,
+    native/native_engine.py:207-221) before the attention reads them.
     Returns (out [T, hidden] float32, k_full, v_full [Hkv, P + T, D] fp16)."""
     T = x_f32.shape[0]
     q, k, v = qkv_project(x_f32, w_q, w_k, w_v, hq, hkv)
@@ -235,6 +238,9 @@ def attention_layer(x_f32: np.ndarray, w_q: np.ndarray, w_k: np.ndarray, w_v: np
     qr, kc = qk_norm_rope(q, k, q_w, k_w, eps, rope_inv_freq(theta, d), scaling, start)
     k_new = kc.transpose(1, 0, 2)
     v_new = v.astype(np.float16).transpose(1, 0, 2)
+    if int8_cache:
+        k_new = dequantize_kv_int8(*quantize_kv_int8(k_new))
+        v_new = dequantize_kv_int8(*quantize_kv_int8(v_new))
     k_full = k_new if prev_k is None else np.concatenate([prev_k, k_new], axis=1)
     v_full = v_new if prev_v is None else np.concatenate([prev_v, v_new], axis=1)
     attn = sdpa_prefill(qr, k_full, v_full, start, scale)

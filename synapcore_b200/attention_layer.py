@@ -16,8 +16,10 @@ every row of a batch and a prefill call one prompt, in three steps:
   attention output entering as a 16-bit hi + lo pair so the products keep
   fp32 accuracy.
 
-The pool is fp16 or bf16 (the fused append writes 16-bit rows; int8 and
-FP8 pools take their K/V through `KVPool.append`). Page bookkeeping follows
+The pool is fp16, bf16 or int8 (the arena's int8 mode: each new K / V row
+quantised by the fused epilogue as the arena quantises its fp16 pages); FP8
+pools, whose page scale spans 16 tokens, take their K/V through
+`KVPool.append`. Page bookkeeping follows
 `PagedKVCache`: pages for a prompt are reserved
 when layer 0 runs and the sequence's length advances after the last layer;
 a decode step reserves its token's pages on the device at layer 0.
@@ -35,10 +37,10 @@ from .pool import rope_inv_freq, to_device
 class PagedAttentionLayer:
     def __init__(self, cache: PagedKVCache, num_q_heads: int, rope_theta: float = 10000.0,
                  rope_scaling: float = 1.0, rms_eps: float = 1e-6, scale: Optional[float] = None):
-        if cache.pool.kv_dtype not in ("fp16", "bf16"):
-            # the fused projection + norm + rotation + append writes 16-bit
-            # rows; one-byte pools take their K/V through KVPool.append
-            raise ValueError("PagedAttentionLayer needs an fp16 or bf16 pool "
+        if cache.pool.kv_dtype not in ("fp16", "bf16", "int8"):
+            # the fused projection + norm + rotation + append writes whole
+            # rows; an FP8 page's scale spans 16 tokens (KVPool.append does it)
+            raise ValueError("PagedAttentionLayer needs an fp16, bf16 or int8 pool "
                              f"(got {cache.pool.kv_dtype!r})")
         if num_q_heads % cache.num_kv_heads != 0:
             raise ValueError("num_q_heads must be a multiple of the cache's kv heads "

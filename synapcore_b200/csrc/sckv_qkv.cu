@@ -69,6 +69,7 @@ struct QkvCfg {
 struct QkvParams {
   void* q_out;
   void* pool_data;
+  __half* pool_scales;     // int8 pools: fp16 per-token scales [L][P][K|V][H][16]
   int32_t* status;
   const __half* q_norm_w;  // [128] or null
   const __half* k_norm_w;  // [128] or null
@@ -184,6 +185,26 @@ __device__ __forceinline__ void store32(void* dst, int64_t idx, int dtype, const
       d[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+}
+
+// int8 pools: a K or V row is stored as the arena quantises its fp16 pages
+// (quantize_kv_int8_numpy, native/native_engine.py:207-215): the fp16 value
+// x, s = max(max|x| / 127, 1e-7) in fp32, codes rint(x / s) clipped to
+// +-127, s kept as fp16. IEEE division, as the append kernel does.
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float int8_row_scale(float amax) { return fmaxf(amax / 127.0f, 1e-7f); }
+__device__ __forceinline__ uint32_t int8_code4(float a, float b, float c, float d, float s) {
+  const float v[4] = {a, b, c, d};
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float r = fminf(fmaxf(rintf(f16_round(v[i]) / s), -127.0f), 127.0f);
+    w |= (uint32_t)(uint8_t)(int8_t)r << (8 * i);
+  }
+  return w;
+}
+__device__ __forceinline__ int64_t int8_scale_index(const QkvParams& p, int64_t slab, int kv, int head, int pos) {
+  return ((slab * 2 + kv) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS;
 }
 
 // Split-K partial sums: per (head tile g = head + heads x token tile, split
@@ -309,7 +330,18 @@ __global__ void __launch_bounds__(256, 6) qkv_finish_kernel(const QkvParams p, i
     out_dtype = p.pool_dtype;
   }
   dst += 4 * lane;
-  if (out_dtype == SCKV_DTYPE_F32) {
+  if (out_dtype == SCKV_DTYPE_INT8) {
+    // the row's scale: max over the warp's 128 fp16 values
+    float m = fmaxf(fmaxf(fabsf(f16_round(y[0])), fabsf(f16_round(y[1]))),
+                    fmaxf(fabsf(f16_round(y[2])), fabsf(f16_round(y[3]))));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float s8 = int8_row_scale(m);
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(out) + dst) = int8_code4(y[0], y[1], y[2], y[3], s8);
+    if (lane == 0)
+      p.pool_scales[int8_scale_index(p, (int64_t)p.layer * p.max_pages + meta.y, kind - 1, head, meta.x)] =
+          __float2half_rn(s8);
+  } else if (out_dtype == SCKV_DTYPE_F32) {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + dst) = make_float4(y[0], y[1], y[2], y[3]);
   } else if (out_dtype == SCKV_DTYPE_BF16) {
     *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + dst) =
@@ -552,6 +584,13 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
             out = p.pool_data;
             out_dtype = p.pool_dtype;
           }
+          // int8 pools: a first pass finds the row's largest fp16 magnitude,
+          // the second stores the codes (tile-uniform, so the tensor-memory
+          // loads stay warp-wide)
+          const bool q8 = tl.kind > 0 && p.pool_dtype == SCKV_DTYPE_INT8;
+          float amax = 0.f, s8 = 1.f;
+#pragma unroll 1
+          for (int pass = q8 ? 0 : 1; pass < 2; ++pass) {
 #pragma unroll 1
           for (int hf = 0; hf < 2; ++hf) {
             // dims d = 32 hf + i and their rotation partners d + 64
@@ -578,8 +617,33 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
                 y2[i] = x2;
               }
             }
-            store32(out, dst + hf * 32, out_dtype, y1);
-            store32(out, dst + 64 + hf * 32, out_dtype, y2);
+            if (!q8) {
+              store32(out, dst + hf * 32, out_dtype, y1);
+              store32(out, dst + 64 + hf * 32, out_dtype, y2);
+            } else if (pass == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                amax = fmaxf(amax, fmaxf(fabsf(f16_round(y1[i])), fabsf(f16_round(y2[i]))));
+            } else {
+              uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                const float* y = half ? y2 : y1;
+                uint4* d4 = reinterpret_cast<uint4*>(o8 + dst + half * 64 + hf * 32);
+#pragma unroll
+                for (int v = 0; v < 2; ++v)
+                  d4[v] = make_uint4(int8_code4(y[16 * v], y[16 * v + 1], y[16 * v + 2], y[16 * v + 3], s8),
+                                     int8_code4(y[16 * v + 4], y[16 * v + 5], y[16 * v + 6], y[16 * v + 7], s8),
+                                     int8_code4(y[16 * v + 8], y[16 * v + 9], y[16 * v + 10], y[16 * v + 11], s8),
+                                     int8_code4(y[16 * v + 12], y[16 * v + 13], y[16 * v + 14], y[16 * v + 15], s8));
+              }
+            }
+          }
+          if (q8 && pass == 0) {
+            s8 = int8_row_scale(amax);
+            if (dst >= 0)
+              p.pool_scales[int8_scale_index(p, slot_row, tl.kind - 1, head, pos)] = __float2half_rn(s8);
+          }
           }
         }
       }
@@ -733,7 +797,10 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (x_dtype != SCKV_DTYPE_F16 && x_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
   if (q_out_dtype != SCKV_DTYPE_F32 && q_out_dtype != SCKV_DTYPE_F16 && q_out_dtype != SCKV_DTYPE_BF16)
     return SCKV_ERR_INVALID_ARG;
-  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+  // 16-bit pools, and int8 pools (each K / V row quantised as the arena
+  // does); FP8 page scales span 16 tokens, which one row cannot set
+  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16 && pool->kv_dtype != SCKV_DTYPE_INT8)
+    return SCKV_ERR_UNSUPPORTED;
   if (pool->head_dim != kHead) return SCKV_ERR_UNSUPPORTED;
   // norms over the whole projection need every head of a token: the
   // unfused path (projection, then sckv_append_rope) covers them
@@ -791,6 +858,7 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   QkvParams prm{};
   prm.q_out = q_out;
   prm.pool_data = pool->data;
+  prm.pool_scales = reinterpret_cast<__half*>(pool->scales);
   prm.status = pool->status;
   prm.q_norm_w = q_norm_len ? reinterpret_cast<const __half*>(q_norm_w) : nullptr;
   prm.k_norm_w = k_norm_len ? reinterpret_cast<const __half*>(k_norm_w) : nullptr;

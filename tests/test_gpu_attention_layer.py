@@ -191,6 +191,47 @@ def test_layer_prompt_batch_matches_oracle(cuda_device):
     cache.pool.raise_on_status()
 
 
+def test_layer_on_int8_pool_matches_oracle(cuda_device):
+    """The arena's int8 mode under a whole layer: new K / V rows quantised by
+    the fused projection epilogue (quantize_kv_int8), attention over the
+    dequantised pages, against the oracle's composition with the same int8
+    round trip of the cache. A prompt, then two decode steps (the second
+    crossing into a fresh page for one sequence)."""
+    from synapcore_b200 import PagedAttentionLayer, PagedKVCache
+
+    dev = cuda_device
+    hq, hkv = 8, 2
+    hidden = hq * D
+    eps, theta = 1e-6, 10000.0
+    rng = np.random.default_rng(23)
+    sd = 1.0 / np.sqrt(hidden)
+    W = [(rng.standard_normal(sh) * sd).astype(np.float16)
+         for sh in ((hq * D, hidden), (hkv * D, hidden), (hkv * D, hidden), (hidden, hq * D))]
+    NW = [rng.uniform(0.5, 1.5, D).astype(np.float16) for _ in range(2)]
+    Wd = [_dev(w, dev) for w in W]
+    NWd = [_dev(w, dev) for w in NW]
+    cache = PagedKVCache(1, hkv, D, max_pages=64, max_seqs=4, max_blocks_per_seq=16, kv_dtype="int8", device=dev)
+    layer = PagedAttentionLayer(cache, hq, rope_theta=theta, rms_eps=eps)
+    prompts = [47, 15]
+    hk = [None, None]
+    hv = [None, None]
+    for b, T in enumerate(prompts):
+        cache.add_sequence(b)
+        x = rng.standard_normal((T, hidden)).astype(np.float32)
+        out = layer.prefill(0, b, _dev(x, dev), *Wd, q_norm_w=NWd[0], k_norm_w=NWd[1]).cpu().numpy()
+        ref, hk[b], hv[b] = O.attention_layer(x, *W, hq, hkv, hk[b], hv[b], NW[0], NW[1], eps, theta, int8_cache=True)
+        assert _rel_err(out, ref) <= ATTN_TOL, b
+    for step in range(2):
+        x = rng.standard_normal((2, hidden)).astype(np.float32)
+        out = layer.decode(0, _dev(x, dev), 2, *Wd, q_norm_w=NWd[0], k_norm_w=NWd[1]).cpu().numpy()
+        for b in range(2):
+            ref, hk[b], hv[b] = O.attention_layer(x[b:b + 1], *W, hq, hkv, hk[b], hv[b], NW[0], NW[1], eps, theta,
+                                                  int8_cache=True)
+            assert _rel_err(out[b:b + 1], ref) <= ATTN_TOL, (step, b)
+    torch.cuda.synchronize()
+    cache.pool.raise_on_status()
+
+
 @pytest.mark.parametrize("n_tok,fin,fout,x_kind,wdt,out_dtype", [
     (1, 512, 1024, "f32", torch.float16, torch.float32),        # decode size: split over in_features
     (128, 4096, 4096, "f32", torch.float16, torch.float32),     # Qwen3-8B decode batch, 4-way split

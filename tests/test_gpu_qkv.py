@@ -152,3 +152,55 @@ def test_qkv_append_reports_bad_pages_and_rejects_unsupported(cuda_device):
     with pytest.raises(N.SCKVError) as e:
         pool.qkv_append(0, xb, *wb, cu, st, bt, inv)
     assert e.value.code == N.SCKV_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("hidden,Ts", [(256, [40, 3, 0, 90]), (2048, [5, 1, 9])])  # unsplit; split + finishing kernel
+def test_qkv_append_int8_pool_quantises_rows_as_the_arena(cuda_device, hidden, Ts):
+    """int8 pools: every new K / V row is stored as the arena's int8 mode
+    stores its fp16 pages (quantize_kv_int8: per-row scale max|x|/127,
+    round-half-even codes). The fp16 row may differ from numpy's by one ulp
+    (projection sum order), so codes are checked through their dequantised
+    values: within one quantisation step of the oracle's."""
+    from synapcore_b200.pool import KVPool
+
+    dev = cuda_device
+    rng = np.random.default_rng(31)
+    hq, hkv = 8, 2
+    n = sum(Ts)
+    x = rng.standard_normal((n, hidden)).astype(np.float32)
+    sc = 1.0 / np.sqrt(hidden)
+    w = [(rng.standard_normal((h * D, hidden)) * sc).astype(np.float16) for h in (hq, hkv, hkv)]
+    qw, kw = rng.uniform(0.5, 1.5, D).astype(np.float16), rng.uniform(0.5, 1.5, D).astype(np.float16)
+    starts = [3, 17, 0, 40][:len(Ts)]
+    inv = O.rope_inv_freq(10000.0, D)
+    cu = np.concatenate([[0], np.cumsum(Ts)]).astype(np.int32)
+    mb = max((s + t + 15) // 16 for s, t in zip(starts, Ts))
+    P = len(Ts) * mb + 2
+    pool = KVPool(1, hkv, D, P, "int8", device=dev)
+    bt = rng.permutation(P)[:len(Ts) * mb].reshape(len(Ts), mb).astype(np.int32)
+    pool.qkv_append(0, torch.from_numpy(x).to(dev), *(torch.from_numpy(a).to(dev) for a in w),
+                    torch.from_numpy(cu).to(dev), torch.from_numpy(np.array(starts, np.int32)).to(dev),
+                    torch.from_numpy(bt).to(dev), torch.from_numpy(inv).to(dev), q_norm_w=torch.from_numpy(qw).to(dev),
+                    k_norm_w=torch.from_numpy(kw).to(dev), eps=1e-6)
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    codes = pool.pool_view()[0].cpu().numpy()      # [P, 2, H, 16, D] int8
+    scales = pool.scale_view()[0].cpu().numpy()    # [P, 2, H, 16] fp16
+    q_all, k_all, v_all = O.qkv_project(x, *(a.astype(np.float32) for a in w), hq, hkv)
+    for b, (s0, t) in enumerate(zip(starts, Ts)):
+        if t == 0:
+            continue
+        sl = slice(cu[b], cu[b + 1])
+        _, k16 = O.qk_norm_rope(q_all[sl], k_all[sl], qw, kw, 1e-6, inv, 1.0, s0)   # [t, Hkv, D] fp16
+        v16 = v_all[sl].astype(np.float16)
+        pos = np.arange(s0, s0 + t)
+        for kv, ref16 in ((0, k16), (1, v16)):
+            rq, rs = O.quantize_kv_int8(ref16)
+            ref = O.dequantize_kv_int8(rq, rs).astype(np.float32)
+            gq = codes[bt[b, pos // 16], kv, :, pos % 16]          # [t, Hkv, D]
+            gs = scales[bt[b, pos // 16], kv, :, pos % 16]         # [t, Hkv]
+            got = O.dequantize_kv_int8(gq, gs[..., None]).astype(np.float32)
+            step = rs.astype(np.float32)
+            assert np.all(np.abs(got - ref) <= 1.01 * step + 2e-3 * np.abs(ref)), (b, kv)
+            assert np.all(np.abs(gs.astype(np.float32) - rs[..., 0].astype(np.float32))
+                          <= 2e-3 * rs[..., 0].astype(np.float32) + 1e-7)
