@@ -235,9 +235,11 @@ SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
                      int64_t bt_stride, int max_blocks, void* stream);
 
 /* Projections + per-head QK-norm + RoPE + K/V append of one layer in one
- * tcgen05 kernel (f16, bf16 and int8 pools, head_dim 128; an int8 pool gets
- * each new K / V row quantised as the arena quantises its fp16 pages,
- * native/native_engine.py:207-216; FP8 pools: SCKV_ERR_UNSUPPORTED). Replaces q/k/v = x @ W^T
+ * tcgen05 kernel (head_dim 128). f16 / bf16 pools take the rows directly;
+ * an int8 pool gets each new K / V row quantised as the arena quantises its
+ * fp16 pages (native/native_engine.py:207-216); an FP8 pool gets the rows
+ * staged in fp16 in the workspace and stored by the FP8 append (page
+ * scales grow with the tokens a page holds), one more launch. Replaces q/k/v = x @ W^T
  * (models/adapters.py:1167-1169, fp16 weights), the per-head RMSNorm
  * (:1171-1185), RoPE (:1191-1192) and the KV-cache concat (:1194-1207) of
  * ModularAttentionEngine.forward_numpy: k and v of token i of sequence b

@@ -16,10 +16,10 @@ every row of a batch and a prefill call one prompt, in three steps:
   attention output entering as a 16-bit hi + lo pair so the products keep
   fp32 accuracy.
 
-The pool is fp16, bf16 or int8 (the arena's int8 mode: each new K / V row
-quantised by the fused epilogue as the arena quantises its fp16 pages); FP8
-pools, whose page scale spans 16 tokens, take their K/V through
-`KVPool.append`. Page bookkeeping follows
+Every pool type works: fp16 / bf16 rows are stored by the fused epilogue,
+int8 rows quantised there as the arena quantises its fp16 pages, and FP8
+rows (whose page scale spans 16 tokens) staged in fp16 and stored by the
+FP8 append launch that follows. Page bookkeeping follows
 `PagedKVCache`: pages for a prompt are reserved
 when layer 0 runs and the sequence's length advances after the last layer;
 a decode step reserves its token's pages on the device at layer 0.
@@ -37,11 +37,6 @@ from .pool import rope_inv_freq, to_device
 class PagedAttentionLayer:
     def __init__(self, cache: PagedKVCache, num_q_heads: int, rope_theta: float = 10000.0,
                  rope_scaling: float = 1.0, rms_eps: float = 1e-6, scale: Optional[float] = None):
-        if cache.pool.kv_dtype not in ("fp16", "bf16", "int8"):
-            # the fused projection + norm + rotation + append writes whole
-            # rows; an FP8 page's scale spans 16 tokens (KVPool.append does it)
-            raise ValueError("PagedAttentionLayer needs an fp16, bf16 or int8 pool "
-                             f"(got {cache.pool.kv_dtype!r})")
         if num_q_heads % cache.num_kv_heads != 0:
             raise ValueError("num_q_heads must be a multiple of the cache's kv heads "
                              "(models/adapters.py:1107-1111)")

@@ -70,6 +70,8 @@ struct QkvParams {
   void* q_out;
   void* pool_data;
   __half* pool_scales;     // int8 pools: fp16 per-token scales [L][P][K|V][H][16]
+  __half* k_stage;         // FP8 pools: the new K / V rows [n_tok][Hkv][128] fp16, appended afterwards
+  __half* v_stage;
   int32_t* status;
   const __half* q_norm_w;  // [128] or null
   const __half* k_norm_w;  // [128] or null
@@ -322,6 +324,10 @@ __global__ void __launch_bounds__(256, 6) qkv_finish_kernel(const QkvParams p, i
     dst = ((int64_t)t * p.hq + head) * kHead;
     out = p.q_out;
     out_dtype = p.q_out_dtype;
+  } else if (p.k_stage != nullptr) {
+    dst = ((int64_t)t * p.hkv + head) * kHead;
+    out = kind == 1 ? p.k_stage : p.v_stage;
+    out_dtype = SCKV_DTYPE_F16;
   } else {
     if (meta.y < 0) return;  // reported by token_meta
     const int64_t slab = (int64_t)p.layer * p.max_pages + meta.y;
@@ -546,9 +552,11 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       } else {
         const __half* nw = tl.kind == 0 ? p.q_norm_w : (tl.kind == 1 ? p.k_norm_w : nullptr);
         const bool live = tok < p.n_tok;
-        // the token's page slab (k and v tiles); q rows go to q_out
+        // the token's page slab (k and v tiles); q rows go to q_out; FP8
+        // pools stage the k / v rows for the FP8 append
+        const bool stage = tl.kind > 0 && p.k_stage != nullptr;  // tile-uniform
         int pos = 0;
-        const int64_t slot_row = (live && tl.kind > 0) ? token_slab(p, tok, &pos, tl.head0 == 0) : -1;
+        const int64_t slot_row = (live && tl.kind > 0 && !stage) ? token_slab(p, tok, &pos, tl.head0 == 0) : -1;
 #pragma unroll 1
         for (int hh = 0; hh < kHeads; ++hh) {
           const int head = tl.head0 + hh;
@@ -577,6 +585,10 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
           int out_dtype = p.q_out_dtype;
           if (live && tl.kind == 0) {
             dst = ((int64_t)tok * p.hq + head) * kHead;
+          } else if (live && stage) {
+            dst = ((int64_t)tok * p.hkv + head) * kHead;
+            out = tl.kind == 1 ? p.k_stage : p.v_stage;
+            out_dtype = SCKV_DTYPE_F16;
           } else if (slot_row >= 0) {
             // data layout [L][P][K|V][H][16][D]
             dst = (((slot_row * 2 + (tl.kind - 1)) * p.hkv + head) * SCKV_PAGE_TOKENS + pos % SCKV_PAGE_TOKENS) *
@@ -719,13 +731,28 @@ size_t split_part_bytes(int64_t n_tokens, int64_t n_tiles_out, int64_t ks) {
   return (size_t)ks * n_tiles_out * ((n_tokens + kQkvBM - 1) / kQkvBM) * kQkvBM * kHead * sizeof(float);
 }
 
-// The cos / sin table, then (split) the partial sums and the per-token lookups.
-size_t qkv_workspace_bytes(int64_t n_tokens, int64_t n_heads, int hidden, int num_sms) {
+// Workspace of one sckv_qkv_append call, in order: the cos / sin table;
+// split over the hidden dim, the partial sums and the per-token lookups;
+// for FP8 pools, the new K and V rows in fp16 (the FP8 append takes them
+// from there). Offsets are 256-byte aligned.
+struct QkvWs {
+  size_t part, meta, kstage, vstage, total;
+};
+
+inline size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+QkvWs qkv_workspace(int64_t n_tokens, int64_t hkv, int64_t n_heads, int hidden, int num_sms, bool stage_kv) {
   const int per = qkv_steps_per_split(n_tokens, n_heads, hidden, num_sms);
   const int nk = (hidden + kQkvBK - 1) / kQkvBK;
   const int64_t ks = (nk + per - 1) / per;
-  return (size_t)n_tokens * kRopePairs * sizeof(float2) + split_part_bytes(n_tokens, n_heads, ks) +
-         (ks > 1 ? (size_t)n_tokens * sizeof(int2) : 0);
+  QkvWs w;
+  w.part = align256((size_t)n_tokens * kRopePairs * sizeof(float2));
+  w.meta = align256(w.part + split_part_bytes(n_tokens, n_heads, ks));
+  w.kstage = align256(w.meta + (ks > 1 ? (size_t)n_tokens * sizeof(int2) : 0));
+  const size_t rows = stage_kv ? (size_t)n_tokens * hkv * kHead * sizeof(__half) : 0;
+  w.vstage = align256(w.kstage + rows);
+  w.total = w.vstage + rows;
+  return w;
 }
 
 size_t oproj_workspace_bytes(int64_t n_tokens, int in_features, int out_features, int num_sms) {
@@ -770,7 +797,9 @@ int launch_projection(const QkvParams& prm, const CUtensorMap (&maps)[5], bool b
 
 extern "C" size_t sckv_qkv_workspace_bytes(const sckv_pool* pool, int n_tokens, int num_q_heads, int hidden) {
   if (pool == nullptr || n_tokens < 0 || num_q_heads <= 0 || hidden <= 0) return 0;
-  return qkv_workspace_bytes(n_tokens, (int64_t)num_q_heads + 2LL * pool->num_kv_heads, hidden, pool->num_sms);
+  return qkv_workspace(n_tokens, pool->num_kv_heads, (int64_t)num_q_heads + 2LL * pool->num_kv_heads, hidden,
+                       pool->num_sms, pool->kv_dtype == SCKV_DTYPE_FP8_E4M3)
+      .total;
 }
 
 extern "C" int sckv_split_hi_lo(const float* x, int64_t n, void* hi, void* lo, int dtype, void* stream) {
@@ -797,9 +826,10 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (x_dtype != SCKV_DTYPE_F16 && x_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_INVALID_ARG;
   if (q_out_dtype != SCKV_DTYPE_F32 && q_out_dtype != SCKV_DTYPE_F16 && q_out_dtype != SCKV_DTYPE_BF16)
     return SCKV_ERR_INVALID_ARG;
-  // 16-bit pools, and int8 pools (each K / V row quantised as the arena
-  // does); FP8 page scales span 16 tokens, which one row cannot set
-  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16 && pool->kv_dtype != SCKV_DTYPE_INT8)
+  // 16-bit pools; int8 pools (each K / V row quantised as the arena does);
+  // FP8 pools through a second launch (their page scales span 16 tokens)
+  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16 && pool->kv_dtype != SCKV_DTYPE_INT8 &&
+      pool->kv_dtype != SCKV_DTYPE_FP8_E4M3)
     return SCKV_ERR_UNSUPPORTED;
   if (pool->head_dim != kHead) return SCKV_ERR_UNSUPPORTED;
   // norms over the whole projection need every head of a token: the
@@ -813,9 +843,10 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (!x || !w_q || !w_k || !w_v || !inv_freq || !cu_tokens || !start_pos || !block_table || !q_out ||
       !workspace || max_blocks <= 0 || bt_stride < max_blocks || !(rope_scaling != 0.f))
     return SCKV_ERR_INVALID_ARG;
-  if (workspace_bytes < qkv_workspace_bytes(n_tokens, (int64_t)num_q_heads + 2LL * pool->num_kv_heads, hidden,
-                                            pool->num_sms))
-    return SCKV_ERR_INVALID_ARG;
+  const bool stage_kv = pool->kv_dtype == SCKV_DTYPE_FP8_E4M3;
+  const QkvWs ws = qkv_workspace(n_tokens, pool->num_kv_heads, (int64_t)num_q_heads + 2LL * pool->num_kv_heads,
+                                 hidden, pool->num_sms, stage_kv);
+  if (workspace_bytes < ws.total) return SCKV_ERR_INVALID_ARG;
   if (!aligned16(x) || (x_lo && !aligned16(x_lo)) || !aligned16(w_q) || !aligned16(w_k) || !aligned16(w_v) ||
       !aligned16(q_out) || !aligned16(workspace))
     return SCKV_ERR_ALIGNMENT;
@@ -883,13 +914,22 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   prm.k_steps_per_split = per_split;
   prm.hd_total = (int)(n_heads * kHead);
   prm.k_splits = k_splits;
+  char* wsb = reinterpret_cast<char*>(workspace);
   if (k_splits > 1) {
-    char* w = reinterpret_cast<char*>(workspace) + (size_t)n_tokens * kRopePairs * sizeof(float2);
-    prm.partial = reinterpret_cast<float*>(w);
-    prm.tok_meta = reinterpret_cast<int2*>(w + split_part_bytes(n_tokens, n_heads, k_splits));
+    prm.partial = reinterpret_cast<float*>(wsb + ws.part);
+    prm.tok_meta = reinterpret_cast<int2*>(wsb + ws.meta);
   }
-  return launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
-                           pool->num_sms, s);
+  if (stage_kv) {
+    prm.k_stage = reinterpret_cast<__half*>(wsb + ws.kstage);
+    prm.v_stage = reinterpret_cast<__half*>(wsb + ws.vstage);
+  }
+  rc = launch_projection(prm, maps, bf16, x_lo != nullptr, k_splits, heads, n_groups, (int)m_tiles,
+                         pool->num_sms, s);
+  if (rc != SCKV_OK || !stage_kv) return rc;
+  // FP8 pools: the page-head scales grow with the tokens a page holds, so
+  // the rows go through the FP8 append (scale growth, re-encoding)
+  return sckv_append(pool, layer, 1, prm.k_stage, prm.v_stage, SCKV_DTYPE_F16, n_seqs, n_tokens, cu_tokens,
+                     start_pos, block_table, bt_stride, max_blocks, stream);
 }
 
 extern "C" size_t sckv_o_proj_workspace_bytes(const sckv_pool* pool, int n_tokens, int in_features,

@@ -232,6 +232,52 @@ def test_layer_on_int8_pool_matches_oracle(cuda_device):
     cache.pool.raise_on_status()
 
 
+def test_layer_on_fp8_pool_matches_oracle_over_its_pages(cuda_device):
+    """FP8 pools under a whole layer (rows staged, then the FP8 append): a
+    prompt then a decode step; each output against the oracle's causal SDPA
+    and o_proj over the K / V the pool actually holds (decoded from its
+    pages), with the oracle's own rotated q. How the rows are encoded is
+    checked against the oracle's FP8 pool in test_gpu_qkv.py."""
+    from synapcore_b200 import PagedAttentionLayer, PagedKVCache
+
+    dev = cuda_device
+    hq, hkv = 8, 2
+    hidden = hq * D
+    eps, theta = 1e-6, 10000.0
+    rng = np.random.default_rng(29)
+    sd = 1.0 / np.sqrt(hidden)
+    W = [(rng.standard_normal(sh) * sd).astype(np.float16)
+         for sh in ((hq * D, hidden), (hkv * D, hidden), (hkv * D, hidden), (hidden, hq * D))]
+    NW = [rng.uniform(0.5, 1.5, D).astype(np.float16) for _ in range(2)]
+    cache = PagedKVCache(1, hkv, D, max_pages=32, max_seqs=2, max_blocks_per_seq=8, kv_dtype="fp8_e4m3",
+                         device=dev)
+    layer = PagedAttentionLayer(cache, hq, rope_theta=theta, rms_eps=eps)
+    cache.add_sequence("s")
+    inv = O.rope_inv_freq(theta, D)
+    start = 0
+    for T in (37, 1):
+        x = rng.standard_normal((T, hidden)).astype(np.float32)
+        xd = _dev(x, dev)
+        wd = [_dev(w, dev) for w in W]
+        if T > 1:
+            out = layer.prefill(0, "s", xd, *wd, q_norm_w=_dev(NW[0], dev), k_norm_w=_dev(NW[1], dev))
+        else:
+            out = layer.decode(0, xd, 1, *wd, q_norm_w=_dev(NW[0], dev), k_norm_w=_dev(NW[1], dev))
+        torch.cuda.synchronize()
+        cache.pool.raise_on_status()
+        n = start + T
+        pages = cache.page_ids("s")
+        codes = cache.pool.pool_view()[0].cpu().numpy()
+        scales = cache.pool.scale_view()[0].cpu().numpy()
+        kv = np.stack([np.concatenate([O.fp8_decode(codes[pg, i]) * scales[pg, i][:, None, None] for pg in pages],
+                                      axis=1)[:, :n] for i in range(2)])        # [2, Hkv, n, D]
+        q, k, _ = O.qkv_project(x, *(w.astype(np.float32) for w in W[:3]), hq, hkv)
+        qr, _ = O.qk_norm_rope(q, k, NW[0], NW[1], eps, inv, 1.0, start)
+        ref = O.o_project(O.sdpa_prefill(qr, kv[0], kv[1], start), W[3])
+        assert _rel_err(out.cpu().numpy(), ref) <= ATTN_TOL, T
+        start = n
+
+
 @pytest.mark.parametrize("n_tok,fin,fout,x_kind,wdt,out_dtype", [
     (1, 512, 1024, "f32", torch.float16, torch.float32),        # decode size: split over in_features
     (128, 4096, 4096, "f32", torch.float16, torch.float32),     # Qwen3-8B decode batch, 4-way split

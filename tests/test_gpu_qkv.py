@@ -143,9 +143,10 @@ def test_qkv_append_reports_bad_pages_and_rejects_unsupported(cuda_device):
     code, detail, _, _ = pool.status()
     assert code == N.SCKV_ERR_BOUNDS and detail == 9
     pool.clear_status()
-    fp8 = KVPool(1, hkv, D, 4, "fp8_e4m3", device=dev)
+    d64 = KVPool(1, hkv, 64, 4, "fp16", device=dev)  # head_dim 128 only
+    w64 = [torch.randn(h * 64, hidden, device=dev, dtype=torch.float16) * 0.05 for h in (hq, hkv, hkv)]
     with pytest.raises(N.SCKVError) as e:
-        fp8.qkv_append(0, x, *w, cu, st, bt[:, :1], inv)
+        d64.qkv_append(0, x, *w64, cu, st, bt[:, :1], inv[:32])
     assert e.value.code == N.SCKV_ERR_UNSUPPORTED
     xb = torch.randn(4, 100, device=dev, dtype=torch.float16)  # hidden % 8 != 0
     wb = [torch.randn(h * D, 100, device=dev, dtype=torch.float16) for h in (hq, hkv, hkv)]
@@ -204,3 +205,55 @@ def test_qkv_append_int8_pool_quantises_rows_as_the_arena(cuda_device, hidden, T
             assert np.all(np.abs(got - ref) <= 1.01 * step + 2e-3 * np.abs(ref)), (b, kv)
             assert np.all(np.abs(gs.astype(np.float32) - rs[..., 0].astype(np.float32))
                           <= 2e-3 * rs[..., 0].astype(np.float32) + 1e-7)
+
+
+def test_qkv_append_fp8_pool_through_the_fp8_append(cuda_device):
+    """FP8 pools: the projection stages the new K / V rows in fp16 and the
+    FP8 append stores them (per-page-head scale max|x| / 448, grown and
+    re-encoded as later tokens of a page arrive). Two calls, the second
+    filling pages the first left partial, against the oracle's FP8 pool fed
+    the oracle's fp16 rows. A row one fp16 ulp off can move an e4m3 code by
+    one step (2^-3 relative) and a page scale slightly, hence the bound."""
+    from synapcore_b200.pool import KVPool
+
+    dev = cuda_device
+    rng = np.random.default_rng(41)
+    hq, hkv, hidden = 8, 2, 512
+    sc = 1.0 / np.sqrt(hidden)
+    w = [(rng.standard_normal((h * D, hidden)) * sc).astype(np.float16) for h in (hq, hkv, hkv)]
+    qw, kw = rng.uniform(0.5, 1.5, D).astype(np.float16), rng.uniform(0.5, 1.5, D).astype(np.float16)
+    inv = O.rope_inv_freq(10000.0, D)
+    mb, P = 4, 16
+    bt = rng.permutation(P)[:3 * mb].reshape(3, mb).astype(np.int32)
+    pool = KVPool(1, hkv, D, P, "fp8_e4m3", device=dev)
+    ora = O.PagedPoolOracle(1, hkv, D, P, "fp8_e4m3")
+    lens = [0, 0, 0]
+    for Ts in ([5, 20, 1], [7, 30, 16]):
+        n = sum(Ts)
+        x = rng.standard_normal((n, hidden)).astype(np.float32)
+        cu = np.concatenate([[0], np.cumsum(Ts)]).astype(np.int32)
+        st = np.array(lens, np.int32)
+        pool.qkv_append(0, torch.from_numpy(x).to(dev), *(torch.from_numpy(a).to(dev) for a in w),
+                        torch.from_numpy(cu).to(dev), torch.from_numpy(st).to(dev), torch.from_numpy(bt).to(dev),
+                        torch.from_numpy(inv).to(dev), q_norm_w=torch.from_numpy(qw).to(dev),
+                        k_norm_w=torch.from_numpy(kw).to(dev), eps=1e-6)
+        q_all, k_all, v_all = O.qkv_project(x, *(a.astype(np.float32) for a in w), hq, hkv)
+        k16 = np.zeros((n, hkv, D), np.float16)
+        for b in range(3):
+            sl = slice(cu[b], cu[b + 1])
+            if Ts[b]:
+                _, k16[sl] = O.qk_norm_rope(q_all[sl], k_all[sl], qw, kw, 1e-6, inv, 1.0, lens[b])
+        v16 = v_all.astype(np.float16)
+        ora.append(0, k16.astype(np.float32)[None], v16.astype(np.float32)[None], cu, st, bt)
+        lens = [a + b for a, b in zip(lens, Ts)]
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    codes = pool.pool_view()[0].cpu().numpy()
+    scales = pool.scale_view()[0].cpu().numpy()
+    for b in range(3):
+        for page in bt[b, :(lens[b] + 15) // 16]:
+            for kv in range(2):
+                ref = ora.values(0, page, kv)
+                got = O.fp8_decode(codes[page, kv]) * scales[page, kv][:, None, None]
+                pmax = np.max(np.abs(ref), axis=(1, 2), keepdims=True)
+                assert np.all(np.abs(got - ref) <= 0.07 * np.abs(ref) + 0.01 * pmax), (b, page, kv)
