@@ -122,6 +122,12 @@ WORKLOADS = {
                       kv="bf16", batch=128, tokens_per_seq=1, ctx=16384),
     "qwen3-qkv-prefill": dict(kind="qkv", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
                               kv="bf16", batch=8, tokens_per_seq=1024, ctx=0),
+    # the whole attention layer at BASELINE config 4's shape and FP8 pool,
+    # through PagedAttentionLayer.decode: fused q/k/v projection + QK-norm +
+    # RoPE (rows staged, FP8 append), decode attention over 16,384 tokens,
+    # o_proj; fp32 normed input x and fp16 weights as the reference engine
+    "qwen3-fp8-layer": dict(kind="layer", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
+                            kv="fp8_e4m3", batch=128, ctx=16384),
     # the other side: o_proj of the fp32 attention output with fp16 weights
     # (models/adapters.py:1231), one sckv_o_proj per layer
     "qwen3-oproj": dict(kind="oproj", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
@@ -944,6 +950,161 @@ def qkv_bytes(w, n_tok: int) -> int:
     return 2 * (hd * w["hidden"] + n_tok * w["hidden"] + n_tok * hd)
 
 
+def bench_layer(args, w, world, rank, local):
+    """One step = PagedAttentionLayer.decode for every layer: one new token
+    for each of `batch` sequences whose contexts start at `ctx` (seeded FP8
+    pages) and grow by one per step."""
+    from synapcore_b200 import PagedAttentionLayer, PagedKVCache
+    from synapcore_b200 import _native as N
+
+    dev = torch.device("cuda", local)
+    L, H, hq, d, hidden, B, ctx0 = w["layers"], w["hkv"], w["hq"], w["d"], w["hidden"], w["batch"], w["ctx"]
+    steps_total = args.warmup + 2 * args.steps + 2
+    blocks = (ctx0 + steps_total + PAGE - 1) // PAGE
+    cache = PagedKVCache(L, H, d, max_pages=B * blocks + 64, max_seqs=B, max_blocks_per_seq=blocks, kv_dtype=w["kv"],
+                         device=dev)
+    # synthetic contexts: every sequence holds ctx0 tokens of seeded pages
+    for b in range(B):
+        cache.add_sequence(b)
+    cache._grow_rows(0, [ctx0] * B)
+    for b in range(B):
+        cache.lengths[b] = ctx0
+    cache.ctx_lens[:B].fill_(ctx0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    view = cache.pool.pool_view()
+    for l in range(L):
+        for c0 in range(0, view.shape[1], 8192):
+            blk = view[l, c0:c0 + 8192]
+            codes = torch.randint(0, 0x7F, blk.shape, dtype=torch.uint8, device=dev, generator=g)
+            codes |= torch.randint(0, 2, blk.shape, dtype=torch.uint8, device=dev, generator=g) << 7
+            blk.copy_(codes)
+            del codes
+    cache.pool.scale_view().uniform_(0.5 / 448 * 4, 4.0 / 448 * 4, generator=g)
+    layer = PagedAttentionLayer(cache, hq, rope_theta=1e6, rms_eps=1e-6)
+    sc = hidden ** -0.5
+    wts = [[(torch.randn(r, c, device=dev, generator=g) * sc).half()
+            for r, c in ((hq * d, hidden), (H * d, hidden), (H * d, hidden), (hidden, hq * d))] for _ in range(L)]
+    qn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+    kn = torch.rand(d, device=dev, generator=g).add_(0.5).half()
+    x = torch.randn(L, B, hidden, device=dev, generator=g)
+    out = torch.empty(B, hidden, device=dev)
+
+    def step():
+        for l in range(L):
+            o = layer.decode(l, x[l], B, *wts[l], q_norm_w=qn, k_norm_w=kn)
+        out.copy_(o)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    cache.pool.raise_on_status()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    n0 = N.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    launches = N.launch_count() - n0
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    cache.pool.raise_on_status()
+    # e2e: each step's normed inputs come from pinned host memory and the
+    # last layer's output goes back
+    h_x = x.cpu().pin_memory()
+    h_o = torch.empty(B, hidden).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        x.copy_(h_x, non_blocking=True)
+        step()
+        h_o.copy_(out, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world) / args.steps
+    # algorithmic bytes per step: K/V codes + page scales read, weights and
+    # activations, the new rows
+    ctx_mid = ctx0 + args.warmup + args.steps // 2
+    kv_b = B * ctx_mid * H * d * 2 + B * ((ctx_mid + PAGE - 1) // PAGE) * H * 2 * 4
+    w_b = 2 * ((hq + 2 * H) * d * hidden + hidden * hq * d)
+    act_b = B * (hidden * 4 + hq * d * 4 * 2 + hidden * 4)
+    per_layer = kv_b + w_b + act_b
+    peak, peak_kind = measured_peak_gbs()
+    achieved = per_layer / (ms * 1e-3 / L) / 1e9
+    res = {
+        "metric": "whole attention layer decode tok/s (projections, FP8 paged attention, o_proj)",
+        "value": round(world * B / (ms * 1e-3), 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8 KV, fp16 weights, fp32 activations",
+        "data": "synthetic (seeded e4m3 pages and U[0.5,4]-scaled page scales, N(0,1) inputs, N(0,1/hidden) weights)",
+        "kv_gb_per_s": round(world * L * per_layer / (ms * 1e-3) / 1e9, 1),
+        "config": {"workload": f"{args.workload}: {w['model']} {L} layers, hidden {hidden}, {hq}q/{H}kv heads x d{d}, "
+                               f"FP8 pool, {B} sequences from {ctx0} tokens, one token each per step through "
+                               f"PagedAttentionLayer.decode",
+                   "global_batch": world * B, "seq_len": ctx0, "parallelism": f"sequence-sharded x{world}",
+                   "l2": "each layer's K/V (%.1f GB) >> L2" % (kv_b / 1e9)},
+        "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": int(h_x.numel() * 4), "d2h_bytes_per_step": int(h_o.numel() * 4)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "one layer's launches (projection, finish, FP8 append, reserve, decode attention, "
+                               "combine, split, o_proj), step time / layers",
+                     "bytes_per_launch": int(per_layer), "avg_launch_ms": round(ms / L, 4)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_layer(w, budget_s=args.cpu_seconds)
+    return res
+
+
+def cpu_baseline_layer(w, budget_s: float = 15.0):
+    """The reference's forward_numpy for one layer and one decode token of a
+    sequence with `ctx` cached tokens (oracle composition of
+    models/adapters.py:1148-1231), repeated for ~budget_s; tok/s of the full
+    model step extrapolated (/ layers)."""
+    from oracle.kv_oracle import attention_layer
+
+    rng = np.random.default_rng(0)
+    hidden, hq, H, d, ctx = w["hidden"], w["hq"], w["hkv"], w["d"], w["ctx"]
+    sc = hidden ** -0.5
+    wts = [(rng.standard_normal(sh) * sc).astype(np.float16)
+           for sh in ((hq * d, hidden), (H * d, hidden), (H * d, hidden), (hidden, hq * d))]
+    qn = kn = np.ones(d, np.float16)
+    pk = rng.standard_normal((H, ctx, d)).astype(np.float16)
+    pv = rng.standard_normal((H, ctx, d)).astype(np.float16)
+    x = rng.standard_normal((1, hidden)).astype(np.float32)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        attention_layer(x, *wts, hq, H, pk, pv, qn, kn, 1e-6, 1e6)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    return {"value": round(reps / el / w["layers"], 4), "unit": "tok/s",
+            "cores": int(os.environ.get("OMP_NUM_THREADS", "0") or 0) or (os.cpu_count() or 1), "kind": "port",
+            "sample": f"1 layer x 1 sequence x ctx {ctx} (fp16 cache), {reps} reps in {el:.1f}s; "
+                      f"tok/s = layer calls per second / {w['layers']} layers"}
+
+
 def bench_qkv(args, w, world, rank, local):
     """One step = sckv_qkv_append for every layer over the step's tokens
     (decode: one token per sequence; prefill: whole prompts)."""
@@ -1609,12 +1770,24 @@ def bench_reference(args, w, world, rank):
             r = cpu_baseline_prefill(w, budget_s=budget)
         elif kind == "paging":
             r = cpu_baseline_gather(w, budget_s=budget)
+        elif kind == "layer":
+            r = cpu_baseline_layer(w, budget_s=budget)
         else:
             r = cpu_baseline(w, budget_s=budget)
         if i >= args.warmup:
             steps.append(r["value"])
     val = float(np.mean(steps))
     cores = os.cpu_count() or 1
+    if kind == "layer":
+        return {"metric": "whole attention layer decode tok/s (projections, FP8 paged attention, o_proj)",
+                "impl": "reference", "value": round(val, 6), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+                "config": {"workload": f"{args.workload}: reference NumPy forward_numpy on a bounded host sample",
+                           "parallelism": "host cores"},
+                "cpu_baseline": {"value": round(val, 6), "unit": "tok/s", "cores": cores, "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": round(val, 6), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if kind in ("prefill", "paging"):
         return {"metric": ("causal prefill attention TFLOP/s (counting the causal half)" if kind == "prefill"
                            else "paging kernels GB/s (append + gather + CoW page copy)"),
@@ -1681,6 +1854,8 @@ def main():
             res = bench_mix(args, w, world, rank, local)
         elif w.get("kind") in ("qkv", "oproj"):
             res = bench_qkv(args, w, world, rank, local)
+        elif w.get("kind") == "layer":
+            res = bench_layer(args, w, world, rank, local)
         elif w.get("kind") == "prefill":
             res = bench_prefill(args, w, world, rank, local)
         elif w.get("kind") == "paging":
