@@ -246,9 +246,12 @@ class KVPool:
         one tensor-core launch; returns the rotated q [n_tokens, Hq, D].
         An fp32 x is split into hi + lo parts of the weights' type, so the
         products keep fp32 accuracy; a 16-bit x must have the weights' type.
-        Whole-width norms (weights of Hq*D / Hkv*D elements) need every head
-        of a token in one place and take the unfused route: the projections
-        as fp32 matmuls, then append_rope."""
+        Pools: f16 / bf16 rows are stored directly, int8 rows quantised as
+        the arena quantises its fp16 pages, FP8 rows staged in fp16 and
+        stored by the FP8 append (one more launch). Whole-width norms
+        (weights of Hq*D / Hkv*D elements) need every head of a token in one
+        place and take the unfused route (16-bit pools): the projections as
+        fp32 matmuls, then append_rope."""
         nt, hidden = x.shape
         wdt = w_q.dtype
         if wdt not in (torch.float16, torch.bfloat16) or w_k.dtype != wdt or w_v.dtype != wdt:
