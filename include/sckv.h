@@ -211,7 +211,7 @@ SCKV_API int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q,
                       int max_blocks, float scale, void* out, int out_dtype,
                       void* stream);
 
-/* Fused attention input for new tokens (16-bit pools): optional RMSNorm of
+/* Fused attention input for new tokens: optional RMSNorm of
  * q and k, rotary position embedding of both at positions start_pos[b] + i,
  * then the K/V append of sckv_append for one layer; the rotated q lands in
  * q_out. Replaces the QK-norm, RoPE and KV-cache concat of
@@ -223,7 +223,10 @@ SCKV_API int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q,
  * heads x head_dim (one norm over the whole projection).
  * inv_freq: device fp32 [head_dim / 2], 1 / theta^(2i / head_dim) as the
  * reference computes it; positions are divided by rope_scaling.
- * head_dim 128, at most 256 heads; other pools: SCKV_ERR_UNSUPPORTED. */
+ * Pools f16 / bf16, and int8 (each K / V row stored as the arena stores its
+ * fp16 pages: the fp16 value quantised per row, native/native_engine.py:
+ * 207-216); FP8 pools: SCKV_ERR_UNSUPPORTED (their page scales span 16
+ * tokens: sckv_append). head_dim 128, at most 256 heads. */
 SCKV_API int sckv_append_rope(sckv_pool* pool, int layer, const void* q_in,
                      void* q_out, int num_q_heads, int q_dtype,
                      int q_out_dtype, const void* k_in, const void* v_in,

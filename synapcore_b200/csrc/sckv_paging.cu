@@ -540,6 +540,25 @@ __device__ __forceinline__ float rope_warp_sum(float v) {
   return v;
 }
 
+// int8 pools: one warp's K or V row (4 values per lane at `dims`) stored as
+// the arena stores its fp16 pages: the fp16 value, quantised per row as
+// quantize_kv_int8_numpy does (native/native_engine.py:207-216).
+__device__ __forceinline__ void store_row_int8(const Geo& g, int layer, int64_t page, int kv, int h, int pos,
+                                               const int (&dims)[4], const float (&y)[4]) {
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = __half2float(__float2half_rn(y[i]));
+  int8_t q[4];
+  __half s;
+  quant_row_int8<4>(x, q, &s);
+  const int64_t off = row_off(g, layer, page, kv, h, pos % SCKV_PAGE_TOKENS);
+  int8_t* d = reinterpret_cast<int8_t*>(g.data);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[off + dims[i]] = q[i];
+  if ((threadIdx.x & 31) == 0)
+    reinterpret_cast<__half*>(g.scales)[int8_scale_idx(g, layer, page, kv, h, pos % SCKV_PAGE_TOKENS)] = s;
+}
+
 __global__ void __launch_bounds__(kRopeWarps * 32) append_rope_kernel(
     Geo g, int layer, const void* q_in, void* q_out, int hq, int q_dtype, int q_out_dtype, const void* k_in,
     const void* v_in, int src_dtype, const __half* q_w, int q_norm_len, const __half* k_w, int k_norm_len,
@@ -611,15 +630,26 @@ __global__ void __launch_bounds__(kRopeWarps * 32) append_rope_kernel(
 #pragma unroll
       for (int i = 0; i < 4; ++i) sckv_store_from_float(q_out, base + dims[i], q_out_dtype, y[i]);
     } else if (page >= 0) {
-      const int64_t off = row_off(g, layer, page, 0, h, pos % SCKV_PAGE_TOKENS);
+      if (g.dtype == SCKV_DTYPE_INT8) {
+        store_row_int8(g, layer, page, 0, h, pos, dims, y);
+      } else {
+        const int64_t off = row_off(g, layer, page, 0, h, pos % SCKV_PAGE_TOKENS);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sckv_store_from_float(g.data, off + dims[i], g.dtype, y[i]);
+        for (int i = 0; i < 4; ++i) sckv_store_from_float(g.data, off + dims[i], g.dtype, y[i]);
+      }
     }
   }
   // v: copied into the page as is
   if (page >= 0) {
     for (int r = warp; r < hk; r += kRopeWarps) {
       const int64_t base = ((int64_t)t * hk + r) * D;
+      if (g.dtype == SCKV_DTYPE_INT8) {
+        float y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) y[i] = sckv_load_as_float(v_in, base + dims[i], src_dtype);
+        store_row_int8(g, layer, page, 1, r, pos, dims, y);
+        continue;
+      }
       const int64_t off = row_off(g, layer, page, 1, r, pos % SCKV_PAGE_TOKENS);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -747,7 +777,10 @@ extern "C" int sckv_append_rope(sckv_pool* p, int layer, const void* q_in, void*
                                 int64_t bt_stride, int max_blocks, void* stream) {
   if (p == nullptr || layer < 0 || layer >= p->num_layers || n_seqs < 0 || n_tokens < 0 || num_q_heads <= 0)
     return SCKV_ERR_INVALID_ARG;
-  if (p->kv_dtype != SCKV_DTYPE_F16 && p->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+  // 16-bit and int8 pools (rows quantised as the arena does); FP8 page
+  // scales span 16 tokens and go through sckv_append
+  if (p->kv_dtype != SCKV_DTYPE_F16 && p->kv_dtype != SCKV_DTYPE_BF16 && p->kv_dtype != SCKV_DTYPE_INT8)
+    return SCKV_ERR_UNSUPPORTED;
   if (p->head_dim != 128 || num_q_heads > kRopeMaxHeads || p->num_kv_heads > kRopeMaxHeads)
     return SCKV_ERR_UNSUPPORTED;
   if (!is_src_dtype(src_dtype) || !is_src_dtype(q_dtype) || !is_src_dtype(q_out_dtype)) return SCKV_ERR_INVALID_ARG;

@@ -250,8 +250,8 @@ class KVPool:
         the arena quantises its fp16 pages, FP8 rows staged in fp16 and
         stored by the FP8 append (one more launch). Whole-width norms
         (weights of Hq*D / Hkv*D elements) need every head of a token in one
-        place and take the unfused route (16-bit pools): the projections as
-        fp32 matmuls, then append_rope."""
+        place and take the unfused route (16-bit and int8 pools): the
+        projections as fp32 matmuls, then append_rope."""
         nt, hidden = x.shape
         wdt = w_q.dtype
         if wdt not in (torch.float16, torch.bfloat16) or w_k.dtype != wdt or w_v.dtype != wdt:

@@ -191,7 +191,8 @@ def test_layer_prompt_batch_matches_oracle(cuda_device):
     cache.pool.raise_on_status()
 
 
-def test_layer_on_int8_pool_matches_oracle(cuda_device):
+@pytest.mark.parametrize("norm", ["head", "full"])
+def test_layer_on_int8_pool_matches_oracle(cuda_device, norm):
     """The arena's int8 mode under a whole layer: new K / V rows quantised by
     the fused projection epilogue (quantize_kv_int8), attention over the
     dequantised pages, against the oracle's composition with the same int8
@@ -207,7 +208,9 @@ def test_layer_on_int8_pool_matches_oracle(cuda_device):
     sd = 1.0 / np.sqrt(hidden)
     W = [(rng.standard_normal(sh) * sd).astype(np.float16)
          for sh in ((hq * D, hidden), (hkv * D, hidden), (hkv * D, hidden), (hidden, hq * D))]
-    NW = [rng.uniform(0.5, 1.5, D).astype(np.float16) for _ in range(2)]
+    # per-head norm weights (fused projection), or whole-width ones (the
+    # unfused route: fp32 projections, then append_rope)
+    NW = [rng.uniform(0.5, 1.5, D if norm == "head" else h * D).astype(np.float16) for h in (hq, hkv)]
     Wd = [_dev(w, dev) for w in W]
     NWd = [_dev(w, dev) for w in NW]
     cache = PagedKVCache(1, hkv, D, max_pages=64, max_seqs=4, max_blocks_per_seq=16, kv_dtype="int8", device=dev)

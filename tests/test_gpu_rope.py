@@ -112,3 +112,45 @@ def test_fused_rope_varlen_batch_matches_oracle(cuda_device, kv_dtype, norm):
         kref = torch.from_numpy(np.ascontiguousarray(kr32)).to(dt).float().numpy()
         assert np.all(np.abs(ks[b] - kref) <= _ulp16(kref, dt)), b
         assert torch.equal(vs[b], torch.from_numpy(v[cu[b]:cu[b + 1]]).to(dt)), b
+
+
+@pytest.mark.parametrize("case", [c["name"] for c in GOLD["qk_rope"]])
+def test_fused_rope_on_int8_pool_quantises_as_the_arena(cuda_device, case):
+    """int8 pools: the rotated K row and the V row are stored as the arena's
+    int8 mode stores fp16 pages (quantize_kv_int8 of the fp16 values). The
+    reference golden K rows are the fp16 cache values; the kernel's fp16 K
+    may sit one ulp away, so codes are compared through their dequantised
+    values, within one quantisation step; V (fp16 input, copied) exactly."""
+    from synapcore_b200.pool import KVPool
+
+    dev = cuda_device
+    g = next(c for c in GOLD["qk_rope"] if c["name"] == case)
+    q, k = ARR[f"rope_{case}_q"], ARR[f"rope_{case}_k"]
+    qw = ARR[f"rope_{case}_qw"] if g["norm"] else None
+    kw = ARR[f"rope_{case}_kw"] if g["norm"] else None
+    v16 = np.random.default_rng(0).standard_normal(k.shape).astype(np.float16)
+    v = v16.astype(np.float32)  # k's dtype; fp16-representable values
+    T, hq, hkv, s0 = g["T"], g["hq"], g["hkv"], g["pos"]
+    mb = (s0 + T + 15) // 16
+    pool = KVPool(1, hkv, 128, mb, "int8", device=dev)
+    bt = np.arange(mb, dtype=np.int32).reshape(1, mb)
+    pool.append_rope(0, torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev),
+                     torch.tensor([0, T], dtype=torch.int32, device=dev),
+                     torch.tensor([s0], dtype=torch.int32, device=dev), torch.from_numpy(bt).to(dev),
+                     torch.from_numpy(ARR[f"rope_{case}_inv_freq"]).to(dev), rope_scaling=g["scaling"],
+                     q_norm_w=None if qw is None else torch.from_numpy(qw).to(dev),
+                     k_norm_w=None if kw is None else torch.from_numpy(kw).to(dev), eps=g["eps"])
+    torch.cuda.synchronize()
+    pool.raise_on_status()
+    pos = np.arange(s0, s0 + T)
+    codes = pool.pool_view()[0].cpu().numpy()[bt[0, pos // 16], :, :, pos % 16]   # [T, 2, H, D]
+    scales = pool.scale_view()[0].cpu().numpy()[bt[0, pos // 16], :, :, pos % 16]  # [T, 2, H]
+    for kv, ref16 in ((0, ARR[f"rope_{case}_k_cache"]), (1, v16)):
+        rq, rs = O.quantize_kv_int8(ref16)
+        got = O.dequantize_kv_int8(codes[:, kv], scales[:, kv][..., None]).astype(np.float32)
+        ref = O.dequantize_kv_int8(rq, rs).astype(np.float32)
+        if kv == 1:
+            np.testing.assert_array_equal(codes[:, kv], rq)
+            np.testing.assert_array_equal(scales[:, kv], rs[..., 0])
+        else:
+            assert np.all(np.abs(got - ref) <= 1.01 * rs.astype(np.float32) + 2e-3 * np.abs(ref))
