@@ -19,7 +19,8 @@ every row of a batch and a prefill call one prompt, in three steps:
 Every pool type works: fp16 / bf16 rows are stored by the fused epilogue,
 int8 rows quantised there as the arena quantises its fp16 pages, and FP8
 rows (whose page scale spans 16 tokens) staged in fp16 and stored by the
-FP8 append launch that follows. Page bookkeeping follows
+FP8 append launch that follows. Whole-width QK-norm weights (OLMoE style)
+take the unfused route, which serves 16-bit and int8 pools. Page bookkeeping follows
 `PagedKVCache`: pages for a prompt are reserved
 when layer 0 runs and the sequence's length advances after the last layer;
 a decode step reserves its token's pages on the device at layer 0.
