@@ -156,7 +156,9 @@ SCKV_API int sckv_copy_pages(sckv_pool* pool, const int32_t* src_ids,
 /* Kernels 3+4 — paged decode attention (split-K), fused FP8 dequant          */
 /* ========================================================================== */
 
-/* Bytes of scratch sckv_decode_attn needs for these sizes (split partials). */
+/* Bytes of scratch sckv_decode_attn needs for these sizes (split partials);
+ * 0 when the chosen split is 1 (an unsplit launch writes its output
+ * directly) or on bad arguments. */
 SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
                                    int num_q_heads, int max_blocks,
                                    int chunk_pages);
@@ -174,7 +176,8 @@ SCKV_API size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
  *               "sequence" of length start+t+1 over the same pages).
  * chunk_pages : pages per split (split-K unit); <= 0 picks one. A fixed
  *               value makes each sequence's result independent of the batch.
- * workspace   : device scratch of sckv_decode_workspace_bytes bytes.
+ * workspace   : device scratch of sckv_decode_workspace_bytes bytes (may be
+ *               NULL when that is 0), 16-byte aligned.
  * Pool dtypes F16, BF16 (bf16 queries for the tensor-core kernel),
  * FP8_E4M3 (per-page-head scale) and INT8 (per-token fp16 scales);
  * num_q_heads / num_kv_heads <= 16. Kernel choice: tensor cores (mma.sync,
@@ -315,10 +318,13 @@ SCKV_API size_t sckv_o_proj_workspace_bytes(const sckv_pool* pool,
  * fixed SCKV_NOALLOC_SCRATCH_BYTES device array inside the library (one per
  * GPU, held until exit) instead of a caller workspace; nothing is allocated
  * per call. chunk_pages <= 0 picks a split that fits; a request whose
- * partials cannot fit (n_seqs * num_q_heads * splits * 520 bytes) returns
- * SCKV_ERR_SCRATCH_LIMIT before launching anything. The first call on a
- * device resolves the array's device address, so make it before any stream
- * capture. All calls share the array: calls that overlap on the GPU race. */
+ * partials cannot fit (n_seqs * num_q_heads * splits * 520 bytes when
+ * splits > 1; an unsplit request needs none) returns SCKV_ERR_SCRATCH_LIMIT
+ * before launching anything, after the same argument checks as
+ * sckv_decode_attn. The first call on a device (and the first after a device
+ * reset, which moves the array) resolves the array's device address, so make
+ * it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. Leaves the caller's current device unchanged. */
 SCKV_API int sckv_decode_attn_noalloc(sckv_pool* pool, int layer, const void* q,
                              int q_dtype, int num_q_heads,
                              const int32_t* block_table, int64_t bt_stride,
@@ -419,8 +425,13 @@ SCKV_API int sckv_kv_lookup(const uint8_t* table, const uint8_t* prefix_hash32,
 /* Replaces synapcore_native_kv_insert (native/synapcore_native.mm:736-780):
  * 1 = stored in an empty or equal slot; 2 = overwrote the probe window's
  * oldest created_at slot, whose hash goes to out_evicted_hash32 (if not
- * NULL) and *evictions is incremented (if not NULL); SCKV_ERR_INVALID_ARG on
- * NULL table/hash. */
+ * NULL) and *evictions is incremented (if not NULL); 3 = the window was full
+ * but no slot had created_at < +inf (all NaN or +inf): the home slot was
+ * overwritten and counted as an eviction, its hash still goes to
+ * out_evicted_hash32, but the reference's Python bridge reports no evicted
+ * hash for this case (native/native_engine.py:1747-1752) while its C++
+ * returns 2 — treat 3 as 2 to follow the C++; SCKV_ERR_INVALID_ARG on NULL
+ * table/hash. */
 SCKV_API int sckv_kv_insert(uint8_t* table, const uint8_t* prefix_hash32,
                    const uint8_t* parent_hash32, uint32_t token_end,
                    double timestamp, uint8_t* out_evicted_hash32,

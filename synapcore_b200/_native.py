@@ -26,6 +26,10 @@ SCKV_ERR_TIMEOUT = -7
 SCKV_ERR_UNSUPPORTED = -8
 SCKV_ERR_SCRATCH_LIMIT = -9
 
+# Size of the fixed per-GPU scratch behind sckv_decode_attn_noalloc
+# (SCKV_NOALLOC_SCRATCH_BYTES in include/sckv.h).
+NOALLOC_SCRATCH_BYTES = 4 << 20
+
 # Element types.
 DTYPE_F16 = 0
 DTYPE_BF16 = 1

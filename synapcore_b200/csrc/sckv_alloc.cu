@@ -527,7 +527,7 @@ int ensure_configured(int device) {
 
 extern "C" int sckv_alloc_reset(sckv_pool* p, void* stream) {
   if (p == nullptr) return SCKV_ERR_INVALID_ARG;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   int64_t blocks = (p->max_pages + 255) / 256;
@@ -541,7 +541,7 @@ extern "C" int sckv_alloc_reset(sckv_pool* p, void* stream) {
 extern "C" int sckv_alloc_pages(sckv_pool* p, int n, int pin, int32_t* out_ids, int32_t* out_victims, void* stream) {
   if (p == nullptr || n < 0 || (n > 0 && out_ids == nullptr)) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   alloc_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), n, pin ? 1 : 0, out_ids, out_victims);
@@ -552,7 +552,7 @@ extern "C" int sckv_alloc_pages(sckv_pool* p, int n, int pin, int32_t* out_ids, 
 extern "C" int sckv_free_pages(sckv_pool* p, const int32_t* ids, int n, void* stream) {
   if (p == nullptr || n < 0 || (n > 0 && ids == nullptr)) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   free_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), ids, n);
@@ -563,7 +563,7 @@ extern "C" int sckv_free_pages(sckv_pool* p, const int32_t* ids, int n, void* st
 extern "C" int sckv_touch_pages(sckv_pool* p, const int32_t* ids, int n, void* stream) {
   if (p == nullptr || n < 0 || (n > 0 && ids == nullptr)) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   cudaStream_t s = as_stream(stream);
   int blocks = (n + 255) / 256;
   if (blocks > p->num_sms * 4) blocks = p->num_sms * 4;
@@ -577,7 +577,7 @@ extern "C" int sckv_touch_pages(sckv_pool* p, const int32_t* ids, int n, void* s
 extern "C" int sckv_pin_pages(sckv_pool* p, const int32_t* ids, int n, int delta, void* stream) {
   if (p == nullptr || n < 0 || (n > 0 && ids == nullptr)) return SCKV_ERR_INVALID_ARG;
   if (n == 0 || delta == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int blocks = (n + 255) / 256;
   if (blocks > p->num_sms * 4) blocks = p->num_sms * 4;
   pin_kernel<<<blocks, 256, 0, as_stream(stream)>>>(view_of(p), ids, n, delta);
@@ -588,7 +588,7 @@ extern "C" int sckv_pin_pages(sckv_pool* p, const int32_t* ids, int n, int delta
 extern "C" int sckv_release_pages(sckv_pool* p, const int32_t* ids, int n, int keep_cached, void* stream) {
   if (p == nullptr || n < 0 || (n > 0 && ids == nullptr)) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   release_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), ids, n, keep_cached ? 1 : 0);
@@ -599,7 +599,7 @@ extern "C" int sckv_release_pages(sckv_pool* p, const int32_t* ids, int n, int k
 extern "C" int sckv_evict_lru(sckv_pool* p, int n, int32_t* out_ids, void* stream) {
   if (p == nullptr || n < 0) return SCKV_ERR_INVALID_ARG;
   if (n == 0) return SCKV_OK;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   evict_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), n, out_ids);
@@ -612,7 +612,7 @@ extern "C" int sckv_reserve_decode(sckv_pool* p, int32_t* bt, int64_t stride, in
   if (p == nullptr || n_seqs < 0 || max_blocks <= 0 || stride < max_blocks) return SCKV_ERR_INVALID_ARG;
   if (n_seqs == 0) return SCKV_OK;
   if (bt == nullptr || ctx_lens == nullptr) return SCKV_ERR_INVALID_ARG;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
   reserve_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), bt, stride, max_blocks, ctx_lens,
@@ -623,7 +623,7 @@ extern "C" int sckv_reserve_decode(sckv_pool* p, int32_t* bt, int64_t stride, in
 
 extern "C" int sckv_alloc_state(const sckv_pool* p, int64_t out[5], void* stream) {
   if (p == nullptr || out == nullptr) return SCKV_ERR_INVALID_ARG;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   cudaStream_t s = as_stream(stream);
   SCKV_CUDA_CHECK(cudaMemcpyAsync(out, p->ctl, 5 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
   SCKV_CUDA_CHECK(cudaStreamSynchronize(s));

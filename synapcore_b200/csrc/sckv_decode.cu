@@ -24,9 +24,12 @@
 //    records SCKV_ERR_TIMEOUT, stops issuing, drains copies in flight and
 //    returns. Invalid page ids are recorded (SCKV_ERR_BOUNDS) and page 0 is
 //    read in their place so the ring stays consistent.
+#include <cuda.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+
+#include <mutex>
 
 #include "sckv_decode_common.cuh"
 
@@ -521,14 +524,19 @@ extern "C" size_t sckv_decode_workspace_bytes(const sckv_pool* pool, int n_seqs,
   if (pool == nullptr || n_seqs <= 0 || num_q_heads <= 0 || max_blocks <= 0) return 0;
   if (chunk_pages <= 0) chunk_pages = pick_chunk(pool, n_seqs, max_blocks);
   const int64_t splits = (max_blocks + chunk_pages - 1) / chunk_pages;
+  // an unsplit launch writes its output directly and never touches partials
+  if (splits <= 1) return 0;
   const int64_t slots = (int64_t)n_seqs * num_q_heads * splits;
   return (size_t)(slots * (kHD + 2) * sizeof(float));
 }
 
-extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
-                                const int32_t* block_table, int64_t bt_stride, int max_blocks,
-                                const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
-                                void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+namespace {
+
+// Argument checks shared by both decode entry points, run before anything
+// else so a bad call reports INVALID_ARG / UNSUPPORTED whatever its size.
+int validate_decode_args(const sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                         const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
+                         int n_seqs, const void* out, int out_dtype) {
   if (pool == nullptr) return SCKV_ERR_INVALID_ARG;
   if (pool->head_dim != kHD) return SCKV_ERR_UNSUPPORTED;
   if (layer < 0 || layer >= pool->num_layers) return SCKV_ERR_INVALID_ARG;
@@ -539,9 +547,22 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
   if (q_dtype != SCKV_DTYPE_F16 && q_dtype != SCKV_DTYPE_BF16 && q_dtype != SCKV_DTYPE_F32) return SCKV_ERR_INVALID_ARG;
   if (out_dtype != SCKV_DTYPE_F16 && out_dtype != SCKV_DTYPE_BF16 && out_dtype != SCKV_DTYPE_F32)
     return SCKV_ERR_INVALID_ARG;
+  if (pool->device < 0) return SCKV_ERR_INVALID_ARG;
+  return SCKV_OK;
+}
+
+}  // namespace
+
+extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                                const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                                const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
+                                void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+  const int vrc = validate_decode_args(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks,
+                                      ctx_lens, n_seqs, out, out_dtype);
+  if (vrc != SCKV_OK) return vrc;
   if (chunk_pages <= 0) chunk_pages = pick_chunk(pool, n_seqs, max_blocks);
   const size_t need = sckv_decode_workspace_bytes(pool, n_seqs, num_q_heads, max_blocks, chunk_pages);
-  if (workspace == nullptr || workspace_bytes < need) return SCKV_ERR_INVALID_ARG;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return SCKV_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(workspace) & 15) return SCKV_ERR_ALIGNMENT;
 
   DecodeParams prm{};
@@ -569,7 +590,7 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
   prm.scale_log2 = scale * 1.4426950408889634f;
   const int G = num_q_heads / pool->num_kv_heads;
   cudaStream_t s = as_stream(stream);
-  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  SCKV_DEVICE_GUARD(pool->device);
   if (use_tensor_core_path(pool, G, q_dtype)) {
     const int rc = launch_decode_mma(pool, G, prm, s);
     if (rc != SCKV_ERR_UNSUPPORTED) return rc;
@@ -596,15 +617,20 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
 // loaded on that GPU and held until the process exits.
 //
 // The array's name is only a host-side stand-in for the device symbol, so the
-// host resolves its device address once per device (with that device
-// current) through cudaGetSymbolAddress and passes the address down; device
-// code could name the array directly. The first call on a device performs
-// that set-up, so make it before capturing any stream into a CUDA graph.
+// host resolves its device address (with that device current) through
+// cudaGetSymbolAddress and passes the address down; device code could name
+// the array directly. The first call on a device performs that set-up, so
+// make it before capturing any stream into a CUDA graph. A device reset, or
+// any other teardown and re-creation of the device's primary context, loads
+// the module again and moves the array; the next call sees the new context's
+// id and resolves the address again (so, after a reset, again make one call
+// before any capture).
 //
 // Every call reuses the same array and it keeps the last call's contents.
 // Nothing in it needs to start at zero: each split partial a call reads is
 // written earlier in the same call. Calls whose work overlaps on the GPU (two
-// streams, or two host threads) race on the array; serialise them.
+// streams, or two host threads) race on the array; serialise them. The
+// host-side set-up itself is safe to enter from several threads at once.
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -613,7 +639,42 @@ static_assert(kNoAllocScratchBytes % 256 == 0, "scratch size must keep 256-byte 
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-void* g_noalloc_scratch_addr[64] = {};
+// Per device: the array's device address and the id of the context it was
+// resolved in.
+struct NoAllocScratchSlot {
+  std::mutex mu;
+  void* addr = nullptr;
+  unsigned long long ctx_id = 0;
+};
+NoAllocScratchSlot g_noalloc_slots[64];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context; 0 when the driver cannot
+// say (the address is then resolved on every call).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 }  // namespace
 
@@ -621,13 +682,15 @@ extern "C" int sckv_decode_attn_noalloc(sckv_pool* pool, int layer, const void* 
                                         const int32_t* block_table, int64_t bt_stride, int max_blocks,
                                         const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
                                         int chunk_pages, void* stream) {
-  if (pool == nullptr) return SCKV_ERR_INVALID_ARG;
-  if (n_seqs <= 0 || num_q_heads <= 0 || max_blocks <= 0) return SCKV_ERR_INVALID_ARG;
+  const int vrc = validate_decode_args(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks,
+                                      ctx_lens, n_seqs, out, out_dtype);
+  if (vrc != SCKV_OK) return vrc;
   const int dev = pool->device;
-  if (dev < 0 || dev >= 64) return SCKV_ERR_INVALID_ARG;
+  if (dev >= 64) return SCKV_ERR_INVALID_ARG;
   int chunk = chunk_pages;
   if (chunk <= 0) {
-    // Default split, widened until the partials fit the fixed buffer.
+    // Default split, widened until the partials fit the fixed buffer (an
+    // unsplit launch needs none).
     chunk = pick_chunk(pool, n_seqs, max_blocks);
     while (chunk < max_blocks &&
            sckv_decode_workspace_bytes(pool, n_seqs, num_q_heads, max_blocks, chunk) > kNoAllocScratchBytes)
@@ -635,12 +698,20 @@ extern "C" int sckv_decode_attn_noalloc(sckv_pool* pool, int layer, const void* 
   }
   if (sckv_decode_workspace_bytes(pool, n_seqs, num_q_heads, max_blocks, chunk) > kNoAllocScratchBytes)
     return SCKV_ERR_SCRATCH_LIMIT;
-  if (g_noalloc_scratch_addr[dev] == nullptr) {
-    SCKV_CUDA_CHECK(cudaSetDevice(dev));
-    void* addr = nullptr;
-    SCKV_CUDA_CHECK(cudaGetSymbolAddress(&addr, g_noalloc_scratch));
-    g_noalloc_scratch_addr[dev] = addr;
+  SCKV_DEVICE_GUARD(dev);
+  void* scratch = nullptr;
+  {
+    NoAllocScratchSlot& slot = g_noalloc_slots[dev];
+    std::lock_guard<std::mutex> lock(slot.mu);
+    const unsigned long long id = current_context_id();
+    if (slot.addr == nullptr || id == 0 || id != slot.ctx_id) {
+      void* addr = nullptr;
+      SCKV_CUDA_CHECK(cudaGetSymbolAddress(&addr, g_noalloc_scratch));
+      slot.addr = addr;
+      slot.ctx_id = id;
+    }
+    scratch = slot.addr;
   }
   return sckv_decode_attn(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens, n_seqs,
-                          scale, out, out_dtype, g_noalloc_scratch_addr[dev], kNoAllocScratchBytes, chunk, stream);
+                          scale, out, out_dtype, scratch, kNoAllocScratchBytes, chunk, stream);
 }

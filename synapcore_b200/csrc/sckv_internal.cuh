@@ -263,6 +263,35 @@ inline int sckv_record_error(const char* file, int line, const char* what, const
     if (_e != cudaSuccess) return sckv_record_error(__FILE__, __LINE__, #expr, cudaGetErrorName(_e)); \
   } while (0)
 
+// Makes a pool's device current for the rest of the enclosing scope and puts
+// the calling thread's previous device back on exit, so no entry point leaves
+// the caller on another GPU.
+class SckvDeviceGuard {
+ public:
+  SckvDeviceGuard() = default;
+  SckvDeviceGuard(const SckvDeviceGuard&) = delete;
+  SckvDeviceGuard& operator=(const SckvDeviceGuard&) = delete;
+  cudaError_t enter(int dev) {
+    cudaError_t e = cudaGetDevice(&prev_);
+    if (e != cudaSuccess) return e;
+    if (prev_ == dev) return cudaSuccess;
+    e = cudaSetDevice(dev);
+    if (e == cudaSuccess) switched_ = true;
+    return e;
+  }
+  ~SckvDeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0;
+  bool switched_ = false;
+};
+
+#define SCKV_DEVICE_GUARD(dev)           \
+  SckvDeviceGuard _sckv_device_guard;    \
+  SCKV_CUDA_CHECK(_sckv_device_guard.enter(dev))
+
 // Kernels launched by this library in this process (every launch site is
 // followed by exactly one SCKV_LAUNCH_CHECK, which counts it).
 inline std::atomic<unsigned long long>& sckv_launch_counter() {

@@ -9,7 +9,9 @@
 // Insert semantics: synapcore_native_kv_insert (:736-780) — first empty or
 // equal slot in the window is (over)written; otherwise the slot with the
 // smallest created_at in the window (first such on ties, home slot if none is
-// finite) is overwritten and its hash reported.
+// below +inf) is overwritten and its hash reported; when none was below +inf
+// the return code is 3 instead of 2, because the reference's Python bridge
+// (native/native_engine.py:1747-1752) reports no hash for that case.
 #include <cstdint>
 #include <cstring>
 #include <limits>
@@ -76,6 +78,7 @@ extern "C" int sckv_kv_insert(uint8_t* table, const uint8_t* prefix_hash32, cons
   const uint32_t slot = home_slot(prefix_hash32);
   uint32_t oldest = slot;
   double oldest_ts = std::numeric_limits<double>::infinity();
+  bool found_older = false;  // some slot had created_at < +inf
   for (uint32_t probe = 0; probe < kProbes; ++probe) {
     const uint32_t idx = (slot + probe) & (kSlots - 1);
     uint8_t* s = slot_ptr(table, idx);
@@ -87,11 +90,14 @@ extern "C" int sckv_kv_insert(uint8_t* table, const uint8_t* prefix_hash32, cons
     if (ts < oldest_ts) {
       oldest_ts = ts;
       oldest = idx;
+      found_older = true;
     }
   }
   uint8_t* victim = slot_ptr(table, oldest);
   if (out_evicted_hash32) std::memcpy(out_evicted_hash32, victim, 32);
   write_slot(victim, prefix_hash32, parent_hash32, token_end, timestamp);
   if (evictions) ++*evictions;
-  return 2;
+  // No comparable timestamp in the window: the home slot is overwritten
+  // either way; the Python bridge then reports no evicted hash.
+  return found_older ? 2 : 3;
 }

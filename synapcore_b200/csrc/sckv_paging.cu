@@ -673,7 +673,7 @@ extern "C" int sckv_append(sckv_pool* p, int layer0, int n_layers, const void* k
   if ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) return SCKV_ERR_ALIGNMENT;
   Geo g = geo_of(p);
   cudaStream_t s = as_stream(stream);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   if (p->kv_dtype == SCKV_DTYPE_F16 || p->kv_dtype == SCKV_DTYPE_BF16) {
     // one block per new token
     append16_kernel<<<n_tokens, 256, 0, s>>>(g, layer0, n_layers, k_new, v_new, src_dtype, n_seqs,
@@ -703,7 +703,7 @@ extern "C" int sckv_write_pages(sckv_pool* p, const int32_t* ids, int n, const v
   if ((reinterpret_cast<uintptr_t>(k_src) | reinterpret_cast<uintptr_t>(v_src)) & 15) return SCKV_ERR_ALIGNMENT;
   Geo g = geo_of(p);
   cudaStream_t s = as_stream(stream);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   if (p->kv_dtype == SCKV_DTYPE_F16 || p->kv_dtype == SCKV_DTYPE_BF16) {
     int64_t work = (int64_t)n * 2 * p->num_layers * p->num_kv_heads * SCKV_PAGE_TOKENS * (p->head_dim / 8);
     write_pages16_kernel<<<grid_for(p, work, 256), 256, 0, s>>>(g, ids, n, k_src, v_src, src_dtype);
@@ -728,7 +728,7 @@ extern "C" int sckv_write_pages_quantized(sckv_pool* p, const int32_t* ids, int 
     return SCKV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(kq) | reinterpret_cast<uintptr_t>(vq)) & 15) return SCKV_ERR_ALIGNMENT;
   Geo g = geo_of(p);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   int64_t work = (int64_t)n * 2 * p->num_layers * p->num_kv_heads * SCKV_PAGE_TOKENS * (p->head_dim / 16);
   write_pages_quantized_kernel<<<grid_for(p, work, 256), 256, 0, as_stream(stream)>>>(
       g, ids, n, kq, reinterpret_cast<const __half*>(ks), vq, reinterpret_cast<const __half*>(vs));
@@ -745,7 +745,7 @@ extern "C" int sckv_gather(sckv_pool* p, int layer0, int n_layers, const int32_t
   if (!ids || !out_k || !out_v) return SCKV_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(out_k) | reinterpret_cast<uintptr_t>(out_v)) & 15) return SCKV_ERR_ALIGNMENT;
   Geo g = geo_of(p);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   // one block per (listed page holding gathered tokens, layer)
   const int64_t blocks = (int64_t)((n_tokens + SCKV_PAGE_TOKENS - 1) / SCKV_PAGE_TOKENS) * n_layers;
   if (blocks > INT32_MAX) return SCKV_ERR_INVALID_ARG;
@@ -760,7 +760,7 @@ extern "C" int sckv_copy_pages(sckv_pool* p, const int32_t* src_ids, const int32
   if (n == 0) return SCKV_OK;
   if (!src_ids || !dst_ids) return SCKV_ERR_INVALID_ARG;
   Geo g = geo_of(p);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   // one block per (page pair, layer)
   const int64_t blocks = (int64_t)n * p->num_layers;
   if (blocks > INT32_MAX) return SCKV_ERR_INVALID_ARG;
@@ -794,7 +794,7 @@ extern "C" int sckv_append_rope(sckv_pool* p, int layer, const void* q_in, void*
       bt_stride < max_blocks || max_blocks <= 0)
     return SCKV_ERR_INVALID_ARG;
   Geo g = geo_of(p);
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   append_rope_kernel<<<n_tokens, kRopeWarps * 32, 0, as_stream(stream)>>>(
       g, layer, q_in, q_out, num_q_heads, q_dtype, q_out_dtype, k_in, v_in, src_dtype,
       reinterpret_cast<const __half*>(q_norm_w), q_norm_len, reinterpret_cast<const __half*>(k_norm_w), k_norm_len,

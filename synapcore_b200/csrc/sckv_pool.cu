@@ -91,7 +91,7 @@ extern "C" int sckv_pool_create(int L, int H, int D, int T, int64_t P, int dtype
   *out = nullptr;
   int rc = validate_geometry(L, H, D, T, P, dtype);
   if (rc != SCKV_OK) return rc;
-  SCKV_CUDA_CHECK(cudaSetDevice(device));
+  SCKV_DEVICE_GUARD(device);
   size_t data_b = 0, scale_b = 0, alloc_b = 0;
   sckv_pool_required_bytes(L, H, D, T, P, dtype, &data_b, &scale_b, &alloc_b);
   sckv_pool* p = new (std::nothrow) sckv_pool{};
@@ -140,7 +140,8 @@ extern "C" int sckv_pool_wrap(int L, int H, int D, int T, int64_t P, int dtype, 
 extern "C" void sckv_pool_destroy(sckv_pool* p) {
   if (p == nullptr) return;
   if (p->owns_memory) {
-    cudaSetDevice(p->device);
+    SckvDeviceGuard guard;
+    guard.enter(p->device);
     if (p->data) cudaFree(p->data);
     if (p->scales) cudaFree(p->scales);
     if (p->alloc_state) cudaFree(p->alloc_state);
@@ -191,7 +192,7 @@ __global__ void selftest_wait_kernel(int32_t* status, uint64_t limit_ns) {
 
 extern "C" int sckv_selftest_wait_timeout(sckv_pool* p, unsigned limit_us, void* stream) {
   if (p == nullptr || limit_us == 0 || limit_us > 2000000u) return SCKV_ERR_INVALID_ARG;
-  SCKV_CUDA_CHECK(cudaSetDevice(p->device));
+  SCKV_DEVICE_GUARD(p->device);
   selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(p->status, (uint64_t)limit_us * 1000ull);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;

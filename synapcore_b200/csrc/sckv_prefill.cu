@@ -505,7 +505,7 @@ extern "C" int sckv_prefill_attn(sckv_pool* pool, int layer, const void* q, int 
   // SCKV_PREFILL_KERNEL=mma asks for this one (f16 / bf16 / FP8)
   const char* env = getenv("SCKV_PREFILL_KERNEL");
   const bool forced = env != nullptr && strcmp(env, "mma") == 0;
-  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  SCKV_DEVICE_GUARD(pool->device);
   if (!forced) {
     const int rc = launch_prefill_tc(pool, layer, q, q_dtype, num_q_heads, n_seqs, n_tokens, cu_q, start_pos,
                                      block_table, bt_stride, max_blocks, scale, out, out_dtype, lg,

@@ -875,7 +875,7 @@ extern "C" int sckv_qkv_append(sckv_pool* pool, int layer, const void* x, const 
   if (rc != SCKV_OK) return rc;
 
   cudaStream_t s = as_stream(stream);
-  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  SCKV_DEVICE_GUARD(pool->device);
   float2* cs = reinterpret_cast<float2*>(workspace);
   if (k_splits == 1) {
     // the fused epilogue reads a per-token cos / sin table (split over the
@@ -973,7 +973,7 @@ extern "C" int sckv_o_proj(sckv_pool* pool, const void* x, const void* x_lo, int
   if (rc != SCKV_OK) return rc;
   maps[3] = maps[2];  // no k / v tiles in a plain projection
   maps[4] = maps[2];
-  SCKV_CUDA_CHECK(cudaSetDevice(pool->device));
+  SCKV_DEVICE_GUARD(pool->device);
 
   QkvParams prm{};
   prm.q_out = out;

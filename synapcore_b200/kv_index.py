@@ -63,9 +63,12 @@ class KVPrefixIndex:
             return bool(self._lib.sckv_kv_lookup(self._ptr, h, None))
 
     def kv_lookup_token_end(self, prefix_hash_bytes: bytes) -> Optional[int]:
+        h = bytes(prefix_hash_bytes)
+        if len(h) != 32:
+            return None
         out = ctypes.c_uint32(0)
         with self.idx_lock:
-            if self._lib.sckv_kv_lookup(self._ptr, bytes(prefix_hash_bytes), ctypes.byref(out)):
+            if self._lib.sckv_kv_lookup(self._ptr, h, ctypes.byref(out)):
                 return int(out.value)
         return None
 
@@ -84,6 +87,11 @@ class KVPrefixIndex:
             return None
         if rc == 2:
             return ev.raw.hex()
+        if rc == 3:
+            # window full with no timestamp below +inf (e.g. all NaN): the
+            # home slot was overwritten, and the reference bridge names no
+            # evicted hash (native/native_engine.py:1747-1752)
+            return None
         N.check(rc, "sckv_kv_insert")
         return None
 

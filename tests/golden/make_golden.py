@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Generate golden fixtures by running the reference's own Python code.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
+    (or set SCKV_REFERENCE_DIR)
 
 Imports the reference's PagedKVArena, NativeKVPrefixCache, int8 KV
 quantisation, prefix-chain hash, KV hash-table twin, ModularAttentionEngine
@@ -21,6 +22,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import shutil
 import struct
 import sys
@@ -229,6 +231,86 @@ def kv_table_long_context(ne):
     }
 
 
+def kv_table_unordered_timestamps(ne):
+    """Probe windows whose created_at values compare false (NaN) or never
+    below +inf: the Python twin overwrites the home slot, counts an eviction
+    and names no evicted hash (native/native_engine.py:1741-1752)."""
+    out = {}
+    for name, ts_fill in (("nan", float("nan")), ("inf", float("inf")), ("mixed", None)):
+        b = stand_in_bridge(ne)
+        rets = []
+        for c in range(64):
+            h = struct.pack("<I", 300 | ((c + 1) << 10)) + bytes([c]) + b"\x22" * 27
+            ts = ts_fill if ts_fill is not None else (float("nan") if c % 3 else float("inf"))
+            rets.append(b.kv_insert(h, b"\x00" * 32, (c + 1) * 16, ts))
+        for c in range(3):
+            h = struct.pack("<I", 300 | ((c + 100) << 10)) + b"\x33" * 28
+            rets.append(b.kv_insert(h, b"\x01" * 32, 7 + c, 50.0 + c))
+        out[name] = {
+            "returns": rets,
+            "evictions": b.kv_evictions_issued,
+            "table_sha256": hashlib.sha256(bytes(b.idx_mmap[ne.OFFSET_KV_HASH_TBL:])).hexdigest(),
+        }
+    return out
+
+
+def arena_alloc_streams(ne, arrays):
+    """PagedKVArena's page-id bookkeeping (native/native_engine.py:297-337)
+    over long seeded operation streams: writes of new keys (FIFO free list,
+    then LRU victims), rewrites of live keys (a touch), lookups that hit and
+    miss (the clock ticks on both), and evict_prefix_hash of live and absent
+    keys. Every returned page id / bool is recorded with the final counters,
+    free-list order and clocks, so a page-id-keyed allocator can be replayed
+    against it op for op."""
+    streams = []
+    for seed, max_pages, n_ops in ((11, 40, 1500), (12, 97, 2500), (13, 300, 4000)):
+        rng = np.random.default_rng(seed)
+        arena = ne.PagedKVArena(max_pages=max_pages, num_layers=1, num_kv_heads=1, head_dim=8, quant_mode="fp16")
+        page = np.zeros((1, 1, 1, 16, 8), np.float16)
+        next_key = 0
+        seen = []
+        ops = []
+        for _ in range(n_ops):
+            r = rng.random()
+            live = [int(h, 16) for h in arena.page_table.keys()]
+            if r < 0.45 or not seen:
+                if rng.random() < 0.1 and seen:
+                    key = seen[int(rng.integers(0, len(seen)))]  # live or evicted earlier
+                else:
+                    key = next_key
+                    next_key += 1
+                    seen.append(key)
+                ops.append((0, key, int(arena.write_page_fp16(f"{key:064x}", page, page))))
+            elif r < 0.8:
+                if rng.random() < 0.6 and live:
+                    key = live[int(rng.integers(0, len(live)))]
+                elif rng.random() < 0.5:
+                    key = seen[int(rng.integers(0, len(seen)))]
+                else:
+                    key = 10**9 + int(rng.integers(0, 10**6))  # never written
+                pid = arena.lookup_page_id(f"{key:064x}")
+                ops.append((1, key, -1 if pid is None else int(pid)))
+            else:
+                if rng.random() < 0.8 and live:
+                    key = live[int(rng.integers(0, len(live)))]
+                else:
+                    key = seen[int(rng.integers(0, len(seen)))]
+                ops.append((2, key, int(bool(arena.evict_prefix_hash(f"{key:064x}")))))
+        arrays[f"arena_stream_{seed}_ops"] = np.asarray(ops, np.int64)
+        streams.append({
+            "seed": seed,
+            "max_pages": max_pages,
+            "ops": f"arena_stream_{seed}_ops",
+            "step_clock": arena.step_clock,
+            "page_hits": arena.page_hits,
+            "page_misses": arena.page_misses,
+            "page_evictions": arena.page_evictions,
+            "free_pages": list(map(int, arena.free_pages)),
+            "last_used_by_page": {str(arena.page_table[h]): int(c) for h, c in arena.page_last_used.items()},
+        })
+    return streams
+
+
 def sdpa_cases(ad, arrays):
     """Decode SDPA through ModularAttentionEngine.forward_numpy
     (models/adapters.py:1148-1231) with identity q/o projections, zero k/v
@@ -423,8 +505,11 @@ def scheduler_runs(ne, ad, arrays):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SCKV_REFERENCE_DIR"),
+                    help="path of the reference checkout (default: $SCKV_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or SCKV_REFERENCE_DIR) is required")
     sys.path.insert(0, args.reference)
     from native import native_engine as ne  # noqa: E402
     from models import adapters as ad  # noqa: E402
@@ -437,6 +522,8 @@ def main():
         "prefix_cache_t4": prefix_cache_t4(ne),
         "kv_table_kat": kv_table_kat(ne),
         "kv_table_long_context": kv_table_long_context(ne),
+        "kv_table_unordered_timestamps": kv_table_unordered_timestamps(ne),
+        "arena_alloc_streams": arena_alloc_streams(ne, arrays),
         "sdpa": sdpa_cases(ad, arrays),
         "scheduler": scheduler_runs(ne, ad, arrays),
         "qk_rope": qk_rope_cases(ad, arrays),

@@ -102,3 +102,35 @@ def test_bad_hash_length_rejected():
     with pytest.raises(ValueError):
         idx.kv_insert(b"\x00" * 31, b"\x00" * 32, 1, 0.0)
     assert idx.kv_lookup(b"short") is False
+
+
+def test_short_hash_token_end_lookup_is_a_miss():
+    idx = KVPrefixIndex()
+    h = hashlib.sha256(b"x").digest()
+    assert idx.kv_insert(h, b"\x00" * 32, 16, 1.0) is None
+    assert idx.kv_lookup_token_end(h) == 16
+    assert idx.kv_lookup_token_end(h[:4]) is None
+    assert idx.kv_lookup_token_end(b"") is None
+
+
+@pytest.mark.parametrize("case", ["nan", "inf", "mixed"])
+def test_window_without_comparable_timestamps_matches_reference(case):
+    """A full probe window whose created_at values are all NaN / +inf: the
+    reference bridge overwrites the home slot, counts the eviction and names
+    no evicted hash; later inserts with finite stamps evict normally."""
+    g = GOLD["kv_table_unordered_timestamps"][case]
+    idx, twin = KVPrefixIndex(), KVTableOracle()
+    rets = []
+    for c in range(64):
+        h = struct.pack("<I", 300 | ((c + 1) << 10)) + bytes([c]) + b"\x22" * 27
+        ts = {"nan": float("nan"), "inf": float("inf")}.get(case, float("nan") if c % 3 else float("inf"))
+        rets.append(idx.kv_insert(h, b"\x00" * 32, (c + 1) * 16, ts))
+        assert twin.insert(h, b"\x00" * 32, (c + 1) * 16, ts) == rets[-1]
+    for c in range(3):
+        h = struct.pack("<I", 300 | ((c + 100) << 10)) + b"\x33" * 28
+        rets.append(idx.kv_insert(h, b"\x01" * 32, 7 + c, 50.0 + c))
+        assert twin.insert(h, b"\x01" * 32, 7 + c, 50.0 + c) == rets[-1]
+    assert rets == g["returns"]
+    assert idx.kv_evictions_issued == g["evictions"] == twin.evictions
+    assert hashlib.sha256(idx.table_bytes()).hexdigest() == g["table_sha256"]
+    assert idx.table_bytes() == bytes(twin.table)

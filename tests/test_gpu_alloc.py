@@ -168,3 +168,46 @@ def test_reserve_decode_bounds_error_changes_nothing(cuda_device):
     assert ctx.cpu().tolist() == [32, 3] and bt.cpu().tolist() == [[-1, -1], [-1, -1]]
     pool.clear_status()
     pool.close()
+
+
+class _DeviceAllocator:
+    """The device allocator (kernel 5) behind the replay interface."""
+
+    def __init__(self, pool):
+        self.pool = pool
+
+    def alloc(self, n):
+        ids, vic = self.pool.alloc_pages(n)
+        return ids.cpu().tolist(), vic.cpu().tolist()
+
+    def touch(self, ids):
+        self.pool.touch_pages(torch.tensor(ids, dtype=torch.int32))
+
+    def free(self, ids):
+        self.pool.free_pages(torch.tensor(ids, dtype=torch.int32))
+
+
+@pytest.mark.parametrize("idx", [0, 1, 2])
+@pytest.mark.parametrize("batch", [False, True])
+def test_device_allocator_replays_reference_arena_streams(cuda_device, idx, batch):
+    """Kernel 5 reproduces, page id for page id, the reference PagedKVArena's
+    allocations, LRU victims, clock, eviction count, free-list order and LRU
+    order over long operation streams recorded from the reference itself
+    (tests/golden arena_alloc_streams), issued one operation per call and in
+    batched calls (n allocations in one launch = n reference allocations)."""
+    import json
+    from pathlib import Path
+
+    from arena_replay import check_final_state, replay
+
+    gold_dir = Path(__file__).resolve().parent / "golden"
+    st = json.loads((gold_dir / "golden.json").read_text())["arena_alloc_streams"][idx]
+    ops = np.load(gold_dir / "golden_arrays.npz")[st["ops"]]
+    pool = _pool(cuda_device, st["max_pages"])
+    dev = _DeviceAllocator(pool)
+    counters = replay(ops, dev, batch=batch)
+    state = pool.alloc_state()
+    assert state["free"] == len(st["free_pages"])
+    assert pool.status()[0] == 0
+    check_final_state(dev, st, counters, state["clock"], state["evictions"])
+    pool.close()

@@ -6,7 +6,9 @@ only holds the pool handle): its split-K partials live in a fixed device
 array inside the library instead of a caller-provided workspace. This test
 checks it against the allocating entry point, sckv_decode_attn, on two calls
 in a row (the shared array keeps the previous call's contents, which must
-not matter), and that an oversized request is refused before any launch.
+not matter), that an oversized request is refused before any launch (after
+the usual argument checks), and that an unsplit request, which needs no
+scratch, is never refused.
 It lives in its own file, collected last, and builds all of its own state so
 it passes alone in a fresh process as well as after the other tests.
 """
@@ -103,7 +105,53 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
     q = torch.zeros((B, hq, 128), dtype=torch.float16, device=dev)
     out = torch.zeros((B, hq, 128), dtype=torch.float32, device=dev)
     assert _call_noalloc(lib, pool, 0, q, bt, max_blocks, ctx, out, 1) == N.SCKV_ERR_SCRATCH_LIMIT
+    # an invalid call is reported as such even when it is also oversized, so
+    # a caller that falls back to the allocating entry point on the scratch
+    # limit is not misled
+    assert _call_noalloc(lib, pool, 1, q, bt, max_blocks, ctx, out, 1) == N.SCKV_ERR_INVALID_ARG
     torch.cuda.synchronize()
     assert pool.status()[0] == N.SCKV_OK
     assert N.status_string(N.SCKV_ERR_SCRATCH_LIMIT) == "request exceeds the fixed no-allocation scratch"
+    pool.close()
+
+
+def test_noalloc_unsplit_large_batch_needs_no_scratch(cuda_device):
+    """An unsplit launch writes its output directly and uses none of the
+    fixed array, so a batch whose partials would not fit (512 sequences x 32
+    query heads, GQA 32/8) still runs at one split, and its result matches
+    the oracle's SDPA over the same pages."""
+    from oracle.kv_oracle import sdpa_decode
+    from synapcore_b200 import _native as N
+
+    lib = N.load()
+    dev = cuda_device
+    pool, rng = _pool_with_pages(dev, layers=1, hkv=8, pages=64, seed=7)
+    hq, B, max_blocks = 32, 512, 4
+    bt_np = np.stack([rng.choice(64, size=max_blocks, replace=False) for _ in range(B)]).astype(np.int32)
+    ctx_np = rng.integers(1, max_blocks * 16 + 1, size=B).astype(np.int32)
+    bt = torch.from_numpy(bt_np).to(dev)
+    ctx = torch.from_numpy(ctx_np).to(dev)
+    q = torch.from_numpy(rng.standard_normal((B, hq, 128)).astype(np.float16)).to(dev)
+    # 512 * 32 * 2 splits * 520 bytes = 17 MB of partials: refused when split
+    assert lib.sckv_decode_workspace_bytes(pool.handle, B, hq, max_blocks, 2) > N.NOALLOC_SCRATCH_BYTES
+    assert _call_noalloc(lib, pool, 0, q, bt, max_blocks, ctx, torch.empty((B, hq, 128), dtype=torch.float32,
+                                                                          device=dev), 2) == N.SCKV_ERR_SCRATCH_LIMIT
+    assert lib.sckv_decode_workspace_bytes(pool.handle, B, hq, max_blocks, max_blocks) == 0
+    k_all = pool.pool_view()[0, :, 0].float().cpu().numpy()  # [pages, hkv, 16, 128]
+    v_all = pool.pool_view()[0, :, 1].float().cpu().numpy()
+    q_np = q.float().cpu().numpy()
+    for chunk in (max_blocks, 0):  # explicit single split, and the default pick widened to fit
+        for _ in range(2):
+            out = torch.full((B, hq, 128), float("nan"), dtype=torch.float32, device=dev)
+            assert _call_noalloc(lib, pool, 0, q, bt, max_blocks, ctx, out, chunk) == N.SCKV_OK
+            torch.cuda.synchronize()
+            assert pool.status()[0] == N.SCKV_OK
+            got = out.cpu().numpy()
+            for b in range(0, B, 37):
+                n = int(ctx_np[b])
+                pages = bt_np[b, : (n + 15) // 16]
+                kk = np.concatenate([k_all[p] for p in pages], axis=1)[:, :n]
+                vv = np.concatenate([v_all[p] for p in pages], axis=1)[:, :n]
+                exp = sdpa_decode(q_np[b], kk, vv)
+                assert _rel_err(got[b], exp) <= TOL
     pool.close()
