@@ -314,19 +314,23 @@ def seq_contexts(w, rank: int) -> np.ndarray:
     return np.full(w["batch"], w["ctx"], np.int64)
 
 
-def build_state(w, rank: int, grow_steps: int = 0):
+def build_state(w, rank: int, grow_steps: int = 0, ctx0=None):
     """Pool, block tables and per-layer inputs of one rank.
 
     Fixed-context workloads: the step's new token rewrites slot ctx-1, so
     every step moves the same bytes. Growing workloads (`grow`): the new
     token goes to slot ctx and contexts advance by one per step; block tables
-    have room for `grow_steps` more tokens and `reset()` rewinds them."""
+    have room for `grow_steps` more tokens and `reset()` rewinds them.
+    `ctx0` (optional, one int per sequence) replaces the seeded starting
+    contexts."""
     from synapcore_b200.pool import KVPool
 
     dev = torch.device("cuda", torch.cuda.current_device())
     L, hq, hkv, d, B = w["layers"], w["hq"], w["hkv"], w["d"], w["batch"]
     grow = bool(w.get("grow"))
-    ctx0 = seq_contexts(w, rank)
+    ctx0 = seq_contexts(w, rank) if ctx0 is None else np.asarray(ctx0, np.int64)
+    if ctx0.shape != (B,):
+        raise ValueError(f"ctx0 must hold {B} contexts")
     cap = ctx0 + (grow_steps + 1 if grow else 0)
     n_blocks = (cap + PAGE - 1) // PAGE
     max_blocks = int(n_blocks.max())
