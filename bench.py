@@ -1391,7 +1391,10 @@ class MixState:
         max_blocks = (hi + w["prompt"][1] + max_steps + 2 * PAGE) // PAGE + 1
         self.max_rows = w["batch"] + w["new_per_step"] + 1
         self.P = int(w["pool_pages"])
-        self.cache = PagedKVCache(L, hkv, d, self.P, self.max_rows, max_blocks, w["kv"], device=dev)
+        # retired sequences keep their pages cached; the cache evicts them LRU
+        # first whenever more than evict_at of the pool is allocated
+        self.cache = PagedKVCache(L, hkv, d, self.P, self.max_rows, max_blocks, w["kv"], device=dev,
+                                  evict_watermark=w["evict_at"])
         g = torch.Generator(device=dev)
         g.manual_seed(4321 + rank)
         self.src_k = torch.randn((L, hi, hkv, d), generator=g, device=dev).to(w["qdt"])
@@ -1405,15 +1408,12 @@ class MixState:
         self.k_dec = torch.randn((L, self.max_rows, hkv, d), generator=g, device=dev).to(w["qdt"])
         self.v_dec = torch.randn((L, self.max_rows, hkv, d), generator=g, device=dev).to(w["qdt"])
         self.out_dec = torch.empty((self.max_rows, hq, d), dtype=w["qdt"], device=dev)
-        # pool accounting: ring (free), cached (unpinned, evictable), pinned
-        self.free, self.cached = self.P, 0
         self.forked = set()
         self.next_id = 0
         c = self.cache
         # the shared prefix: written once, held by one extra pin
         npre = w["prefix"]
         c.add_sequence("prefix")
-        self._alloc(-(-npre // PAGE))
         c.append_prefill("prefix", self.src_k[:, :npre], self.src_v[:, :npre])
         self.prefix_pages = c.page_ids("prefix")
         c.pool.pin_pages(torch.tensor(self.prefix_pages, dtype=torch.int32, device=dev), +1)
@@ -1429,7 +1429,6 @@ class MixState:
                 own = int(self.rng.integers(lo, hi - npre + 1))
             else:
                 own = int(self.rng.integers(lo, hi + 1))
-            self._alloc(self._pages_needed(c.length(sid), own))
             c.append_prefill(sid, self.src_k[:, :own], self.src_v[:, :own])
         torch.cuda.synchronize()
         self.check_accounting()
@@ -1439,24 +1438,9 @@ class MixState:
         self.next_id += 1
         return self.next_id
 
-    @staticmethod
-    def _pages_needed(length: int, add: int) -> int:
-        return -(-(length + add) // PAGE) - (-(-length // PAGE))
-
-    def _alloc(self, n: int):
-        take = min(n, self.free)
-        self.free -= take
-        self.cached -= n - take
-        if self.cached < 0:
-            raise RuntimeError("pool exhausted")
-
-    def occupancy(self) -> int:
-        return self.P - self.free
-
     def check_accounting(self):
-        st = self.cache.pool.alloc_state()
-        if st["free"] != self.free:
-            raise RuntimeError(f"pool accounting drifted: device ring has {st['free']}, host expects {self.free}")
+        """The allocator recorded no error (an exhausted pool would show here)."""
+        self.cache.check()
 
     def step(self, timing=None, io=None):
         """One serving step; returns (algorithmic bytes, decode tokens, prefill tokens, launch bytes)."""
@@ -1467,18 +1451,11 @@ class MixState:
         live = list(c.seq_at)
         gone = [live[i] for i in self.rng.choice(len(live), size=w["new_per_step"], replace=False)]
         for sid in gone:
-            own = -(-c.length(sid) // PAGE) - (len(self.prefix_pages) if sid in self.forked else 0)
-            self.cached += own
             self.forked.discard(sid)
         c.remove_sequences(gone, keep_cached=True)
-        # 2. eviction policy: occupancy at most evict_at of the pool
-        limit = int(w["evict_at"] * self.P)
-        if self.occupancy() > limit:
-            k = min(self.occupancy() - limit, self.cached)
-            if k > 0:
-                c.pool.evict_lru(k)
-                self.cached -= k
-                self.free += k
+        # 2. eviction policy: the cache evicts LRU cached pages on the device
+        #    until at most evict_at of the pool is allocated
+        c.enforce_watermark()
         # 3. admit new prompts: forks share the prefix pages, all prefill causally
         plo, phi = w["prompt"]
         new_ids, T, starts = [], [], []
@@ -1489,7 +1466,6 @@ class MixState:
                 c.share_prefix(sid, self.prefix_pages)
                 self.forked.add(sid)
             t = int(self.rng.integers(plo, phi + 1))
-            self._alloc(self._pages_needed(c.length(sid), t))
             new_ids.append(sid)
             T.append(t)
             starts.append(c.length(sid))
@@ -1513,7 +1489,6 @@ class MixState:
                 timing["pre"][-1].record()
         # 4. decode one token for every live sequence
         n = c.n_live
-        self._alloc(sum(1 for r in range(n) if c.lengths[r] % PAGE == 0))
         if io is not None:
             io["dec_in"](n)
         c.decode_reserve(n)
@@ -1678,8 +1653,7 @@ def bench_mix(args, w, world, rank, local):
                      "bytes_per_launch": int(dec_launch_bytes), "avg_launch_ms": round(dec_avg_ms, 4)},
         "prefill_roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
                              "frac": round(tflops / tc_peak, 4),
-                             "kernel": ("prefill_tc_kernel (tcgen05)" if w["kv"] in ("fp16", "bf16")
-                                        else "prefill_kernel (mma.sync)") + " per layer launch",
+                             "kernel": "prefill_tc_kernel (tcgen05) per layer launch",
                              "flops_per_launch": int(np.mean(pre_flops) / L), "avg_launch_ms": round(pre_avg_ms, 4)},
         "clocks": clocks,
     }

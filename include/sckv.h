@@ -380,6 +380,18 @@ SCKV_API int sckv_release_pages(sckv_pool* pool, const int32_t* ids, int n,
  * tail, oldest first; out_ids (may be NULL) receives them, -1 padded. */
 SCKV_API int sckv_evict_lru(sckv_pool* pool, int n, int32_t* out_ids, void* stream);
 
+/* Occupancy-bounded eviction: evict unpinned allocated pages in LRU order
+ * until at most max_allocated pages are allocated (or no unpinned page is
+ * left), the allocated count being read on the device, so a serving loop
+ * needs no host accounting or device read for it (and the call can sit in a
+ * captured graph). out_count (device int32, may be NULL) receives how many
+ * were evicted. Each eviction counts as in sckv_evict_lru. No reference
+ * counterpart: the reference evicts only when an allocation finds the free
+ * list empty (native/native_engine.py:324-331), which sckv_alloc_pages does;
+ * this is the "evict at X % full" policy of a continuous-batching server. */
+SCKV_API int sckv_evict_to_watermark(sckv_pool* pool, int64_t max_allocated,
+                             int32_t* out_count, void* stream);
+
 /* Decode-step page reservation, fully on device: for b in 0..n_seqs-1 in
  * order, if ctx_lens[b] % 16 == 0 a page is allocated (as sckv_alloc_pages,
  * pinned) into block_table[b][ctx_lens[b]/16]; then ctx_lens[b] += 1. */

@@ -439,6 +439,16 @@ class AllocatorOracle:
             out.append(v)
         return out + [-1] * (n - len(out))
 
+    def evict_to_watermark(self, max_allocated: int) -> int:
+        """LRU evictions until at most max_allocated pages are allocated (or
+        no unpinned page is left); the serving policy of the device pool
+        (no reference counterpart: the arena evicts only when its free list
+        is empty, native/native_engine.py:324-331)."""
+        over = int(self.allocated.sum()) - int(max_allocated)
+        if over <= 0:
+            return 0
+        return sum(1 for v in self.evict_lru(over) if v >= 0)
+
     def reserve_decode(self, block_table: np.ndarray, ctx_lens: np.ndarray) -> None:
         need = [b for b in range(len(ctx_lens)) if ctx_lens[b] % PAGE_TOKENS == 0]
         ids, _ = self.alloc(len(need), pin=True)

@@ -104,6 +104,7 @@ _SIGNATURES = [
     ("sckv_pin_pages", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     ("sckv_release_pages", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     ("sckv_evict_lru", c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    ("sckv_evict_to_watermark", c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     ("sckv_reserve_decode", c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p]),
     ("sckv_alloc_state", c_int, [c_void_p, POINTER(c_int64), c_void_p]),
     ("sckv_get_status", c_int, [c_void_p, POINTER(c_int32), c_void_p]),

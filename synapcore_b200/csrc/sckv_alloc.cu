@@ -421,9 +421,16 @@ __global__ void pin_kernel(AllocView a, const int32_t* ids, int n, int delta) {
   }
 }
 
-__global__ void __launch_bounds__(kT) evict_kernel(AllocView a, int n, int32_t* out_ids) {
+// LRU eviction of n pages, or (watermark >= 0) of as many as bring the
+// allocated count down to the watermark, read on the device.
+__global__ void __launch_bounds__(kT) evict_kernel(AllocView a, int n, int64_t watermark, int32_t* out_ids,
+                                                   int32_t* out_count) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& s = *reinterpret_cast<SelectSmem*>(smem_raw);
+  if (watermark >= 0) {
+    const int64_t over = a.ctl[CTL_ALLOCATED] - watermark;
+    n = over > 0 ? (int)(over < a.P ? over : a.P) : 0;
+  }
   int done = 0;
   unsigned long long lo = 0;
   while (done < n) {
@@ -452,6 +459,7 @@ __global__ void __launch_bounds__(kT) evict_kernel(AllocView a, int n, int32_t* 
   }
   if (out_ids)
     for (int k = done + threadIdx.x; k < n; k += kT) out_ids[k] = -1;
+  if (out_count && threadIdx.x == 0) *out_count = done;
 }
 
 // Decode-step reservation: sequences whose next token starts a page get one,
@@ -602,7 +610,17 @@ extern "C" int sckv_evict_lru(sckv_pool* p, int n, int32_t* out_ids, void* strea
   SCKV_DEVICE_GUARD(p->device);
   int rc = ensure_configured(p->device);
   if (rc != SCKV_OK) return rc;
-  evict_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), n, out_ids);
+  evict_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), n, -1, out_ids, nullptr);
+  SCKV_LAUNCH_CHECK();
+  return SCKV_OK;
+}
+
+extern "C" int sckv_evict_to_watermark(sckv_pool* p, int64_t max_allocated, int32_t* out_count, void* stream) {
+  if (p == nullptr || max_allocated < 0) return SCKV_ERR_INVALID_ARG;
+  SCKV_DEVICE_GUARD(p->device);
+  int rc = ensure_configured(p->device);
+  if (rc != SCKV_OK) return rc;
+  evict_kernel<<<1, kT, kSelectSmemBytes, as_stream(stream)>>>(view_of(p), 0, max_allocated, nullptr, out_count);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }

@@ -32,7 +32,16 @@ def _ceil_div(a: int, b: int) -> int:
 class PagedKVCache:
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_pages: int, max_seqs: int,
                  max_blocks_per_seq: int, kv_dtype: str = "fp16", device: Optional[torch.device] = None,
-                 chunk_pages: int = 32):
+                 chunk_pages: int = 32, evict_watermark: Optional[float] = None):
+        """evict_watermark: None keeps the arena's policy — pages released
+        with keep_cached stay allocated and are taken back, least recently
+        used first, only when an allocation finds the free ring empty
+        (native/native_engine.py:324-331). A fraction f in (0, 1] adds the
+        serving policy "evict at f full": enforce_watermark() evicts cached
+        pages, LRU first, until at most f * max_pages are allocated."""
+        if evict_watermark is not None and not 0.0 < float(evict_watermark) <= 1.0:
+            raise ValueError("evict_watermark must be in (0, 1]")
+        self.evict_watermark = None if evict_watermark is None else float(evict_watermark)
         self.pool = KVPool(num_layers, num_kv_heads, head_dim, max_pages, kv_dtype, device=device)
         self.device = self.pool.device
         self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
@@ -128,6 +137,17 @@ class PagedKVCache:
         self.lengths[row], self.lengths[r] = self.lengths[r], self.lengths[row]
         self.row_of[seq_id], self.row_of[other] = row, r
 
+    # ------------------------------------------------------------- eviction
+    def enforce_watermark(self, out_count: Optional[torch.Tensor] = None) -> None:
+        """With an evict_watermark, evict cached (unpinned) pages in LRU order
+        until at most watermark * max_pages pages are allocated; decided on
+        the device (one launch, no host read). Pages held by live sequences
+        or a prefix index (pinned) are never evicted. No-op without one."""
+        if self.evict_watermark is None:
+            return
+        limit = int(self.evict_watermark * self.pool.max_pages)
+        self.pool.evict_to_watermark(limit, out_count=out_count)
+
     # -------------------------------------------------------------- prefill
     def _grow(self, r: int, n_new: int) -> None:
         """Allocate (pinned) pages so row r can hold n_new more tokens."""
@@ -204,6 +224,79 @@ class PagedKVCache:
                          layer0=0, max_blocks=self.max_blocks)
         for i in range(n):
             self.lengths[r0 + i] += T[i]
+        self.ctx_lens[r0:r0 + n].copy_(to_device(self.lengths[r0:r0 + n], torch.int32, self.device))
+
+    def begin_prefill_batch(self, seq_ids: Sequence[Hashable], n_new: Sequence[int],
+                            shared: Optional[Sequence[Sequence[tuple]]] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Set up the prompt pass of several new, empty sequences on
+        consecutive rows (added one after another), to be run layer by layer
+        with `append_layer_batch` + `prefill_attention_batch` and closed with
+        `end_prefill_batch`.
+
+        n_new[i]: tokens sequence i computes in this pass.
+        shared[i] (optional): its leading full blocks, taken from elsewhere
+        instead of computed, each ("page", page_id) — a page another holder
+        keeps (a prefix index) — or ("row", j, b) — block b of the j-th
+        sequence of this same batch (j < i), which this pass allocates and
+        whose append runs before any attention reads it.
+
+        One allocation launch covers every sequence's own pages; shared pages
+        get one more pin per new holder. Returns the device int32 cu_tokens
+        [n + 1] and start_pos [n] of the pass."""
+        seq_ids = list(seq_ids)
+        n = len(seq_ids)
+        shared = [list(s) for s in shared] if shared is not None else [[] for _ in range(n)]
+        if len(shared) != n or len(n_new) != n:
+            raise ValueError("one n_new and one shared list per sequence")
+        r0 = self._consecutive_rows(seq_ids)
+        page_rc, page_ids, dst_rc, src_rc = [], [], [], []
+        for i, blocks in enumerate(shared):
+            r = r0 + i
+            if self.lengths[r] != 0:
+                raise ValueError("begin_prefill_batch needs empty sequences")
+            for b, src in enumerate(blocks):
+                if src[0] == "page":
+                    page_rc.append((r, b))
+                    page_ids.append(int(src[1]))
+                elif src[0] == "row" and 0 <= int(src[1]) < i:
+                    dst_rc.append((r, b))
+                    src_rc.append((r0 + int(src[1]), int(src[2])))
+                else:
+                    raise ValueError(f"bad shared block source {src!r}")
+            self.lengths[r] = len(blocks) * PAGE_TOKENS
+        if page_ids:
+            t = to_device([[r for r, _ in page_rc], [c for _, c in page_rc], page_ids], torch.int64, self.device)
+            self.block_table[t[0], t[1]] = t[2].to(torch.int32)
+        self._grow_rows(r0, [int(t) for t in n_new])
+        if dst_rc:
+            t = to_device([[r for r, _ in dst_rc], [c for _, c in dst_rc], [r for r, _ in src_rc],
+                           [c for _, c in src_rc]], torch.int64, self.device)
+            self.block_table[t[0], t[1]] = self.block_table[t[2], t[3]]
+        held = page_rc + dst_rc
+        if held:
+            t = to_device([[r for r, _ in held], [c for _, c in held]], torch.int64, self.device)
+            self.pool.pin_pages(self.block_table[t[0], t[1]], +1)
+        cu = [0]
+        for t in n_new:
+            cu.append(cu[-1] + int(t))
+        meta = to_device(cu + [self.lengths[r0 + i] for i in range(n)], torch.int32, self.device)
+        return meta[:n + 1], meta[n + 1:]
+
+    def append_layer_batch(self, layer: int, seq_ids: Sequence[Hashable], k: torch.Tensor, v: torch.Tensor,
+                           cu_tokens: torch.Tensor, start_pos: torch.Tensor) -> None:
+        """One layer's K/V of a pass set up by begin_prefill_batch:
+        k, v [total, Hkv, D]."""
+        r0 = self._consecutive_rows(seq_ids)
+        n = len(seq_ids)
+        self.pool.append(k, v, cu_tokens, start_pos, self.block_table[r0:r0 + n], layer0=layer,
+                         max_blocks=self.max_blocks)
+
+    def end_prefill_batch(self, seq_ids: Sequence[Hashable], n_new: Sequence[int]) -> None:
+        """Advance the lengths once every layer of the pass has been written."""
+        r0 = self._consecutive_rows(seq_ids)
+        n = len(seq_ids)
+        for i in range(n):
+            self.lengths[r0 + i] += int(n_new[i])
         self.ctx_lens[r0:r0 + n].copy_(to_device(self.lengths[r0:r0 + n], torch.int32, self.device))
 
     def prefill_attention_batch(self, layer: int, seq_ids: Sequence[Hashable], q: torch.Tensor,

@@ -564,6 +564,16 @@ class KVPool:
         N.check(self.lib.sckv_evict_lru(self.handle, n, out.data_ptr(), _stream_ptr(stream)), "sckv_evict_lru")
         return out[:n]
 
+    def evict_to_watermark(self, max_allocated: int, out_count: Optional[torch.Tensor] = None,
+                           stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Evict LRU unpinned pages until at most max_allocated are allocated
+        (decided on the device; out_count, an int32 device tensor, receives
+        how many were evicted)."""
+        if out_count is not None:
+            _need(out_count, "out_count", self.device, torch.int32, 1)
+        N.check(self.lib.sckv_evict_to_watermark(self.handle, int(max_allocated), _ptr(out_count),
+                                                 _stream_ptr(stream)), "sckv_evict_to_watermark")
+
     def reserve_decode(self, block_table: torch.Tensor, ctx_lens: torch.Tensor, n_seqs: Optional[int] = None,
                        max_blocks: Optional[int] = None, stream: Optional[torch.cuda.Stream] = None) -> None:
         n = ctx_lens.numel() if n_seqs is None else int(n_seqs)

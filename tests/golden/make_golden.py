@@ -428,64 +428,66 @@ def attention_layer_cases(ad, arrays):
     return out
 
 
-def scheduler_runs(ne, ad, arrays):
-    """The reference ContinuousBatchScheduler (engine/scheduler.py) over a
-    stub of the reference engine carrying the seeded weights of
+def _stub_engine(ne, ad, w, c, tmp):
+    """A stub of the reference engine carrying the seeded weights of
     tests/stub_model.py: real ModularAttentionEngine attention, real
-    NativeKVPrefixCache (stand-in bridge, fixed clock), one routed expert.
-    Runs the six requests batched (max_batch_size 4) and isolated."""
+    NativeKVPrefixCache (stand-in bridge), one routed expert."""
     import types
+
+    cfg = {"model_type": "olmoe", "num_hidden_layers": c["num_layers"], "num_experts": 1, "num_experts_per_tok": 1,
+           "hidden_size": c["hidden"], "intermediate_size": c["inter"], "num_attention_heads": c["hq"],
+           "num_key_value_heads": c["hkv"], "vocab_size": c["vocab"], "rms_norm_eps": c["rms_eps"],
+           "rope_theta": c["rope_theta"], "eos_token_id": 50279}
+    eng = types.SimpleNamespace()
+    eng.config = cfg
+    eng.num_layers = c["num_layers"]
+    eng.hidden_size = c["hidden"]
+    eng.rms_eps = c["rms_eps"]
+    eng.top_k = 1
+    eng.enable_merkle_kv = True
+    eng.active_merkle_root = GOLDEN_SEED_ROOT
+    eng.adapter = ad.OLMoEAdapter(cfg)
+    eng.attention_engine = ad.ModularAttentionEngine(eng.adapter.spec)
+    eng.kv_prefix_cache = ne.NativeKVPrefixCache(tmp, stand_in_bridge(ne), device="cpu",
+                                                 num_layers=c["num_layers"], num_kv_heads=c["hkv"],
+                                                 head_dim=c["head_dim"], max_pages=64, quant_mode="fp16")
+    eng.emb_np_view = w["emb"]
+    eng.lm_head_w_int8_view = w["lm_w_int8"]
+    eng.lm_head_s_fp16_view = w["lm_s_fp16"]
+    eng.core_np_views = {k: v for k, v in w.items() if k.startswith("model.")}
+    eng.live_routing_buffer = types.SimpleNamespace(record_numpy_layer=lambda l, idx: None)
+    eng._rmsnorm_numpy = types.MethodType(ne.NativeMerkleMoEEngine._rmsnorm_numpy, eng)
+    eng.forward_attention_layer_numpy = types.MethodType(ne.NativeMerkleMoEEngine.forward_attention_layer_numpy,
+                                                         eng)
+    eng.load_or_get_expert_entry = lambda l, e, is_prefetch=False: types.SimpleNamespace(
+        gate_w=w[f"model.layers.{l}.expert.gate"], up_w=w[f"model.layers.{l}.expert.up"],
+        down_w=w[f"model.layers.{l}.expert.down"])
+    return eng
+
+
+def scheduler_runs(ne, ad, arrays):
+    """The reference ContinuousBatchScheduler (engine/scheduler.py) over the
+    stub engine. Runs the six requests batched (max_batch_size 4), isolated,
+    and batched over the first layer only (max_layers=1)."""
     import time as _time
+    import types
 
     sys.path.insert(0, str(OUT.parent))
     from stub_model import CFG, make_weights, prompts  # noqa: E402
     from engine import scheduler as sch  # noqa: E402
 
     w = make_weights()
-    c = CFG
-    cfg = {"model_type": "olmoe", "num_hidden_layers": c["num_layers"], "num_experts": 1, "num_experts_per_tok": 1,
-           "hidden_size": c["hidden"], "intermediate_size": c["inter"], "num_attention_heads": c["hq"],
-           "num_key_value_heads": c["hkv"], "vocab_size": c["vocab"], "rms_norm_eps": c["rms_eps"],
-           "rope_theta": c["rope_theta"], "eos_token_id": 50279}
     ne.time = types.SimpleNamespace(time=lambda: 0.0, perf_counter=_time.perf_counter)
-
-    def make_engine(tmp):
-        eng = types.SimpleNamespace()
-        eng.config = cfg
-        eng.num_layers = c["num_layers"]
-        eng.hidden_size = c["hidden"]
-        eng.rms_eps = c["rms_eps"]
-        eng.top_k = 1
-        eng.enable_merkle_kv = True
-        eng.active_merkle_root = GOLDEN_SEED_ROOT
-        eng.adapter = ad.OLMoEAdapter(cfg)
-        eng.attention_engine = ad.ModularAttentionEngine(eng.adapter.spec)
-        eng.kv_prefix_cache = ne.NativeKVPrefixCache(tmp, stand_in_bridge(ne), device="cpu",
-                                                     num_layers=c["num_layers"], num_kv_heads=c["hkv"],
-                                                     head_dim=c["head_dim"], max_pages=64, quant_mode="fp16")
-        eng.emb_np_view = w["emb"]
-        eng.lm_head_w_int8_view = w["lm_w_int8"]
-        eng.lm_head_s_fp16_view = w["lm_s_fp16"]
-        eng.core_np_views = {k: v for k, v in w.items() if k.startswith("model.")}
-        eng.live_routing_buffer = types.SimpleNamespace(record_numpy_layer=lambda l, idx: None)
-        eng._rmsnorm_numpy = types.MethodType(ne.NativeMerkleMoEEngine._rmsnorm_numpy, eng)
-        eng.forward_attention_layer_numpy = types.MethodType(ne.NativeMerkleMoEEngine.forward_attention_layer_numpy,
-                                                             eng)
-        eng.load_or_get_expert_entry = lambda l, e, is_prefetch=False: types.SimpleNamespace(
-            gate_w=w[f"model.layers.{l}.expert.gate"], up_w=w[f"model.layers.{l}.expert.up"],
-            down_w=w[f"model.layers.{l}.expert.down"])
-        return eng
-
     ps = prompts()
     out = {"prompts": ps}
     try:
-        for mode, mbs in (("batched", 4), ("isolated", 1)):
+        for mode, mbs, max_layers in (("batched", 4, None), ("isolated", 1, None), ("batched_1layer", 4, 1)):
             tmp = Path(tempfile.mkdtemp(prefix="sckv_sched_"))
-            eng = make_engine(tmp)
+            eng = _stub_engine(ne, ad, w, CFG, tmp)
             s_ = sch.ContinuousBatchScheduler(eng, max_batch_size=mbs)
             for i, pr in enumerate(ps):
                 s_.submit_request(f"req_{i}", pr, max_new_tokens=5, stop_token_ids=set())
-            steps = s_.run_until_complete_numpy()
+            steps = s_.run_until_complete_numpy(max_layers=max_layers)
             done = s_.completed_requests
             out[mode] = {
                 "generated": {k: list(map(int, v.generated_ids)) for k, v in done.items()},
@@ -494,6 +496,8 @@ def scheduler_runs(ne, ad, arrays):
                 "blocks_loaded_from_arena": int(eng.kv_prefix_cache.blocks_loaded_from_arena),
                 "steps": len(steps),
                 "batch_sizes": [int(st["batch_size"]) for st in steps],
+                "unique_expert_dispatches": int(s_.total_unique_expert_dispatches),
+                "naive_expert_dispatches": int(s_.total_naive_expert_dispatches),
             }
             for k, v in done.items():
                 arrays[f"sched_{mode}_{k}_logits"] = v.last_logits.astype(np.float32)
@@ -501,6 +505,59 @@ def scheduler_runs(ne, ad, arrays):
     finally:
         ne.time = _time
     return out
+
+
+def scheduler_benchmark(ne, ad):
+    """The body of benchmark_continuous_batch_scheduler
+    (engine/scheduler.py:391-481) over the stub engine (the benchmark itself
+    builds a NativeMerkleMoEEngine from a model store this checkout does not
+    ship): the reference's prompts, each request alone with max_batch_size=1,
+    then all four together; one engine shared by all runs, as there."""
+    import time as _time
+    import types
+
+    sys.path.insert(0, str(OUT.parent))
+    from stub_model import BENCH_CFG, make_weights  # noqa: E402
+    from engine import scheduler as sch  # noqa: E402
+
+    w = make_weights(cfg=BENCH_CFG)
+    ne.time = types.SimpleNamespace(time=lambda: 0.0, perf_counter=_time.perf_counter)
+    tmp = Path(tempfile.mkdtemp(prefix="sckv_bench_"))
+    try:
+        eng = _stub_engine(ne, ad, w, BENCH_CFG, tmp)
+        num_requests, max_new_tokens, max_layers = 4, 3, 2
+        shared_prefix = [1, 512, 1024, 2048, 4096, 8192, 12, 34, 56, 78, 90, 111, 222, 333, 444, 555]
+        prompts = [shared_prefix + [100 + r, 200 + r] for r in range(num_requests)]
+        seq_tokens, seq_logits = {}, {}
+        for r, p_ids in enumerate(prompts):
+            single = sch.ContinuousBatchScheduler(eng, max_batch_size=1)
+            single.submit_request(f"req_{r}", p_ids, max_new_tokens=max_new_tokens, stop_token_ids=set())
+            single.run_until_complete_numpy(max_layers=max_layers)
+            d = single.completed_requests[f"req_{r}"]
+            seq_tokens[f"req_{r}"] = list(map(int, d.generated_ids))
+            seq_logits[f"req_{r}"] = d.last_logits.copy()
+        batch = sch.ContinuousBatchScheduler(eng, max_batch_size=num_requests)
+        for r, p_ids in enumerate(prompts):
+            batch.submit_request(f"req_{r}", p_ids, max_new_tokens=max_new_tokens, stop_token_ids=set())
+        steps = batch.run_until_complete_numpy(max_layers=max_layers)
+        err = max(float(np.max(np.abs(batch.completed_requests[k].last_logits - seq_logits[k]))) for k in seq_logits)
+        uniq, naive = batch.total_unique_expert_dispatches, batch.total_naive_expert_dispatches
+        return {
+            "seq_tokens": seq_tokens,
+            "batch_tokens": {k: list(map(int, v.generated_ids)) for k, v in batch.completed_requests.items()},
+            "total_requests_completed": len(batch.completed_requests),
+            "total_tokens_generated": int(batch.total_tokens_generated),
+            "max_concurrent_batch_size": max(int(st["batch_size"]) for st in steps),
+            "total_batch_steps": len(steps),
+            "total_unique_expert_dispatches": int(uniq),
+            "total_naive_expert_dispatches": int(naive),
+            "cross_request_expert_sharing_pct": round(100.0 * (1.0 - uniq / max(1, naive)), 2),
+            "paged_kv_prefix_tokens_skipped": int(eng.kv_prefix_cache.tokens_skipped),
+            "numerical_parity_max_abs_err": round(err, 8),
+        }
+    finally:
+        ne.time = _time
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def main():
@@ -526,6 +583,7 @@ def main():
         "arena_alloc_streams": arena_alloc_streams(ne, arrays),
         "sdpa": sdpa_cases(ad, arrays),
         "scheduler": scheduler_runs(ne, ad, arrays),
+        "scheduler_benchmark": scheduler_benchmark(ne, ad),
         "qk_rope": qk_rope_cases(ad, arrays),
         "attention_layer": attention_layer_cases(ad, arrays),
         "chain_hash": [ne.chain_merkle_prefix_hash(GOLDEN_SEED_ROOT, list(range(16))),

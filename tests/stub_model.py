@@ -17,6 +17,8 @@ import numpy as np
 
 CFG = dict(num_layers=2, hidden=512, hq=4, hkv=2, head_dim=128, inter=256, vocab=512, rms_eps=1e-5,
            rope_theta=10000.0)
+# the reference scheduler benchmark's prompts use token ids up to 8192
+BENCH_CFG = dict(CFG, vocab=8448)
 
 
 def make_weights(seed: int = 1234, cfg=CFG):
@@ -129,3 +131,57 @@ class TorchStubModel:
     def logits(self, h_last):
         x = self._rms(h_last, self.final_norm)
         return (x @ self.lm_w.T) * self.lm_s[None, :]
+
+
+class StubEngine:
+    """The reference engine's scheduler-facing surface (engine/scheduler.py:
+    119-309) over the same seeded weights, for driving synapcore_b200's
+    ContinuousBatchScheduler(engine, max_batch_size) the way the reference
+    scheduler is driven in tests/golden/make_golden.py. Router: the reference
+    adapter's softmax top-k (models/adapters.py:244-260) over one expert;
+    attention parameters as ModularAttentionEngine derives them for this
+    OLMoE-style config (models/adapters.py:1105-1127)."""
+
+    def __init__(self, w, seed_root_hex: str, cfg=CFG):
+        import types
+
+        self.config = {"model_type": "olmoe", "num_hidden_layers": cfg["num_layers"], "hidden_size": cfg["hidden"],
+                       "num_attention_heads": cfg["hq"], "num_key_value_heads": cfg["hkv"],
+                       "vocab_size": cfg["vocab"], "rms_norm_eps": cfg["rms_eps"], "rope_theta": cfg["rope_theta"],
+                       "eos_token_id": 50279}
+        self.num_layers = cfg["num_layers"]
+        self.hidden_size = cfg["hidden"]
+        self.rms_eps = cfg["rms_eps"]
+        self.top_k = 1
+        self.enable_merkle_kv = True
+        self.active_merkle_root = seed_root_hex
+        self.emb_np_view = w["emb"]
+        self.lm_head_w_int8_view = w["lm_w_int8"]
+        self.lm_head_s_fp16_view = w["lm_s_fp16"]
+        self.core_np_views = {k: v for k, v in w.items() if k.startswith("model.")}
+        self._w = w
+        d = cfg["head_dim"]
+        self.attention_engine = types.SimpleNamespace(
+            num_heads=cfg["hq"], num_kv_heads=cfg["hkv"], head_dim=d, rms_eps=cfg["rms_eps"],
+            rope_scaling_factor=1.0, has_qk_norm=True, scale=float(d) ** -0.5,
+            rope_inv_freq=1.0 / (cfg["rope_theta"] ** (np.arange(0, d, 2, dtype=np.float32) / float(d))))
+        self.adapter = types.SimpleNamespace(route_tokens_numpy=self._route)
+        self.live_routing_buffer = types.SimpleNamespace(record_numpy_layer=lambda l, idx: None)
+        self.closed = False
+
+    def _route(self, x_flat_f32, router_w_fp16):
+        logits = x_flat_f32 @ router_w_fp16.astype(np.float32).T
+        p = np.exp(logits - np.max(logits, axis=-1, keepdims=True))
+        p = p / np.sum(p, axis=-1, keepdims=True)
+        idx = np.argpartition(-p, kth=self.top_k - 1, axis=-1)[:, :self.top_k].astype(np.int32)
+        return idx, np.take_along_axis(p, idx, axis=-1)
+
+    def load_or_get_expert_entry(self, layer, e, is_prefetch=False):
+        import types
+
+        p = f"model.layers.{layer}"
+        return types.SimpleNamespace(gate_w=self._w[f"{p}.expert.gate"], up_w=self._w[f"{p}.expert.up"],
+                                     down_w=self._w[f"{p}.expert.down"])
+
+    def close(self):
+        self.closed = True

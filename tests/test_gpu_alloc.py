@@ -211,3 +211,65 @@ def test_device_allocator_replays_reference_arena_streams(cuda_device, idx, batc
     assert pool.status()[0] == 0
     check_final_state(dev, st, counters, state["clock"], state["evictions"])
     pool.close()
+
+
+def test_evict_to_watermark_matches_oracle(cuda_device):
+    """sckv_evict_to_watermark decides the eviction count on the device:
+    after it at most `limit` pages are allocated (or every unpinned page is
+    gone), victims in LRU order, the same as the oracle's restatement."""
+    rng = np.random.default_rng(17)
+    P = 300
+    pool = _pool(cuda_device, P)
+    ora = AllocatorOracle(P)
+    cnt = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for step in range(60):
+        n = int(rng.integers(1, 40))
+        cand = int(np.count_nonzero(ora.allocated & (ora.pin == 0)))
+        if n <= len(ora.ring) + cand:
+            pin = bool(rng.random() < 0.3)
+            ids, _ = pool.alloc_pages(n, pin=pin)
+            assert ids.cpu().tolist() == ora.alloc(n, pin=pin)[0]
+        if rng.random() < 0.4:
+            t = rng.integers(0, P, size=10).tolist()
+            pool.touch_pages(torch.tensor(t, dtype=torch.int32))
+            ora.touch(t)
+        if rng.random() < 0.2:
+            pinned = np.nonzero(ora.allocated & (ora.pin > 0))[0]
+            if pinned.size:
+                ids = rng.choice(pinned, size=min(5, pinned.size), replace=False).tolist()
+                pool.release_pages(torch.tensor(ids, dtype=torch.int32), keep_cached=True)
+                for i in ids:
+                    ora.pin[i] -= 1
+        limit = int(rng.integers(P // 4, P))
+        pool.evict_to_watermark(limit, out_count=cnt)
+        exp = ora.evict_to_watermark(limit)
+        assert int(cnt.item()) == exp, step
+        _compare(pool, ora)
+        alloc = int(ora.allocated.sum())
+        assert alloc <= limit or not np.any(ora.allocated & (ora.pin == 0))
+    assert pool.status()[0] == 0
+    pool.close()
+
+
+def test_paged_cache_watermark_policy(cuda_device):
+    """PagedKVCache(evict_watermark=f): finished sequences kept cached are
+    evicted LRU first once more than f of the pool is allocated; live
+    sequences' pages are never touched."""
+    from synapcore_b200.paged_cache import PagedKVCache
+
+    c = PagedKVCache(1, 1, 128, max_pages=100, max_seqs=16, max_blocks_per_seq=16, device=cuda_device,
+                     evict_watermark=0.5)
+    kv = torch.zeros((1, 160, 1, 128), dtype=torch.float16, device=cuda_device)
+    for i in range(8):  # 8 x 10 pages
+        c.add_sequence(i)
+        c.append_prefill(i, kv, kv)
+    c.remove_sequences([0, 1, 2, 3], keep_cached=True)  # 40 cached pages, 40 live
+    st = c.pool.alloc_state()
+    assert st["allocated"] == 80
+    c.enforce_watermark()
+    assert c.pool.alloc_state()["allocated"] == 50  # 30 oldest cached pages evicted
+    c.enforce_watermark()
+    assert c.pool.alloc_state()["allocated"] == 50
+    c.remove_sequences([4, 5, 6, 7])  # freed outright
+    assert c.pool.alloc_state()["allocated"] == 10
+    c.check()
