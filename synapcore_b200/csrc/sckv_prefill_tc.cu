@@ -336,7 +336,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     uint64_t* sfull = stage_full + 2 * role;
     uint8_t* stg = base + C::kOffStage + role * 2 * C::kStageSlot;
     const int r = lane >> 1, hf = lane & 1;
-    float scl[2][2];  // [staging slot][page]: this lane's scale (int8: the fp16 value)
+    // This lane's scales (int8: the token's fp16 value) of the tile decoded
+    // next (scl_dec) and of the tile staged last (scl_new). Kept in named
+    // registers, not an array indexed by the staging slot (that would live in
+    // local memory, and storing a scale there waits for its global load).
+    // A tile's scales are loaded after its copies are issued and moved into
+    // scl_dec one tile later, so no copy issue waits on a scale load.
+    float scl_dec0 = 0.f, scl_dec1 = 0.f, scl_new0 = 0.f, scl_new1 = 0.f;
     int g = 0;        // tiles of this warp's ring so far
     uint32_t sg = 0;  // staged tiles issued
     uint32_t sc = 0;  // staged tiles decoded
@@ -363,34 +369,55 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (item >= n_items) break;
       const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
       const int32_t* bt_row = p.block_table + (int64_t)it.seq * p.bt_stride;
+      // this warp's page ids of a local tile (0 past the item's last page)
+      auto fetch_ids = [&](int j, int32_t& a, int32_t& b) {
+        const int first = j * kPagesTc + 2 * part;
+        a = first <= it.jlast ? __ldg(bt_row + first) : 0;
+        b = first + 1 <= it.jlast ? __ldg(bt_row + first + 1) : 0;
+      };
+      auto scale_of = [&](int32_t page) -> float {
+        const int64_t sidx = ((layer_base + page) * 2 + kv) * p.hkv + it.h;
+        if (KVDT == SCKV_DTYPE_INT8)
+          return __half2float(__ldg(reinterpret_cast<const __half*>(p.kv_scales) + sidx * 16 + r));
+        return __ldg(reinterpret_cast<const float*>(p.kv_scales) + sidx);
+      };
+      int32_t nid0 = 0, nid1 = 0;  // page ids of the next tile to stage (fetched one tile ahead)
+      fetch_ids(0, nid0, nid1);
       auto issue = [&](int j) {
         const int first = j * kPagesTc + 2 * part;
         const int np = max(0, min(2, it.jlast + 1 - first));
         const uint32_t sl = sg & 1;
-        int32_t pages[2] = {0, 0};
-        for (int i = 0; i < np; ++i) {
-          int32_t page = __ldg(bt_row + first + i);
-          if (page < 0 || page >= p.max_pages) {
-            if (lane == 0) sckv_report(p.status, SCKV_ERR_BOUNDS, page, KID_PREFILL);
-            page = 0;
-          }
-          pages[i] = page;
-          const int64_t sidx = ((layer_base + page) * 2 + kv) * p.hkv + it.h;
-          if (KVDT == SCKV_DTYPE_INT8)
-            scl[sl][i] = __half2float(__ldg(reinterpret_cast<const __half*>(p.kv_scales) + sidx * 16 + r));
-          else
-            scl[sl][i] = __ldg(reinterpret_cast<const float*>(p.kv_scales) + sidx);
+        int32_t pg0 = nid0, pg1 = nid1;
+        if (j + 1 < it.n_k) fetch_ids(j + 1, nid0, nid1);
+        if (np > 0 && (pg0 < 0 || pg0 >= p.max_pages)) {
+          if (lane == 0) sckv_report(p.status, SCKV_ERR_BOUNDS, pg0, KID_PREFILL);
+          pg0 = 0;
+        }
+        if (np > 1 && (pg1 < 0 || pg1 >= p.max_pages)) {
+          if (lane == 0) sckv_report(p.status, SCKV_ERR_BOUNDS, pg1, KID_PREFILL);
+          pg1 = 0;
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&sfull[sl], (uint32_t)np * C::kPageBox);
-          for (int i = 0; i < np; ++i)
-            tma_load_5d(smem_u32(stg + sl * C::kStageSlot + i * C::kPageBox), &tmap, 0, 0, it.h, kv,
-                        (int)(layer_base + pages[i]), &sfull[sl]);
+          if (np > 0)
+            tma_load_5d(smem_u32(stg + sl * C::kStageSlot), &tmap, 0, 0, it.h, kv, (int)(layer_base + pg0),
+                        &sfull[sl]);
+          if (np > 1)
+            tma_load_5d(smem_u32(stg + sl * C::kStageSlot + C::kPageBox), &tmap, 0, 0, it.h, kv,
+                        (int)(layer_base + pg1), &sfull[sl]);
         }
+        scl_dec0 = scl_new0;
+        scl_dec1 = scl_new1;
+        scl_new0 = np > 0 ? scale_of(pg0) : 0.f;
+        scl_new1 = np > 1 ? scale_of(pg1) : 0.f;
         ++sg;
       };
       if (it.n_k > 0) issue(0);
       if (it.n_k > 1) issue(1);
+      if (it.n_k == 1) {
+        scl_dec0 = scl_new0;
+        scl_dec1 = scl_new1;
+      }
       for (int j = 0; j < it.n_k; ++j) {
         const int gt = g + j;
         const int st = gt % kStagesTc;
@@ -406,10 +433,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const int first = j * kPagesTc + 2 * part;
         const int np = max(0, min(2, it.jlast + 1 - first));
         uint8_t* slot = base + (kv ? kOffV : kOffK) + st * kSlotBytes;
-        for (int i = 0; i < np; ++i) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (i >= np) break;
           const uint8_t* src = stg + sl * C::kStageSlot + i * C::kPageBox + r * 128;
           uint8_t* dst = slot + hf * kTileHalf + (2 * part + i) * 2048 + r * 128;
-          const float sv = scl[sl][i];
+          const float sv = i == 0 ? scl_dec0 : scl_dec1;
           const __half2 s2 = __float2half2_rn(sv);  // int8: the stored fp16 scale, exact
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -444,7 +473,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&fulls[st]);
         ++sc;
-        if (j + 2 < it.n_k) issue(j + 2);
+        if (j + 2 < it.n_k) {
+          issue(j + 2);
+        } else {
+          scl_dec0 = scl_new0;
+          scl_dec1 = scl_new1;
+        }
       }
       if (aborted && !leader) break;
       g += it.n_k;
