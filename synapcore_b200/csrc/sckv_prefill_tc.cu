@@ -141,8 +141,21 @@ __device__ __forceinline__ uint4 load_q8(const void* q, int64_t idx, int dtype) 
     const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(q) + idx + 4);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   } else {
+    // the other 16-bit type: one 16-byte load, converted in registers (the
+    // values are exact in fp32, so the MMA type sees them rounded once)
+    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q) + idx);
+    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = sckv_load_as_float(q, idx + i, dtype);
+    for (int i = 0; i < 4; ++i) {
+      if (dtype == SCKV_DTYPE_BF16) {
+        v[2 * i] = __uint_as_float(w4[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
   }
   uint4 r;
   r.x = pack2<kBF16>(v[0], v[1]);
@@ -593,6 +606,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t kIdescS = instr_desc_f16(kBF16, kKeysTc, false);
     constexpr uint32_t kIdescPV = instr_desc_f16(kBF16, kHDim, true);
+    // descriptors of the first Q tile, K slot and V slot; every operand of
+    // an MMA is one of them advanced by a byte offset
+    const uint64_t q_desc0 = smem_desc_sw128(smem_u32(base), 16, 1024);
+    const uint64_t k_desc0 = smem_desc_sw128(smem_u32(base + kOffK), 16, 1024);
+    const uint64_t v_desc0 = smem_desc_sw128(smem_u32(base + kOffV), kTileHalf, 1024);
     bool ok = true;
     int gk = 0;                     // K/V tiles issued
     int gs[kQTiles] = {0, 0};       // S tiles issued per warpgroup
@@ -617,35 +635,45 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      const uint32_t v_smem = smem_u32(vslot);
+      const uint64_t v_desc = desc_advance(v_desc0, (uint32_t)(st * kSlotBytes));
+      bool live[kQTiles];
+      int bw[kQTiles];
 #pragma unroll
       for (int w = 0; w < kQTiles; ++w) {
-        if (i >= it.n_w[w]) continue;
+        live[w] = i < it.n_w[w];
         const int gw = gw0[w] + i;
-        const int b = gw & 1;
-        if (!warp_wait(&p_full[w * 2 + b], (gw >> 1) & 1)) return false;
-        tc_fence_after();
+        bw[w] = gw & 1;
+        if (!live[w]) continue;
+        if (!warp_wait(&p_full[w * 2 + bw[w]], (gw >> 1) & 1)) return false;
         if (i == 0 && items_w[w] > 0) {
           // O[w] still holds this warpgroup's previous item until its
           // epilogue has read it
           if (!warp_wait(&o_empty[w], (items_w[w] - 1) & 1)) return false;
-          tc_fence_after();
         }
-        if (lane == 0) {
-          const uint32_t s_col = tmem + kColS + (uint32_t)((2 * w + b) * kKeysTc);
-          const uint32_t o_col = tmem + kColO + (uint32_t)(w * kHDim);
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        // the two Q tiles' accumulation chains interleave, so each MMA's
+        // dependency on the previous one into the same O overlaps the other's
 #pragma unroll
-          for (int pg = 0; pg < kPagesTc; ++pg) {
-            // B = V rows of page pg: N = 128 dims in two 64-dim halves (LBO),
-            // K = 16 keys in two groups of 8 rows (SBO)
-            const uint64_t bdesc = smem_desc_sw128(v_smem + pg * 2048, kTileHalf, 1024);
+        for (int pg = 0; pg < kPagesTc; ++pg) {
+          // B = V rows of page pg: N = 128 dims in two 64-dim halves (LBO),
+          // K = 16 keys in two groups of 8 rows (SBO)
+          const uint64_t bdesc = desc_advance(v_desc, (uint32_t)(pg * 2048));
+#pragma unroll
+          for (int w = 0; w < kQTiles; ++w) {
+            if (!live[w]) continue;
+            const uint32_t s_col = tmem + kColS + (uint32_t)((2 * w + bw[w]) * kKeysTc);
+            const uint32_t o_col = tmem + kColO + (uint32_t)(w * kHDim);
             umma_ts(o_col, s_col + (uint32_t)(pg * 8), bdesc, kIdescPV, (i > 0 || pg > 0) ? 1u : 0u);
             if (kBF16) umma_ts(o_col, s_col + (uint32_t)(pg * 8 + 32), bdesc, kIdescPV, 1u);
           }
-          umma_commit(&pv_done[w * 2 + b]);
         }
-        __syncwarp();
+#pragma unroll
+        for (int w = 0; w < kQTiles; ++w)
+          if (live[w]) umma_commit(&pv_done[w * 2 + bw[w]]);
       }
+      __syncwarp();
       if (lane == 0) umma_commit(&v_empty[st]);
       __syncwarp();
       return true;
@@ -673,21 +701,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t k_smem = smem_u32(base + kOffK + st * kSlotBytes);
+          const uint64_t k_desc = desc_advance(k_desc0, (uint32_t)(st * kSlotBytes));
+          // the two Q tiles' 8-step chains interleave: an N = 64 product is
+          // short, so back-to-back MMAs into one accumulator would each wait
+          // for the previous one
 #pragma unroll
-          for (int w = 0; w < kQTiles; ++w) {
-            if (j >= it.n_w[w]) continue;
-            const int b = (gw0[w] + j) & 1;
-            const uint32_t q_smem = smem_u32(base + w * kQTileBytes);
+          for (int ks = 0; ks < 8; ++ks) {
+            const int half = ks >> 2, kk = ks & 3;
+            const uint64_t bdesc = desc_advance(k_desc, (uint32_t)(half * kTileHalf + kk * 32));
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const int half = ks >> 2, kk = ks & 3;
-              const uint64_t adesc = smem_desc_sw128(q_smem + half * kQHalf + kk * 32, 16, 1024);
-              const uint64_t bdesc = smem_desc_sw128(k_smem + half * kTileHalf + kk * 32, 16, 1024);
+            for (int w = 0; w < kQTiles; ++w) {
+              if (j >= it.n_w[w]) continue;
+              const int b = (gw0[w] + j) & 1;
+              const uint64_t adesc = desc_advance(q_desc0, (uint32_t)(w * kQTileBytes + half * kQHalf + kk * 32));
               umma_ss(tmem + kColS + (uint32_t)((2 * w + b) * kKeysTc), adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
             }
-            umma_commit(&s_full[w * 2 + b]);
           }
+#pragma unroll
+          for (int w = 0; w < kQTiles; ++w)
+            if (j < it.n_w[w]) umma_commit(&s_full[w * 2 + ((gw0[w] + j) & 1)]);
           umma_commit(&k_empty[st]);
           if (j == it.n_k - 1) umma_commit(q_empty);  // Q no longer read once these S are done
         }

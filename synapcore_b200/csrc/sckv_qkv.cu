@@ -463,6 +463,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t kIdesc = instr_desc_f16(kBF16, SM::kBN, false);
+    const uint64_t stage_desc0 = smem_desc_sw128(smem_u32(base), 16, 1024);  // stage 0's x tile
     bool ok = true;
     uint32_t gcount = 0;  // stages consumed
     int lt = 0;           // tiles of this CTA
@@ -484,15 +485,15 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a = smem_u32(base + st * SM::kStageBytes);
-          const uint32_t b = a + SM::kOffW;
+          // A = x rows (tokens), B = W rows (output dims), both K-major:
+          // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
+          const uint64_t adesc = desc_advance(stage_desc0, st * (uint32_t)SM::kStageBytes);
+          const uint64_t bdesc = desc_advance(adesc, (uint32_t)SM::kOffW);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            // A = x rows (tokens), B = W rows (output dims), both K-major:
-            // 128-byte rows, 8-row groups 1024 bytes apart; K = 16 is 32 bytes
-            const uint64_t bdesc = smem_desc_sw128(b + kk * 32, 16, 1024);
-            umma_ss(acc, smem_desc_sw128(a + kk * 32, 16, 1024), bdesc, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
-            if (kSplit) umma_ss(acc, smem_desc_sw128(a + SM::kOffLo + kk * 32, 16, 1024), bdesc, kIdesc, 1u);
+            const uint64_t bk = desc_advance(bdesc, (uint32_t)(kk * 32));
+            umma_ss(acc, desc_advance(adesc, (uint32_t)(kk * 32)), bk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+            if (kSplit) umma_ss(acc, desc_advance(adesc, (uint32_t)(SM::kOffLo + kk * 32)), bk, kIdesc, 1u);
           }
           umma_commit(&empty[st]);
         }
