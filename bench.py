@@ -606,6 +606,9 @@ def bench_ours(args, w_full, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_seconds)
+        rc = reference_code_baseline(w, budget_s=min(5.0, args.cpu_seconds))
+        if rc is not None:
+            res["cpu_baseline"]["reference_code"] = rc
     pool.close()
     return res
 
@@ -1710,6 +1713,54 @@ def cpu_baseline(w, budget_s: float = 15.0):
                       f"{w['batch'] * gbs * 1e9 / (w['layers'] * attn_bytes_per_launch(w, [T] * w['batch'])):.3f}"}
 
 
+def reference_code_baseline(w, budget_s: float = 5.0):
+    """The reference's own decode code, when an installed copy is importable
+    from baseline/_ref: ModularAttentionEngine.forward_numpy
+    (models/adapters.py:1148-1231) for one token of one sequence and one layer
+    at the workload's context, its fp16 cache growing by np.concatenate as in
+    the reference. The call includes the reference's q/k/v/o projections,
+    which the device metric does not count, so this is reported beside the
+    SDPA-only port, not in its place. None when no copy is installed."""
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "models" / "adapters.py").exists():
+        return None
+    sys.path.insert(0, str(ref))
+    try:
+        from models import adapters as ad
+    except Exception as e:  # the installed copy does not import here
+        return {"unavailable": f"baseline/_ref does not import: {type(e).__name__}: {e}"[:200]}
+    finally:
+        sys.path.remove(str(ref))
+    hq, hkv, d = w["hq"], w["hkv"], w["d"]
+    hidden = hq * d
+    T = mean_ctx(w)
+    cfg = {"model_type": "olmoe", "num_hidden_layers": 1, "num_experts": 8, "num_experts_per_tok": 2,
+           "hidden_size": hidden, "intermediate_size": hidden * 2, "num_attention_heads": hq,
+           "num_key_value_heads": hkv, "vocab_size": 32000, "rms_norm_eps": 1e-5, "rope_theta": 10000.0}
+    eng = ad.ModularAttentionEngine(ad.OLMoEAdapter(cfg).spec)
+    rng = np.random.default_rng(0)
+    wq = (rng.standard_normal((hidden, hidden)) * 0.02).astype(np.float16)
+    wk = (rng.standard_normal((hkv * d, hidden)) * 0.02).astype(np.float16)
+    wv = (rng.standard_normal((hkv * d, hidden)) * 0.02).astype(np.float16)
+    wo = (rng.standard_normal((hidden, hidden)) * 0.02).astype(np.float16)
+    kk = [rng.standard_normal((1, hkv, T, d)).astype(np.float16)]
+    vv = [rng.standard_normal((1, hkv, T, d)).astype(np.float16)]
+    x = rng.standard_normal((1, 1, hidden)).astype(np.float32)
+    calls, nbytes, t0 = 0, 0, time.perf_counter()
+    while True:
+        ctx = kk[0].shape[2] + 1
+        eng.forward_numpy(x, wq, wk, wv, wo, kv_cache_k=kk, kv_cache_v=vv, layer_idx=0, pos_offset=ctx - 1)
+        calls += 1
+        nbytes += ctx * hkv * d * 2 * 2
+        el = time.perf_counter() - t0
+        if el >= budget_s or calls >= 2000:
+            break
+    gbs = nbytes / el / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "reference",
+            "sample": f"forward_numpy, 1 layer x 1 seq x ctx {T} (fp16 cache; includes its q/k/v/o "
+                      f"projections and concatenate append), {calls} calls in {el:.1f}s"}
+
+
 def cpu_baseline_prefill(w, budget_s: float = 15.0):
     """The reference's NumPy causal prompt pass (oracle restatement of
     models/adapters.py:1209-1229 with its -1e9 mask) on one layer of one
@@ -1808,6 +1859,7 @@ def bench_reference(args, w, world, rank):
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"per step: 1 layer x 8 seqs x ctx {mean_ctx(w)}, ~{args.cpu_seconds / max(1, args.steps):.1f}s"},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_code": reference_code_baseline(w, budget_s=min(5.0, args.cpu_seconds)),
     }
 
 
