@@ -414,6 +414,18 @@ def advance(s):
         s["ctx_host"] = s["ctx_host"] + 1
 
 
+def exchange_layer(s, l, pl, q, out_full=None):
+    """KV-head-sharded layer with the exchange fused into the decode: this
+    rank's heads go straight into every rank's full-head buffer, then a
+    device wait for every rank's flag of this (step, layer)."""
+    ex = s["exchange"]
+    s["epoch"] += 1
+    ex.decode(l, q, s["bt"], s["ctx"], s["epoch"], phys_layer=pl)
+    ex.wait(s["epoch"])
+    if out_full is not None:
+        out_full.copy_(ex.output(l, q.shape[0]))
+
+
 def run_step(w, s, attn_events=None):
     pool = s["pool"]
     gather = s.get("gather")
@@ -423,7 +435,10 @@ def run_step(w, s, attn_events=None):
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
-        pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
+        if "exchange" in s:
+            exchange_layer(s, l, pl, s["q"][l])
+        else:
+            pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
@@ -436,10 +451,16 @@ def bench_ours(args, w_full, world, rank, local):
     w = local_workload(w_full, world, args.layout)
     s = build_state(w, rank, grow_steps=max(args.steps, args.warmup))
     pool = s["pool"]
-    if args.layout == "heads" and world > 1:
+    if args.layout == "heads" and world > 1 and args.exchange == "nccl":
         from synapcore_b200.distributed import HeadShardedOutput
 
         s["gather"] = HeadShardedOutput(world)
+        s["full"] = torch.empty((w["layers"], w["batch"], w_full["hq"], w["d"]), dtype=w["qdt"], device="cuda")
+    elif args.layout == "heads" and world > 1:
+        from synapcore_b200.distributed import HeadShardedExchange
+
+        s["exchange"] = HeadShardedExchange(pool, world, rank, w["layers"], w["batch"], w_full["hq"], w["qdt"])
+        s["epoch"] = 0
         s["full"] = torch.empty((w["layers"], w["batch"], w_full["hq"], w["d"]), dtype=w["qdt"], device="cuda")
     for _ in range(args.warmup):
         run_step(w, s)
@@ -485,7 +506,7 @@ def bench_ours(args, w_full, world, rank, local):
     # computes (two device buffers each); every step still moves its own
     # inputs and reads back its own result inside the timed region.
     L = w["layers"]
-    res_t = s["full"] if "gather" in s else s["out"]
+    res_t = s["full"] if ("gather" in s or "exchange" in s) else s["out"]
     h_q = s["q"].cpu().pin_memory()
     h_k = s["kn"].cpu().pin_memory()
     h_v = s["vn"].cpu().pin_memory()
@@ -515,6 +536,9 @@ def bench_ours(args, w_full, world, rank, local):
         for l in range(L):
             pl = l % s["n_phys"]
             pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=pl)
+            if "exchange" in s:
+                exchange_layer(s, l, pl, d_q[l], out_full=d_res[b][l])
+                continue
             pool.decode_attn(pl, d_q[l], s["bt"], s["ctx"], out=d_out[b][l], workspace=s["ws"])
             if "gather" in s:
                 d_res[b][l].copy_(s["gather"].gather(d_out[b][l]))
@@ -588,7 +612,10 @@ def bench_ours(args, w_full, world, rank, local):
                            if s["n_phys"] < w["layers"] else ""),
             "global_batch": w["batch"] if (args.layout == "heads" and world > 1) else world * w["batch"],
             "seq_len": ctx_desc(w_full),
-            "parallelism": (f"kv-head-sharded x{world} (NCCL all-gather of outputs per layer)"
+            "parallelism": ((f"kv-head-sharded x{world} (NCCL all-gather of outputs per layer)"
+                             if args.exchange == "nccl" else
+                             f"kv-head-sharded x{world} (outputs stored into every rank's buffer by the "
+                             f"decode kernel over NVLink, one flag wait per layer)")
                             if (args.layout == "heads" and world > 1)
                             else f"sequence-sharded x{world} (independent pools)"),
             "l2": "inputs larger than L2 (KV per layer launch >> 126 MB)",
@@ -609,6 +636,15 @@ def bench_ours(args, w_full, world, rank, local):
         rc = reference_code_baseline(w, budget_s=min(5.0, args.cpu_seconds))
         if rc is not None:
             res["cpu_baseline"]["reference_code"] = rc
+    if "exchange" in s:
+        # every rank's writes into this rank's buffer ended before its last
+        # wait; the barrier keeps all ranks' mappings alive until all are done
+        torch.cuda.synchronize()
+        barrier(world)
+        st = s["exchange"].status()
+        if st[0] != 0:
+            raise RuntimeError(f"exchange status {st}")
+        s["exchange"].close()
     pool.close()
     return res
 
@@ -1874,6 +1910,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layout", choices=["seq", "heads"], default="seq",
                     help="multi-GPU layout: sequence sharding (default) or KV-head sharding")
+    ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
+                    help="KV-head sharding's output exchange: fused into the decode over NVLink peer stores "
+                         "(default) or a separate NCCL all-gather")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     world, rank, local = dist_setup(args.gpus)

@@ -52,6 +52,7 @@ extern "C" {
 #define SCKV_DTYPE_F32       4   /* query / output / source type only */
 
 typedef struct sckv_pool sckv_pool;
+typedef struct sckv_exchange sckv_exchange;
 
 /* ========================================================================== */
 /* Pool lifetime                                                               */
@@ -309,6 +310,56 @@ SCKV_API int sckv_o_proj(sckv_pool* pool, const void* x, const void* x_lo,
 /* Workspace sckv_o_proj needs for this call shape (0 on bad arguments). */
 SCKV_API size_t sckv_o_proj_workspace_bytes(const sckv_pool* pool,
                      int n_tokens, int in_features, int out_features);
+
+/* ========================================================================== */
+/* KV-head-sharded output exchange (no reference counterpart: the reference  */
+/* has no multi-process code; this is the optional layout of a multi-GPU box) */
+/* ========================================================================== */
+/* In the KV-head-sharded layout rank r of `world` holds every sequence but
+ * only kv heads [r*Hkv/world, (r+1)*Hkv/world) and the q heads that read them.
+ * The exchange object owns, in this GPU's memory, a full-head output buffer
+ * of out_bytes and a flag word per source rank; every rank maps every other
+ * rank's buffer and flags through CUDA IPC (one process per GPU, one box).
+ * Peer memory is reached by ordinary stores and flag loads/stores only.
+ *
+ * Set-up: sckv_exchange_create on each rank, sckv_exchange_ipc_handles
+ * (128 bytes: buffer handle, flags handle), exchange those bytes between the
+ * ranks (e.g. an all-gather of the process group), sckv_exchange_open_peer
+ * for every other rank. world <= 8. */
+SCKV_API int sckv_exchange_create(int device, int world, int rank, size_t out_bytes,
+                         sckv_exchange** out);
+SCKV_API void* sckv_exchange_buffer(const sckv_exchange* ex);
+SCKV_API int sckv_exchange_ipc_handles(const sckv_exchange* ex, uint8_t* out_handles);
+SCKV_API int sckv_exchange_open_peer(sckv_exchange* ex, int peer, const uint8_t* handles);
+SCKV_API void sckv_exchange_destroy(sckv_exchange* ex);
+
+/* sckv_decode_attn for this rank's heads (q [n_seqs][num_q_heads][128] holds
+ * q heads rank*num_q_heads .. +num_q_heads-1, the pool this rank's kv heads),
+ * whose epilogue stores output element (b, h, d) at element
+ * out_offset + (b * num_q_heads_total + rank * num_q_heads + h) * 128 + d of
+ * EVERY rank's exchange buffer (out_dtype F32 / F16 / BF16; num_q_heads_total
+ * = world * num_q_heads), then, once those stores are complete, sets this
+ * rank's flag to `epoch` (non-zero, increasing per call, the same on every
+ * rank for the same layer and step) on every rank. Replaces the decode +
+ * NCCL all-gather pair of the layout. All ranks' buffers must be open. */
+SCKV_API int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int layer,
+                             const void* q, int q_dtype, int num_q_heads,
+                             const int32_t* block_table, int64_t bt_stride,
+                             int max_blocks, const int32_t* ctx_lens, int n_seqs,
+                             float scale, int out_dtype, int64_t out_offset,
+                             int num_q_heads_total, uint32_t epoch,
+                             void* workspace, size_t workspace_bytes,
+                             int chunk_pages, void* stream);
+
+/* Stream-ordered wait until every rank's flag here reached `epoch` (then the
+ * full-head output of that call is in this rank's buffer for every kernel
+ * launched after it on `stream`). Bounded: after limit_us (0 = 2 s) the
+ * kernel records SCKV_ERR_TIMEOUT (detail = the late rank) in the exchange's
+ * status word and returns. */
+SCKV_API int sckv_exchange_wait(sckv_exchange* ex, uint32_t epoch, unsigned limit_us, void* stream);
+
+/* The exchange's status word (code, detail, kernel, count); clear != 0 resets it. */
+SCKV_API int sckv_exchange_status(const sckv_exchange* ex, int32_t out[4], int clear, void* stream);
 
 /* Fixed per-GPU scratch behind sckv_decode_attn_noalloc (4 MiB). */
 #define SCKV_NOALLOC_SCRATCH_BYTES (4u << 20)

@@ -105,6 +105,16 @@ _SIGNATURES = [
     ("sckv_release_pages", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     ("sckv_evict_lru", c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     ("sckv_evict_to_watermark", c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
+    ("sckv_exchange_create", c_int, [c_int, c_int, c_int, c_size_t, POINTER(c_void_p)]),
+    ("sckv_exchange_buffer", c_void_p, [c_void_p]),
+    ("sckv_exchange_ipc_handles", c_int, [c_void_p, c_void_p]),
+    ("sckv_exchange_open_peer", c_int, [c_void_p, c_int, c_void_p]),
+    ("sckv_exchange_destroy", None, [c_void_p]),
+    ("sckv_decode_attn_exchange", c_int,
+     [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p, c_int, c_float, c_int,
+      c_int64, c_int, c_uint32, c_void_p, c_size_t, c_int, c_void_p]),
+    ("sckv_exchange_wait", c_int, [c_void_p, c_uint32, c_uint32, c_void_p]),
+    ("sckv_exchange_status", c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_reserve_decode", c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p]),
     ("sckv_alloc_state", c_int, [c_void_p, POINTER(c_int64), c_void_p]),
     ("sckv_get_status", c_int, [c_void_p, POINTER(c_int32), c_void_p]),

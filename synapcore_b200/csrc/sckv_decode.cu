@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 2 ? 3 : (G == 4 ? 2 : 1)))
       const int hq = h * G + g;
       if (nsplits == 1) {
         const float o = (L > 0.f) ? O / L : 0.f;
-        sckv_store_from_float(p.out, ((int64_t)b * p.hq + hq) * kHD + d, p.out_dtype, o);
+        store_out(p, b, hq, d, o);
       } else {
         const int64_t slot = ((int64_t)b * p.hq + hq) * p.max_splits + split;
         p.part_acc[slot * kHD + d] = O;
@@ -413,9 +413,8 @@ __global__ void combine_kernel(const DecodeParams p) {
   ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
   const int npages = (ctx + SCKV_PAGE_TOKENS - 1) / SCKV_PAGE_TOKENS;
   const int ns = (npages + p.chunk_pages - 1) / p.chunk_pages;
-  const int64_t out_idx = ((int64_t)b * p.hq + hq) * kHD + d;
   if (ns == 0) {
-    sckv_store_from_float(p.out, out_idx, p.out_dtype, 0.f);
+    store_out(p, b, hq, d, 0.f);
     return;
   }
   if (ns == 1) return;
@@ -432,7 +431,7 @@ __global__ void combine_kernel(const DecodeParams p) {
       O = fmaf(p.part_acc[(base + s) * kHD + d], e, O);
     }
   }
-  sckv_store_from_float(p.out, out_idx, p.out_dtype, L > 0.f ? O / L : 0.f);
+  store_out(p, b, hq, d, L > 0.f ? O / L : 0.f);
 }
 
 }  // namespace
@@ -553,10 +552,61 @@ int validate_decode_args(const sckv_pool* pool, int layer, const void* q, int q_
 
 }  // namespace
 
+namespace {
+
+// Where an exchange decode writes: element offset of the layer's slice in
+// every rank's full-head buffer, the full head count, this rank's first head.
+struct ExchangeTarget {
+  const sckv_exchange* ex;
+  int64_t out_off;
+  int hq_total;
+  int head0;
+};
+
+int decode_attn_impl(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                     const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
+                     int n_seqs, float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                     int chunk_pages, void* stream, const ExchangeTarget* xt);
+
+}  // namespace
+
 extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
                                 const int32_t* block_table, int64_t bt_stride, int max_blocks,
                                 const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
                                 void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+  return decode_attn_impl(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens, n_seqs,
+                          scale, out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, nullptr);
+}
+
+extern "C" int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int layer, const void* q, int q_dtype,
+                                         int num_q_heads, const int32_t* block_table, int64_t bt_stride,
+                                         int max_blocks, const int32_t* ctx_lens, int n_seqs, float scale,
+                                         int out_dtype, int64_t out_offset, int num_q_heads_total, uint32_t epoch,
+                                         void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+  if (pool == nullptr || ex == nullptr || ex->device != pool->device) return SCKV_ERR_INVALID_ARG;
+  for (int r = 0; r < ex->world; ++r)
+    if (!ex->opened[r]) return SCKV_ERR_INVALID_ARG;  // every peer's buffers must be mapped
+  const int head0 = ex->rank * num_q_heads;
+  if (num_q_heads <= 0 || num_q_heads_total != ex->world * num_q_heads || out_offset < 0 || epoch == 0)
+    return SCKV_ERR_INVALID_ARG;
+  const size_t esz = out_dtype == SCKV_DTYPE_F32 ? 4 : 2;
+  const int64_t end = out_offset + (int64_t)n_seqs * num_q_heads_total * kHD;
+  if (n_seqs <= 0 || (size_t)end * esz > ex->out_bytes) return SCKV_ERR_INVALID_ARG;
+  if (((out_offset * (int64_t)esz) & 15) != 0) return SCKV_ERR_ALIGNMENT;
+  const ExchangeTarget xt{ex, out_offset, num_q_heads_total, head0};
+  int rc = decode_attn_impl(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens,
+                            n_seqs, scale, ex->out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, &xt);
+  if (rc != SCKV_OK) return rc;
+  SCKV_DEVICE_GUARD(pool->device);
+  return launch_exchange_signal(ex, epoch, as_stream(stream));
+}
+
+namespace {
+
+int decode_attn_impl(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                     const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
+                     int n_seqs, float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                     int chunk_pages, void* stream, const ExchangeTarget* xt) {
   const int vrc = validate_decode_args(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks,
                                       ctx_lens, n_seqs, out, out_dtype);
   if (vrc != SCKV_OK) return vrc;
@@ -588,6 +638,13 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
   prm.q_dtype = q_dtype;
   prm.out_dtype = out_dtype;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  if (xt != nullptr) {
+    prm.n_peer = xt->ex->world;
+    for (int r = 0; r < xt->ex->world; ++r) prm.peer_out[r] = xt->ex->peer_out[r];
+    prm.out_hq_total = xt->hq_total;
+    prm.out_head0 = xt->head0;
+    prm.out_off = xt->out_off;
+  }
   const int G = num_q_heads / pool->num_kv_heads;
   cudaStream_t s = as_stream(stream);
   SCKV_DEVICE_GUARD(pool->device);
@@ -603,6 +660,8 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
     default: return SCKV_ERR_UNSUPPORTED;
   }
 }
+
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Decode attention for callers that cannot allocate device memory.

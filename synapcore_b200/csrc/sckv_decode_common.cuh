@@ -8,6 +8,7 @@ namespace sckv_detail {
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kHD = 128;  // head_dim handled by this kernel
+constexpr int kMaxExchangeRanks = 8;  // ranks of one box in the KV-head-sharded exchange
 
 struct DecodeParams {
   const uint8_t* pool;
@@ -31,7 +32,26 @@ struct DecodeParams {
   int q_dtype;
   int out_dtype;
   float scale_log2;
+  // KV-head-sharded exchange (n_peer > 0): the output of (sequence b, local
+  // q head h) goes to element out_off + (b * out_hq_total + out_head0 + h) *
+  // HD of every rank's full-head buffer peer_out[r] (plain stores over
+  // NVLink; peer_out[rank] is the local buffer) instead of `out`
+  void* peer_out[kMaxExchangeRanks];
+  int n_peer;
+  int out_hq_total;
+  int out_head0;
+  int64_t out_off;
 };
+
+// One output element of (sequence b, q head hq, dim d).
+__device__ __forceinline__ void store_out(const DecodeParams& p, int b, int hq, int d, float v) {
+  if (p.n_peer == 0) {
+    sckv_store_from_float(p.out, ((int64_t)b * p.hq + hq) * kHD + d, p.out_dtype, v);
+    return;
+  }
+  const int64_t idx = p.out_off + ((int64_t)b * p.out_hq_total + p.out_head0 + hq) * kHD + d;
+  for (int r = 0; r < p.n_peer; ++r) sckv_store_from_float(p.peer_out[r], idx, p.out_dtype, v);
+}
 
 __device__ __forceinline__ int clamp_ctx(const DecodeParams& p, int b, bool report) {
   int ctx = __ldg(p.ctx_lens + b);

@@ -546,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
         }
         const int hq = (h0 + hh) * G + q;
         if (nsplits == 1) {
-          sckv_store_from_float(p.out, ((int64_t)b * p.hq + hq) * kHD + d, p.out_dtype, (L > 0.f) ? O / L : 0.f);
+          store_out(p, b, hq, d, (L > 0.f) ? O / L : 0.f);
         } else {
           const int64_t slot = ((int64_t)b * p.hq + hq) * p.max_splits + split;
           p.part_acc[slot * kHD + d] = O;

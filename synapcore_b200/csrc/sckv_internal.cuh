@@ -31,6 +31,7 @@ enum SckvKernelId : int32_t {
   KID_PREFILL = 13,
   KID_QKV = 14,
   KID_SELFTEST = 15,
+  KID_EXCHANGE = 16,
 };
 
 // Allocator control words (int64, device).
@@ -95,6 +96,29 @@ struct sckv_pool {
   alignas(64) unsigned char tmap_kv2[128];
   int tmap2_ready;
 };
+
+// KV-head-sharded output exchange between the ranks of one box (one process
+// per GPU): a full-head output buffer and an epoch flag per source rank in
+// this GPU's memory, plus the CUDA IPC mappings of every peer's buffer and
+// flags (peer_out[rank] / peer_flags[rank] are the local ones).
+struct sckv_exchange {
+  int device;
+  int world;
+  int rank;
+  void* out;
+  size_t out_bytes;
+  uint32_t* flags;   // [world]: the last epoch each rank signalled here
+  int32_t* status;   // [4]: code, detail, kernel, count (as a pool's status word)
+  void* peer_out[8];
+  uint32_t* peer_flags[8];
+  int opened[8];
+};
+
+namespace sckv_detail {
+// Stream-ordered after a rank's exchange decode: flags[rank] = epoch on every
+// rank (release, system scope), once the decode's peer stores are complete.
+int launch_exchange_signal(const sckv_exchange* ex, uint32_t epoch, cudaStream_t stream);
+}  // namespace sckv_detail
 
 // Next work counter of the pool for one launch (thread-safe on the host).
 static inline unsigned long long* sckv_take_work_counter(const sckv_pool* p) {

@@ -917,7 +917,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
       if (lane == 0) *abort_flag = 1;
     }
-  }
   } else if (warp >= kWarpQ0 && !p.q_tma) {
     // ------------------------------------------------------------ Q loaders
     // q is not in the MMA's element type, so no TMA copy can place it: these

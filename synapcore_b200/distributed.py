@@ -6,9 +6,13 @@ needs no communication — the aggregate is just the sum over ranks.
 
 KV-head sharding (optional): every rank holds all sequences but only kv heads
 [r*Hkv/n, (r+1)*Hkv/n) and the query heads that read them; after each
-layer's attention the per-rank outputs [B, Hq/n, D] are all-gathered (NCCL
-over NVLink) into [B, Hq, D]. The all-gather lands in a local buffer, so no
-kernel ever reads another GPU's memory.
+layer's attention every rank needs the full [B, Hq, D] output. Two ways:
+`HeadShardedExchange` (the default in bench.py) has the decode kernel's
+epilogue store every output element straight into every rank's full-head
+buffer over NVLink (CUDA IPC mappings, plain stores) and flag the layer done
+on every rank, so there is no separate collective; `HeadShardedOutput` is the
+NCCL all-gather of the per-rank [B, Hq/n, D] outputs into a local buffer.
+Neither reads another GPU's memory with TMA or multicast.
 
 The reference has no multi-process code; these layouts are the B200 side's
 way of scaling one box (8 GPUs).
@@ -68,3 +72,111 @@ class HeadShardedOutput:
             self._buf = torch.empty(shape, dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(self._buf, local, group=self.group)
         return self._buf.view(self.world, B, hq_local, D).permute(1, 0, 2, 3).reshape(B, self.world * hq_local, D)
+
+
+class HeadShardedExchange:
+    """KV-head-sharded decode whose output exchange is fused into the kernel.
+
+    Every rank owns an exchange buffer [layers, max_seqs, Hq, D] (out_dtype)
+    in its own memory; the ranks swap CUDA IPC handles once through `group`
+    and map each other's buffers. `decode(layer, q_local, ...)` runs this
+    rank's heads with sckv_decode_attn_exchange, which writes the rank's
+    slice of every output row into every rank's buffer and then raises this
+    rank's flag for the call's epoch on every rank; `wait(epoch)` queues a
+    bounded device wait for all ranks' flags, after which `output(layer, B)`
+    holds the full [B, Hq, D] result. Epochs are step * layers + layer + 1,
+    identical on all ranks. A layer's slice is rewritten only in the next
+    step, after this rank has waited for every rank's signal of every later
+    layer, so no rank overwrites a slice another still reads."""
+
+    def __init__(self, pool, world: int, rank: int, layers: int, max_seqs: int, num_q_heads_total: int,
+                 out_dtype: torch.dtype = torch.float32, group: Optional["torch.distributed.ProcessGroup"] = None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _native as N
+        from .pool import torch_dtype_code
+
+        self.N, self.lib, self.pool = N, N.lib(), pool
+        self.world, self.rank = int(world), int(rank)
+        self.layers, self.max_seqs, self.hq_total = int(layers), int(max_seqs), int(num_q_heads_total)
+        if self.hq_total % self.world:
+            raise ValueError("query heads must split evenly over the ranks")
+        self.out_dtype = out_dtype
+        self.code = torch_dtype_code(out_dtype)
+        self.esize = torch.empty((), dtype=out_dtype).element_size()
+        self.slice_elems = self.max_seqs * self.hq_total * pool.head_dim
+        h = ctypes.c_void_p()
+        N.check(self.lib.sckv_exchange_create(pool.device.index, self.world, self.rank,
+                                              self.layers * self.slice_elems * self.esize, ctypes.byref(h)),
+                "sckv_exchange_create")
+        self.handle = h
+        mine = (ctypes.c_uint8 * 128)()
+        N.check(self.lib.sckv_exchange_ipc_handles(self.handle, mine), "sckv_exchange_ipc_handles")
+        allh = [None] * self.world
+        dist.all_gather_object(allh, bytes(mine), group=group)
+        for r, hb in enumerate(allh):
+            if r != self.rank:
+                buf = (ctypes.c_uint8 * 128).from_buffer_copy(hb)
+                N.check(self.lib.sckv_exchange_open_peer(self.handle, r, buf), "sckv_exchange_open_peer")
+        ptr = int(self.lib.sckv_exchange_buffer(self.handle))
+        self._view = _device_view(ptr, self.layers * self.slice_elems, out_dtype, pool.device)
+        self._ws: Optional[torch.Tensor] = None
+
+    def decode(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor, epoch: int,
+               phys_layer: Optional[int] = None, scale: Optional[float] = None, chunk_pages: int = 0,
+               stream: Optional[torch.cuda.Stream] = None) -> None:
+        from .pool import _stream_ptr, torch_dtype_code
+
+        q = q.contiguous()
+        B, hq, d = q.shape
+        if B > self.max_seqs or hq * self.world != self.hq_total:
+            raise ValueError("q must be [<= max_seqs, Hq / world, D]")
+        mb = block_table.shape[1]
+        need = self.pool.decode_workspace_bytes(B, hq, mb, chunk_pages)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 16), dtype=torch.uint8, device=self.pool.device)
+        scale = float(d) ** -0.5 if scale is None else float(scale)
+        pl = layer if phys_layer is None else phys_layer
+        self.N.check(self.lib.sckv_decode_attn_exchange(
+            self.pool.handle, self.handle, pl, q.data_ptr(), torch_dtype_code(q.dtype), hq, block_table.data_ptr(),
+            block_table.stride(0), mb, ctx_lens.data_ptr(), B, scale, self.code, layer * self.slice_elems,
+            self.hq_total, int(epoch), self._ws.data_ptr(), self._ws.numel(), chunk_pages, _stream_ptr(stream)),
+            "sckv_decode_attn_exchange")
+
+    def wait(self, epoch: int, limit_us: int = 0, stream: Optional[torch.cuda.Stream] = None) -> None:
+        from .pool import _stream_ptr
+
+        self.N.check(self.lib.sckv_exchange_wait(self.handle, int(epoch), int(limit_us), _stream_ptr(stream)),
+                     "sckv_exchange_wait")
+
+    def output(self, layer: int, n_seqs: int) -> torch.Tensor:
+        """The full [n_seqs, Hq, D] output of `layer` (valid after wait)."""
+        d = self.pool.head_dim
+        base = layer * self.slice_elems
+        return self._view[base: base + n_seqs * self.hq_total * d].view(n_seqs, self.hq_total, d)
+
+    def status(self, clear: bool = False):
+        import ctypes
+
+        arr = (ctypes.c_int32 * 4)()
+        self.N.check(self.lib.sckv_exchange_status(self.handle, arr, 1 if clear else 0, None), "sckv_exchange_status")
+        return tuple(int(x) for x in arr)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None:
+            self.lib.sckv_exchange_destroy(self.handle)
+            self.handle = None
+
+
+def _device_view(ptr: int, numel: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A tensor over device memory the library owns (no copy, no ownership)."""
+    esize = torch.empty((), dtype=dtype).element_size()
+
+    class _Mem:
+        __cuda_array_interface__ = {
+            "shape": (numel * esize,), "typestr": "|u1", "data": (ptr, False), "version": 3, "strides": None,
+        }
+
+    return torch.as_tensor(_Mem(), device=device).view(dtype)

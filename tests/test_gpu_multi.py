@@ -89,3 +89,136 @@ def test_head_sharded_decode_equals_single_gpu(tmp_path):
         ref = full.cpu().numpy()
         got = sharded[layer]
         assert np.max(np.abs(got - ref)) <= 2e-3 * np.max(np.abs(ref))
+
+
+def _exchange_worker(rank, world, port, out_path, steps=3):
+    """KV-head-sharded decode with the exchange fused into the kernel: every
+    rank runs its heads, waits for every rank's flag, and rank 0 records the
+    full output of each (step, layer)."""
+    import torch.distributed as dist
+
+    from synapcore_b200.distributed import HeadShardedExchange, head_range, query_head_range
+    from synapcore_b200.pool import KVPool
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    ex = None
+    try:
+        L, hq, hkv, D, P, ctx, k, v, bt, q = _case()
+        kvr = head_range(hkv, world, rank)
+        qr = query_head_range(hq, hkv, world, rank)
+        pool = KVPool(L, len(kvr), D, P, "fp16", device=dev)
+        ids = torch.arange(P, dtype=torch.int32, device=dev)
+        pool.write_pages(ids, torch.from_numpy(np.ascontiguousarray(k[:, :, kvr.start:kvr.stop])).to(dev),
+                         torch.from_numpy(np.ascontiguousarray(v[:, :, kvr.start:kvr.stop])).to(dev))
+        bt_d = torch.from_numpy(bt).to(dev)
+        ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+        ex = HeadShardedExchange(pool, world, rank, L, len(ctx), hq, torch.float32)
+        outs = []
+        for step in range(steps):
+            # each step scales q differently, so a stale slice would show
+            q_d = (torch.from_numpy(np.ascontiguousarray(q[:, qr.start:qr.stop])) * (1.0 + 0.25 * step)).to(dev)
+            for layer in range(L):
+                epoch = step * L + layer + 1
+                ex.decode(layer, q_d, bt_d, ctx_d, epoch)
+                ex.wait(epoch)
+                outs.append(ex.output(layer, len(ctx)).clone())
+        torch.cuda.synchronize()
+        pool.raise_on_status()
+        assert ex.status()[0] == 0
+        if rank == 0:
+            np.save(out_path, torch.stack(outs).cpu().numpy())
+        dist.barrier()
+    finally:
+        if ex is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_head_sharded_exchange_equals_single_gpu(tmp_path):
+    """Two ranks, fused NVLink exchange: every (step, layer) output equals the
+    single-GPU decode of all heads."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from synapcore_b200.pool import KVPool
+
+    out = tmp_path / "exchange.npy"
+    steps = 3
+    mp.start_processes(_exchange_worker, args=(2, _free_port(), str(out), steps), nprocs=2, join=True,
+                       start_method="spawn")
+    got_all = np.load(out)
+    L, hq, hkv, D, P, ctx, k, v, bt, q = _case()
+    dev = torch.device("cuda", 0)
+    pool = KVPool(L, hkv, D, P, "fp16", device=dev)
+    pool.write_pages(torch.arange(P, dtype=torch.int32, device=dev), torch.from_numpy(k).to(dev),
+                     torch.from_numpy(v).to(dev))
+    bt_d = torch.from_numpy(bt).to(dev)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    i = 0
+    for step in range(steps):
+        qs = (torch.from_numpy(q) * (1.0 + 0.25 * step)).to(dev)
+        for layer in range(L):
+            ref = pool.decode_attn(layer, qs, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
+            assert np.max(np.abs(got_all[i] - ref)) <= 2e-3 * np.max(np.abs(ref)), (step, layer)
+            i += 1
+
+
+def test_exchange_single_rank_and_bounded_wait(cuda_device):
+    """One rank (its own buffer is the only target): the exchange decode
+    equals sckv_decode_attn bit for bit in fp32, for MHA and GQA pools; a wait
+    for an epoch nobody signals gives up after its limit, records
+    SCKV_ERR_TIMEOUT (detail = the late rank) and leaves the context usable."""
+    import torch.distributed as dist
+
+    from synapcore_b200 import _native as N
+    from synapcore_b200.distributed import HeadShardedExchange
+    from synapcore_b200.pool import KVPool
+
+    own_group = not dist.is_initialized()
+    if own_group:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        for hq, hkv in ((16, 16), (16, 4)):
+            L, D, P = 2, 128, 96
+            rng = np.random.default_rng(3)
+            ctx = [37, 700, 513, 16, 1]
+            mb = max((c + 15) // 16 for c in ctx)
+            bt = torch.from_numpy(np.stack([rng.choice(P, size=mb, replace=False) for _ in ctx]).astype(np.int32))
+            pool = KVPool(L, hkv, D, P, "fp16", device=cuda_device)
+            kv = torch.from_numpy(rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)).to(cuda_device)
+            pool.write_pages(torch.arange(P, dtype=torch.int32, device=cuda_device), kv, kv * 0.5)
+            bt_d = bt.to(cuda_device)
+            ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+            q = torch.from_numpy(rng.standard_normal((len(ctx), hq, D)).astype(np.float16)).to(cuda_device)
+            ex = HeadShardedExchange(pool, 1, 0, L, 8, hq, torch.float32)
+            for layer in range(L):
+                ex.decode(layer, q, bt_d, ctx_d, epoch=layer + 1)
+                ex.wait(layer + 1)
+                ref = pool.decode_attn(layer, q, bt_d, ctx_d, out_dtype=torch.float32)
+                torch.cuda.synchronize()
+                assert torch.equal(ex.output(layer, len(ctx)), ref)
+            assert ex.status()[0] == 0
+            ex.wait(99, limit_us=20000)  # nothing will ever signal epoch 99
+            torch.cuda.synchronize()
+            code, detail, kernel, _ = ex.status(clear=True)
+            assert code == N.SCKV_ERR_TIMEOUT and detail == 0
+            assert ex.status()[0] == 0
+            pool.raise_on_status()
+            # the context still works
+            again = pool.decode_attn(0, q, bt_d, ctx_d, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.isfinite(again).all()
+            ex.close()
+            pool.close()
+    finally:
+        if own_group:
+            dist.destroy_process_group()
