@@ -11,8 +11,8 @@
 // persistent CTA per SM (512 TMEM columns) claims items from a work counter;
 // 16 warps:
 //   warps 0, 3  claim items (warp 0), load the item's Q (one TMA box per
-//              64-dim half and tile when q has the MMA's type, else warps
-//              13-15 convert it) and stream K: 4 pages (64 keys) per
+//              64-dim half and tile when q has the pool's type, else the
+//              softmax warps write it) and stream K: 4 pages (64 keys) per
 //              tile, one 2 KiB box per (page, 64-dim half), 128-byte swizzle,
 //              into a 4-slot ring laid out as the UMMA K-major canonical tile
 //              (consecutive pages are consecutive rows); each warp copies two
@@ -58,12 +58,10 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;
 constexpr uint32_t kColO = 256;
 
-// warps: 0 claims items, loads Q (TMA) and half of each K tile; 3 the other
-// half of K; 2 and 12 the two halves of V; 1 issues the MMAs; 4-7 and 8-11
-// are the softmax warpgroups of Q tiles 0 and 1; 13-15 convert Q into shared
-// memory when q is not in the MMA's type (else idle)
-constexpr int kWarpK0 = 0, kWarpMma = 1, kWarpV0 = 2, kWarpK1 = 3, kWarpV1 = 12, kWarpQ0 = 13;
-constexpr int kQLoaderThreads = 3 * 32;
+// warps: 0 claims items, loads Q and half of each K tile; 3 the other half
+// of K; 2 and 12 the two halves of V; 1 issues the MMAs; 4-7 and 8-11 are
+// the softmax warpgroups of Q tiles 0 and 1; 13-15 idle
+constexpr int kWarpK0 = 0, kWarpMma = 1, kWarpV0 = 2, kWarpK1 = 3, kWarpV1 = 12;
 
 constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of a Q tile: 16 KiB
 constexpr int kQTileBytes = 2 * kQHalf;
@@ -250,7 +248,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   // parity wait is unambiguous however rarely the thread waits on it.
   uint64_t* pv_done = p_full + 4;
   uint64_t* o_empty = pv_done + 4;              // [w] warpgroup w's O was read out (128 threads)
-  uint64_t* q_full = o_empty + 2;               // Q of the item in shared memory (TMA, or the 96 Q-loader threads)
+  uint64_t* q_full = o_empty + 2;               // Q of the item in shared memory (TMA, or 256 softmax threads)
   uint64_t* q_empty = q_full + 1;               // every S of the item finished (commit): Q may be replaced
   uint64_t* mma_done = q_full + 2;              // every issued MMA finished (drain)
   // [4] item k's index is in item_ring[k & 3] (warp 0). The producers run at
@@ -291,7 +289,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         if (bar >= v_full && bar < v_full + kStagesTc) count = 2;   // two V producer warps
         if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads;
         if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads;
-        if (bar == q_full && !p.q_tma) count = kQLoaderThreads;
+        if (bar == q_full && !p.q_tma) count = kQTiles * kSoftmaxThreads;
         mbar_init(bar, count);
       }
       *abort_flag = 0;
@@ -761,6 +759,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     uint64_t* my_s_full = s_full + 2 * w;
     uint64_t* my_p_full = p_full + 2 * w;
     uint64_t* my_pv_done = pv_done + 2 * w;
+    uint8_t* q_tile = base + w * kQTileBytes;
     bool ok = true;
     int g = 0;
     for (int k = 0; ok; ++k) {
@@ -776,6 +775,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       const bool valid = rtok < it.T;
       const int lim = valid ? it.s0 + rtok : -1;  // last key this row sees
       const int tile_lim = it.s0 + it.tok0 + w * BQ;  // keys up to here are seen by every row of the tile
+      if (!p.q_tma) {
+        // Q row -> shared memory, 128-byte swizzled K-major (the layout a TMA
+        // copy with SWIZZLE_128B produces). This warpgroup's previous S
+        // products are all finished: it waited for every one of them.
+        const int64_t qoff = ((int64_t)(it.q_base + rtok) * p.hq + rhead) * kHDim;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int half = c >> 3, ch = c & 7;
+          const uint4 v = valid ? load_q8<kBF16>(p.q, qoff + c * 8, p.q_dtype) : make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(q_tile + half * kQHalf + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(q_full);
+      }
       const int n = it.n_w[w];
       if (n == 0) continue;  // no token of this item falls in this Q tile
       float m = -INFINITY, l = 0.f;
@@ -916,47 +929,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     if (!ok) {
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
       if (lane == 0) *abort_flag = 1;
-    }
-  } else if (warp >= kWarpQ0 && !p.q_tma) {
-    // ------------------------------------------------------------ Q loaders
-    // q is not in the MMA's element type, so no TMA copy can place it: these
-    // warps convert each item's two Q tiles into shared memory (128-byte
-    // swizzled K-major, the layout a SWIZZLE_128B copy produces) as soon as
-    // every S product of the previous item has finished, while that item's
-    // softmax and epilogue are still running.
-    const int lt = (warp - kWarpQ0) * 32 + lane;
-    bool aborted = false;
-    for (int k = 0;; ++k) {
-      if (*abort_flag || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
-        aborted = true;
-        break;
-      }
-      const int item = item_ring[k & 3];
-      if (item >= n_items) break;
-      const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
-      if (k > 0 && (*abort_flag || !warp_wait(q_empty, (k - 1) & 1))) {
-        aborted = true;
-        break;
-      }
-      // 16-byte chunks: consecutive threads take consecutive chunks of a row
-      for (int c = lt; c < kQTiles * kRowsTc * 16; c += kQLoaderThreads) {
-        const int w = c / (kRowsTc * 16);
-        const int rc = c - w * (kRowsTc * 16);
-        const int row = rc >> 4, c16 = rc & 15;
-        const int half = c16 >> 3, ch = c16 & 7;
-        const int rtok = it.tok0 + w * BQ + (row >> p.lg_g);
-        const int rhead = it.h * G + (row & (G - 1));
-        const int64_t qoff = ((int64_t)(it.q_base + rtok) * p.hq + rhead) * kHDim + c16 * 8;
-        const uint4 v = rtok < it.T ? load_q8<kBF16>(p.q, qoff, p.q_dtype) : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(base + w * kQTileBytes + half * kQHalf + row * 128 + ((ch ^ (row & 7)) << 4)) =
-            v;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(q_full);
-    }
-    if (aborted && lane == 0) {
-      if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
-      *abort_flag = 1;
     }
   }
   tc_fence_before();
