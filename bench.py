@@ -426,16 +426,28 @@ def exchange_layer(s, l, pl, q, out_full=None):
         out_full.copy_(ex.output(l, q.shape[0]))
 
 
+def fused_append(w, s) -> bool:
+    """16-bit pools store the new token's K/V inside the decode launch
+    (sckv_decode_attn_append); one-byte pools and the KV-head-sharded
+    layouts run the append kernel first."""
+    return w["kv"] in ("fp16", "bf16") and "exchange" not in s and "gather" not in s
+
+
 def run_step(w, s, attn_events=None):
     pool = s["pool"]
     gather = s.get("gather")
+    fused = fused_append(w, s)
     for l in range(w["layers"]):
         pl = l % s["n_phys"]
-        pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
+        if not fused:
+            pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
-        if "exchange" in s:
+        if fused:
+            pool.decode_attn_append(pl, s["q"][l], s["kn"][l], s["vn"][l], s["bt"], s["ctx"], out=s["out"][l],
+                                    workspace=s["ws"])
+        elif "exchange" in s:
             exchange_layer(s, l, pl, s["q"][l])
         else:
             pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
@@ -478,9 +490,10 @@ def bench_ours(args, w_full, world, rank, local):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    fused = fused_append(w, s)
     for _ in range(args.steps):
         total_bytes += step_bytes(w, s)
-        launch_bytes.append(attn_bytes_per_launch(w, s["ctx_host"]))
+        launch_bytes.append(attn_bytes_per_launch(w, s["ctx_host"]) + (append_bytes_per_launch(w) if fused else 0))
         run_step(w, s)
     e1.record()
     torch.cuda.synchronize()
@@ -535,6 +548,10 @@ def bench_ours(args, w_full, world, rank, local):
         d_q, d_k, d_v = d_in[b]
         for l in range(L):
             pl = l % s["n_phys"]
+            if fused:
+                pool.decode_attn_append(pl, d_q[l], d_k[l], d_v[l], s["bt"], s["ctx"], out=d_out[b][l],
+                                        workspace=s["ws"])
+                continue
             pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=pl)
             if "exchange" in s:
                 exchange_layer(s, l, pl, d_q[l], out_full=d_res[b][l])
@@ -587,6 +604,10 @@ def bench_ours(args, w_full, world, rank, local):
     avg_launch_bytes = float(np.mean(launch_bytes))
     achieved = avg_launch_bytes / (attn_avg_ms * 1e-3) / 1e9
     traffic = profiled_traffic(args.workload)
+    # a split launch (non-zero workspace) adds the combine kernel
+    split = pool.decode_workspace_bytes(w["batch"], w["hq"], s["bt"].shape[1]) > 0
+    # the exchange adds its signal and wait kernels
+    launches_per_layer = (1 if fused else 2) + (1 if split else 0) + (2 if "exchange" in s else 0)
     res = {
         "metric": "paged decode-attn KV GB/s (% HBM peak) and decode tok/s",
         "value": round(value, 2),
@@ -609,7 +630,9 @@ def bench_ours(args, w_full, world, rank, local):
                         f"batch {w_full['batch']}" + ("" if (args.layout == "heads" and world > 1) else "/GPU")
                         + f", context {ctx_desc(w_full)}, pool {s['pool_pages']} pages x {s['n_phys']} layers"
                         + (f" (logical layer l reads physical layer l mod {s['n_phys']})"
-                           if s["n_phys"] < w["layers"] else ""),
+                           if s["n_phys"] < w["layers"] else "")
+                        + ("; the one-token K/V append runs inside the decode launch" if fused
+                           else "; one append launch then one decode launch per layer"),
             "global_batch": w["batch"] if (args.layout == "heads" and world > 1) else world * w["batch"],
             "seq_len": ctx_desc(w_full),
             "parallelism": ((f"kv-head-sharded x{world} (NCCL all-gather of outputs per layer)"
@@ -622,12 +645,13 @@ def bench_ours(args, w_full, world, rank, local):
         },
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": int(args.steps * L * 3),
+        "gpu_launches": int(args.steps * L * launches_per_layer),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": ("decode_mma_kernel" if (w["hq"] // w["hkv"] >= 2 or kv_bytes_per_elem(w["kv"]) == 1)
                                 else "decode_kernel")
-                               + " (+combine) per layer launch",
+                               + (" with the fused append" if fused else "")
+                               + (" (+combine)" if split else "") + " per layer launch",
                      "bytes_per_launch": int(avg_launch_bytes), "avg_launch_ms": round(attn_avg_ms, 4)},
         "clocks": clocks,
     }

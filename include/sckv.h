@@ -193,6 +193,31 @@ SCKV_API int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q_d
                      void* workspace, size_t workspace_bytes, int chunk_pages,
                      void* stream);
 
+/* One decode token per sequence with its K/V append in the same launch:
+ * the result equals sckv_append of row b of k_new / v_new
+ * ([n_seqs][num_kv_heads][head_dim] of src_dtype F16 / BF16 / F32, 16-byte
+ * aligned) at position ctx_lens[b] - 1 of sequence b (layer `layer`),
+ * followed by sckv_decode_attn over ctx_lens[b] tokens — the KV-cache concat
+ * and SDPA of one decode step of ModularAttentionEngine.forward_numpy
+ * (models/adapters.py:1194-1229). The warp that reads the page holding
+ * position ctx_lens[b] - 1 stores the new row into the pool and into its
+ * staged copy of the page, so no separate append kernel runs. The page a
+ * sequence appends into must be read by no other sequence of the call (the
+ * arena's copy-on-write keeps a page that is still being filled private;
+ * another reader would race with the store). Every other argument as
+ * sckv_decode_attn. F16 / BF16 pools only (SCKV_ERR_UNSUPPORTED
+ * otherwise: one-byte pools quantise a row against its page or token scale,
+ * use sckv_append then sckv_decode_attn). A sequence whose ctx_lens[b] is
+ * out of range or whose page id is invalid is reported as by
+ * sckv_decode_attn and its row is not stored. */
+SCKV_API int sckv_decode_attn_append(sckv_pool* pool, int layer, const void* q,
+                     int q_dtype, int num_q_heads, const void* k_new,
+                     const void* v_new, int src_dtype,
+                     const int32_t* block_table, int64_t bt_stride,
+                     int max_blocks, const int32_t* ctx_lens, int n_seqs,
+                     float scale, void* out, int out_dtype, void* workspace,
+                     size_t workspace_bytes, int chunk_pages, void* stream);
+
 /* Causal prefill attention: for each of n_seqs sequences, the query tokens
  * cu_q[b] .. cu_q[b+1]-1 sit at positions start_pos[b] + i and attend to
  * every token of that sequence at positions <= their own (the new tokens'

@@ -77,6 +77,9 @@ _SIGNATURES = [
     ("sckv_decode_attn", c_int,
      [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p, c_int, c_float, c_void_p, c_int,
       c_void_p, c_size_t, c_int, c_void_p]),
+    ("sckv_decode_attn_append", c_int,
+     [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int, c_void_p, c_int,
+      c_float, c_void_p, c_int, c_void_p, c_size_t, c_int, c_void_p]),
     ("sckv_append_rope", c_int,
      [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int,
       c_void_p, c_int, c_float, c_void_p, c_float, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int,

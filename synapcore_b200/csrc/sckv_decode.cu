@@ -270,10 +270,26 @@ __global__ void __launch_bounds__(kThreads, (G <= 2 ? 3 : (G == 4 ? 2 : 1)))
           aborted = true;
         }
       }
+      bool fused = false;  // this warp stored the sequence's new token into the staged page
       if (!aborted) {
-        const uint8_t* sK = ring + st * SM::kStageBytes;
+        uint8_t* sK = ring + st * SM::kStageBytes;
         const uint8_t* sV = sK + SM::kPH;
         const int nv = min(SCKV_PAGE_TOKENS, ctx - (j0 + i) * SCKV_PAGE_TOKENS);
+        if constexpr (KVDT == SCKV_DTYPE_F16 || KVDT == SCKV_DTYPE_BF16) {
+          int row = 0;
+          const int32_t page = fused_append_page(p, b, ctx, j0 + i, &row);
+          if (page >= 0) {
+            // fused append: lanes 0-15 the K row, 16-31 the V row, dims 8c..8c+7
+            const uint4 v = new_row8(hf ? p.v_new : p.k_new, ((int64_t)b * p.hkv + h) * kHD + c * 8, p.new_dtype, KVDT);
+            const int off = row * kHD * 2 + c * 16;  // in the page-head
+            *reinterpret_cast<uint4*>(sK + hf * SM::kPH + off) = v;
+            uint8_t* pool = const_cast<uint8_t*>(p.pool);
+            *reinterpret_cast<uint4*>(pool + (layer_base + page) * slab_bytes + ((int64_t)hf * p.hkv + h) * SM::kPH +
+                                      off) = v;
+            fused = true;
+            __syncwarp();
+          }
+        }
         if (KVDT == SCKV_DTYPE_INT8) {
           // this lane's score and probability belong to token tok_mine
           const __half* ts = reinterpret_cast<const __half*>(sK + 2 * SM::kPH);
@@ -338,6 +354,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 2 ? 3 : (G == 4 ? 2 : 1)))
           }
         }
       }
+      // the slot's next bulk copy (async proxy) comes after this warp's stores
+      if (fused) fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
@@ -563,10 +581,17 @@ struct ExchangeTarget {
   int head0;
 };
 
+// New K / V rows a decode call stores before attending (sckv_decode_attn_append).
+struct FusedAppend {
+  const void* k;
+  const void* v;
+  int dtype;
+};
+
 int decode_attn_impl(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
                      const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
                      int n_seqs, float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
-                     int chunk_pages, void* stream, const ExchangeTarget* xt);
+                     int chunk_pages, void* stream, const ExchangeTarget* xt, const FusedAppend* fa = nullptr);
 
 }  // namespace
 
@@ -576,6 +601,22 @@ extern "C" int sckv_decode_attn(sckv_pool* pool, int layer, const void* q, int q
                                 void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
   return decode_attn_impl(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens, n_seqs,
                           scale, out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, nullptr);
+}
+
+extern "C" int sckv_decode_attn_append(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
+                                       const void* k_new, const void* v_new, int src_dtype,
+                                       const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                                       const int32_t* ctx_lens, int n_seqs, float scale, void* out, int out_dtype,
+                                       void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+  if (pool == nullptr) return SCKV_ERR_INVALID_ARG;
+  if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+  if (k_new == nullptr || v_new == nullptr) return SCKV_ERR_INVALID_ARG;
+  if (src_dtype != SCKV_DTYPE_F16 && src_dtype != SCKV_DTYPE_BF16 && src_dtype != SCKV_DTYPE_F32)
+    return SCKV_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) return SCKV_ERR_ALIGNMENT;
+  const FusedAppend fa{k_new, v_new, src_dtype};
+  return decode_attn_impl(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens, n_seqs,
+                          scale, out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, nullptr, &fa);
 }
 
 extern "C" int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int layer, const void* q, int q_dtype,
@@ -606,7 +647,7 @@ namespace {
 int decode_attn_impl(sckv_pool* pool, int layer, const void* q, int q_dtype, int num_q_heads,
                      const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* ctx_lens,
                      int n_seqs, float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
-                     int chunk_pages, void* stream, const ExchangeTarget* xt) {
+                     int chunk_pages, void* stream, const ExchangeTarget* xt, const FusedAppend* fa) {
   const int vrc = validate_decode_args(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks,
                                       ctx_lens, n_seqs, out, out_dtype);
   if (vrc != SCKV_OK) return vrc;
@@ -644,6 +685,11 @@ int decode_attn_impl(sckv_pool* pool, int layer, const void* q, int q_dtype, int
     prm.out_hq_total = xt->hq_total;
     prm.out_head0 = xt->head0;
     prm.out_off = xt->out_off;
+  }
+  if (fa != nullptr) {
+    prm.k_new = fa->k;
+    prm.v_new = fa->v;
+    prm.new_dtype = fa->dtype;
   }
   const int G = num_q_heads / pool->num_kv_heads;
   cudaStream_t s = as_stream(stream);

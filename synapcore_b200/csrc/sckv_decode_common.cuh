@@ -41,7 +41,60 @@ struct DecodeParams {
   int out_hq_total;
   int out_head0;
   int64_t out_off;
+  // fused append (16-bit pools; k_new null: none): row (b, h) of k_new /
+  // v_new [n_seqs][Hkv][HD] of new_dtype is sequence b's token at position
+  // ctx_lens[b] - 1; the warp that consumes that page stores it into the
+  // pool page and into its staged copy before the page's scores
+  const void* k_new;
+  const void* v_new;
+  int new_dtype;
 };
+
+// 8 consecutive values of a new K / V row as the pool's 16-bit type, rounded
+// as sckv_append stores them (same type: copied; else through fp32, RN).
+__device__ __forceinline__ uint4 new_row8(const void* src, int64_t idx, int src_dtype, int pool_dtype) {
+  if (src_dtype == pool_dtype) return *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + idx);
+  float v[8];
+  if (src_dtype == SCKV_DTYPE_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx);
+    const float4 c = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = sckv_load_as_float(src, idx + i, src_dtype);
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (pool_dtype == SCKV_DTYPE_F16) {
+      __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h2);
+    } else {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Orders this thread's generic-proxy shared-memory stores before later
+// async-proxy (bulk copy / TMA) writes to the same bytes.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Page id and in-page row of sequence b's new token when the fused append
+// applies to local page j (the page holding position ctx - 1), else -1. A
+// context out of range (reported by clamp_ctx) or an invalid page id
+// (reported by the producer) stores nothing.
+__device__ __forceinline__ int32_t fused_append_page(const DecodeParams& p, int b, int ctx, int j, int* row) {
+  if (p.k_new == nullptr || ctx < 1 || j != (ctx - 1) / SCKV_PAGE_TOKENS) return -1;
+  if (__ldg(p.ctx_lens + b) != ctx) return -1;
+  const int32_t page = __ldg(p.block_table + (int64_t)b * p.bt_stride + j);
+  if (page < 0 || page >= p.max_pages) return -1;
+  *row = (ctx - 1) % SCKV_PAGE_TOKENS;
+  return page;
+}
 
 // One output element of (sequence b, q head hq, dim d).
 __device__ __forceinline__ void store_out(const DecodeParams& p, int b, int hq, int d, float v) {

@@ -255,11 +255,31 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
           aborted = true;
         }
       }
+      bool fused = false;  // this warp stored its head's new token into the staged page
       if (!aborted) {
         const uint32_t stage = smem_u32(ring + st * SM::kStageBytes);
         const uint32_t sK = stage + hg * kBoxBytes;         // K of head hg, column block 0
         const uint32_t sV = stage + (HG + hg) * kBoxBytes;  // V of head hg, column block 0
         const int nv = min(SCKV_PAGE_TOKENS, ctx - (j0 + i) * SCKV_PAGE_TOKENS);
+        if constexpr (!kB8) {
+          int row = 0;
+          const int32_t page = fused_append_page(p, b, ctx, j0 + i, &row);
+          if (page >= 0) {
+            // fused append: lane = (K|V, 64-dim column block, 16-byte chunk);
+            // the staged row sits in the 128-byte swizzle (chunk ^ row % 8)
+            const int kvh = lane >> 4, bx = (lane >> 3) & 1, ch = lane & 7;
+            const int dim0 = bx * 64 + ch * 8;
+            const uint4 v = new_row8(kvh ? p.v_new : p.k_new, ((int64_t)b * p.hkv + h) * kHD + dim0, p.new_dtype, KVDT);
+            *reinterpret_cast<uint4*>(ring + st * SM::kStageBytes + bx * SM::kBoxStride + (kvh * HG + hg) * kBoxBytes +
+                                      row * 128 + ((ch ^ (row & 7)) << 4)) = v;
+            constexpr int64_t kPH = SCKV_PAGE_TOKENS * kHD * 2;  // bytes of one 16-bit page-head
+            uint8_t* pool = const_cast<uint8_t*>(p.pool);
+            *reinterpret_cast<uint4*>(pool + ((layer_base + page) * 2 * p.hkv + (int64_t)kvh * p.hkv + h) * kPH +
+                                      row * kHD * 2 + dim0 * 2) = v;
+            fused = true;
+            __syncwarp();
+          }
+        }
         float ksA = 1.f, ksB = 1.f, vsA = 1.f, vsB = 1.f;  // int8: scales of tokens g, g + 8
         if (kFP8) {
           kscale = sscale[st * SM::kScaleSlot + h];
@@ -487,6 +507,8 @@ __global__ void __launch_bounds__(kThreads, (mma_min_blocks<KVDT, NQT, HG, S>())
           }
         }
       }
+      // the slot's next TMA copy (async proxy) comes after this warp's stores
+      if (fused) fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }

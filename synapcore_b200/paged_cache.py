@@ -371,6 +371,16 @@ class PagedKVCache:
                                      out=out, out_dtype=out_dtype, max_blocks=self.max_blocks,
                                      chunk_pages=self.chunk_pages)
 
+    def decode_append_attention(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_rows: int,
+                                scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                                out_dtype: Optional[torch.dtype] = None,
+                                workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """decode_append then decode_attention for rows 0..n_rows-1; 16-bit
+        pools do both in one launch (sckv_decode_attn_append)."""
+        return self.pool.decode_attn_append(layer, q, k, v, self.block_table[:n_rows], self.ctx_lens[:n_rows],
+                                            scale=scale, out=out, out_dtype=out_dtype, max_blocks=self.max_blocks,
+                                            chunk_pages=self.chunk_pages, workspace=workspace)
+
     # ------------------------------------------------------ sharing / fork
     def share_prefix(self, seq_id: Hashable, page_ids: Sequence[int]) -> None:
         """Start an empty sequence with full prefix pages held elsewhere (a
@@ -425,7 +435,9 @@ class DecodeStepGraph:
     """One decode step of a `PagedKVCache` over rows 0..n_rows-1, captured
     once in a CUDA graph and replayed: page reservation on the device
     allocator, then for every layer the new token's K/V append and the
-    decode attention (2 + 3 x num_layers kernels issued by one call).
+    decode attention (one launch plus the split combine for 16-bit pools,
+    sckv_decode_attn_append; one-byte pools append first), all issued by
+    one call.
 
     The step reads its inputs from static buffers `q` [L, n, Hq, D] and `k`,
     `v` [L, n, Hkv, D] and writes `out` [L, n, Hq, D]; fill them (copy or
@@ -467,13 +479,9 @@ class DecodeStepGraph:
         c, n = self.cache, self.n_rows
         pool = c.pool
         pool.reserve_decode(c.block_table, c.ctx_lens, n_seqs=n, max_blocks=c.max_blocks)
-        start = c.ctx_lens[:n] - 1
         for layer in range(c.num_layers):
-            pool.append(self.k[layer], self.v[layer], c._arange[:n + 1], start, c.block_table[:n], layer0=layer,
-                        max_blocks=c.max_blocks)
-            pool.decode_attn(layer, self.q[layer], c.block_table[:n], c.ctx_lens[:n], scale=self._scale,
-                             out=self.out[layer], max_blocks=c.max_blocks, chunk_pages=c.chunk_pages,
-                             workspace=self._ws)
+            c.decode_append_attention(layer, self.q[layer], self.k[layer], self.v[layer], n, scale=self._scale,
+                                      out=self.out[layer], workspace=self._ws)
 
     def replay(self) -> torch.Tensor:
         """Run the captured step on the current stream; returns `out`."""

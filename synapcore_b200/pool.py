@@ -445,13 +445,10 @@ class KVPool:
     def decode_workspace_bytes(self, n_seqs: int, num_q_heads: int, max_blocks: int, chunk_pages: int = 0) -> int:
         return int(self.lib.sckv_decode_workspace_bytes(self.handle, n_seqs, num_q_heads, max_blocks, chunk_pages))
 
-    def decode_attn(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor,
-                    scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
-                    out_dtype: Optional[torch.dtype] = None, max_blocks: Optional[int] = None,
-                    chunk_pages: int = 0, workspace: Optional[torch.Tensor] = None,
-                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
-        """q [B, Hq, D] -> out [B, Hq, D]: softmax(scale q K^T) V over each
-        sequence's first ctx_lens[b] tokens of `layer`."""
+    def _decode_args(self, layer, q, block_table, ctx_lens, scale, out, out_dtype, max_blocks, chunk_pages,
+                     workspace):
+        """Checks shared by the decode entry points; returns (q, B, hq, mb,
+        scale, out, workspace)."""
         q = q.contiguous()
         B, hq, d = q.shape
         mb = block_table.shape[1] if max_blocks is None else int(max_blocks)
@@ -481,11 +478,57 @@ class KVPool:
             if self._workspace is None or self._workspace.numel() < need:
                 self._workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=self.device)
             workspace = self._workspace
+        return q, B, hq, mb, float(scale), out, workspace
+
+    def decode_attn(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor,
+                    scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                    out_dtype: Optional[torch.dtype] = None, max_blocks: Optional[int] = None,
+                    chunk_pages: int = 0, workspace: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """q [B, Hq, D] -> out [B, Hq, D]: softmax(scale q K^T) V over each
+        sequence's first ctx_lens[b] tokens of `layer`."""
+        q, B, hq, mb, scale, out, workspace = self._decode_args(layer, q, block_table, ctx_lens, scale, out,
+                                                                out_dtype, max_blocks, chunk_pages, workspace)
         N.check(self.lib.sckv_decode_attn(self.handle, layer, q.data_ptr(), torch_dtype_code(q.dtype), hq,
                                           block_table.data_ptr(), block_table.stride(0), mb, ctx_lens.data_ptr(), B,
-                                          float(scale), out.data_ptr(), torch_dtype_code(out.dtype),
+                                          scale, out.data_ptr(), torch_dtype_code(out.dtype),
                                           workspace.data_ptr(), workspace.numel(), chunk_pages, _stream_ptr(stream)),
                 "sckv_decode_attn")
+        return out
+
+    def decode_attn_append(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                           block_table: torch.Tensor, ctx_lens: torch.Tensor, scale: Optional[float] = None,
+                           out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                           max_blocks: Optional[int] = None, chunk_pages: int = 0,
+                           workspace: Optional[torch.Tensor] = None,
+                           stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """One decode step of `layer`: the new token's k_new / v_new [B, Hkv, D]
+        go to position ctx_lens[b] - 1 of each sequence, then q [B, Hq, D]
+        attends over ctx_lens[b] tokens. 16-bit pools do both in the decode
+        launch (sckv_decode_attn_append); one-byte pools, whose rows are
+        quantised against their page or token scale, run sckv_append then
+        sckv_decode_attn."""
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+        q, B, hq, mb, scale, out, workspace = self._decode_args(layer, q, block_table, ctx_lens, scale, out,
+                                                                out_dtype, max_blocks, chunk_pages, workspace)
+        if tuple(k_new.shape) != (B, self.num_kv_heads, self.head_dim) or k_new.shape != v_new.shape:
+            raise ValueError(f"k_new/v_new must be [B, {self.num_kv_heads}, {self.head_dim}]")
+        if k_new.dtype != v_new.dtype:
+            raise TypeError("k_new and v_new must have the same dtype")
+        _need(k_new, "k_new", self.device)
+        _need(v_new, "v_new", self.device)
+        if self.kv_dtype not in ("fp16", "bf16"):
+            cu = torch.arange(B + 1, dtype=torch.int32, device=self.device)
+            self.append(k_new, v_new, cu, ctx_lens - 1, block_table, layer0=layer, max_blocks=mb, stream=stream)
+            return self.decode_attn(layer, q, block_table, ctx_lens, scale=scale, out=out, max_blocks=mb,
+                                    chunk_pages=chunk_pages, workspace=workspace, stream=stream)
+        N.check(self.lib.sckv_decode_attn_append(self.handle, layer, q.data_ptr(), torch_dtype_code(q.dtype), hq,
+                                                 k_new.data_ptr(), v_new.data_ptr(), torch_dtype_code(k_new.dtype),
+                                                 block_table.data_ptr(), block_table.stride(0), mb,
+                                                 ctx_lens.data_ptr(), B, scale, out.data_ptr(),
+                                                 torch_dtype_code(out.dtype), workspace.data_ptr(),
+                                                 workspace.numel(), chunk_pages, _stream_ptr(stream)),
+                "sckv_decode_attn_append")
         return out
 
     def prefill_attn(self, layer: int, q: torch.Tensor, cu_q: torch.Tensor, start_pos: torch.Tensor,

@@ -435,8 +435,7 @@ class ContinuousBatchScheduler:
         cache.decode_reserve(B)
 
         def attend(l, q, k, v):
-            cache.decode_append(l, k, v, B)
-            return cache.decode_attention(l, q, B, scale=self.attn_scale, out_dtype=torch.float32)
+            return cache.decode_append_attention(l, q, k, v, B, scale=self.attn_scale, out_dtype=torch.float32)
 
         h = self._layers(self.model.embed(meta[0]), meta[1], attend, n_layers)
         logits = self.model.logits(h)
