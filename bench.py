@@ -1555,12 +1555,18 @@ class MixState:
         if io is not None:
             io["dec_in"](n)
         c.decode_reserve(n)
+        fused = w["kv"] in ("fp16", "bf16")  # the append runs inside the decode launch
         for l in range(L):
-            c.decode_append(l, self.k_dec[l, :n], self.v_dec[l, :n], n)
+            if not fused:
+                c.decode_append(l, self.k_dec[l, :n], self.v_dec[l, :n], n)
             if timing is not None:
                 timing["dec"].append(torch.cuda.Event(enable_timing=True))
                 timing["dec"][-1].record()
-            c.decode_attention(l, self.q_dec[l, :n], n, out=self.out_dec[:n])
+            if fused:
+                c.decode_append_attention(l, self.q_dec[l, :n], self.k_dec[l, :n], self.v_dec[l, :n], n,
+                                          out=self.out_dec[:n])
+            else:
+                c.decode_attention(l, self.q_dec[l, :n], n, out=self.out_dec[:n])
             if timing is not None:
                 timing["dec"].append(torch.cuda.Event(enable_timing=True))
                 timing["dec"][-1].record()
@@ -1574,6 +1580,8 @@ class MixState:
         pre = int(pre_ctx.sum()) * hkv * d * 2 * eb + tot * hq * d * 2 * 2
         total = L * (dec + pre + (n + tot) * app_tok)
         pre_flops = L * 4 * hq * d * int(sum(t * s + t * (t + 1) // 2 for t, s in zip(T, starts)))
+        if fused:
+            dec += n * app_tok  # the timed decode launch also stores the new rows
         return total, n, tot, dec, pre, pre_flops
 
 

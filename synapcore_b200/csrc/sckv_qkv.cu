@@ -432,6 +432,11 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       uint32_t gcount = 0;  // stages issued by this CTA
       bool aborted = false;
+      // with several token tiles every weight tile is read once per token
+      // tile, a wave of tiles apart: keep the weights in L2 ahead of the
+      // x tiles and the rows the epilogues write
+      const bool keep_w = p.m_tiles > 1;
+      const uint64_t w_policy = l2_policy_evict_last();
       for (int t = blockIdx.x; t < p.n_tiles && !aborted; t += gridDim.x) {
         const QkvTile tl = qkv_tile<kHeads>(p, t);
         const CUtensorMap* wmap = tl.kind == 0 ? &wqmap : (tl.kind == 1 ? &wkmap : &wvmap);
@@ -451,7 +456,10 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
           mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
           const int kx = (tl.s0 + s) * kQkvBK;
           tma_load_2d(stage, &xmap, kx, tl.m0, &full[st]);
-          tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
+          if (keep_w)
+            tma_load_2d_hint(stage + SM::kOffW, wmap, kx, row0, &full[st], w_policy);
+          else
+            tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
           if (kSplit) tma_load_2d(stage + SM::kOffLo, &xlomap, kx, tl.m0, &full[st]);
           ++gcount;
         }
