@@ -36,6 +36,8 @@
 #include <cuda.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "sckv_internal.cuh"
 #include "sckv_mma_common.cuh"
 #include "sckv_tcgen05.cuh"
@@ -95,6 +97,7 @@ struct QkvParams {
   int pool_dtype;
   int k_steps_per_split;  // hidden steps of 64 per split
   int n_groups;           // head groups (of kHeads heads) over q, k and v
+  int group_block;        // head groups per block of the tile order (see qkv_tile)
   int m_tiles;            // token tiles of 128
   int n_tiles;            // n_groups * m_tiles * splits
   int hd_total;           // (hq + 2 hkv) * 128 output columns
@@ -358,8 +361,12 @@ __global__ void __launch_bounds__(256, 6) qkv_finish_kernel(const QkvParams p, i
   }
 }
 
-// Geometry of work tile t: tiles run head group fastest, then token tile,
-// then hidden split, so CTAs working at the same time share the x tile.
+// Geometry of work tile t. Head groups come in blocks of group_block:
+// tiles run head group within the block fastest, then token tile, then
+// block, then hidden split. CTAs working at the same time share each x tile
+// (read by the block's groups together), and consecutive waves walk the
+// token tiles of one block, whose weights (group_block x kHeads x 128 rows)
+// stay in L2 until the next block starts; x is read once per block.
 struct QkvTile {
   int kind, head0, kind_heads, m0, z, s0, nk;
 };
@@ -368,10 +375,16 @@ template <int kHeads>
 __device__ __forceinline__ QkvTile qkv_tile(const QkvParams& p, int t) {
   QkvTile q;
   const int gq = (p.hq + kHeads - 1) / kHeads, gk = (p.hkv + kHeads - 1) / kHeads;
-  const int gx = t % p.n_groups;
-  const int rest = t / p.n_groups;
-  q.m0 = (rest % p.m_tiles) * kQkvBM;
-  q.z = rest / p.m_tiles;
+  const int per_split = p.n_groups * p.m_tiles;
+  q.z = t / per_split;
+  const int r = t - q.z * per_split;
+  const int blk = r / (p.group_block * p.m_tiles);
+  const int r2 = r - blk * p.group_block * p.m_tiles;
+  const int g0 = blk * p.group_block;
+  const int gsz = min(p.group_block, p.n_groups - g0);  // the last block may be smaller
+  const int m = r2 / gsz;
+  const int gx = g0 + (r2 - m * gsz);
+  q.m0 = m * kQkvBM;
   q.kind = gx < gq ? 0 : (gx < gq + gk ? 1 : 2);  // q, k, v
   q.head0 = (gx - (q.kind == 0 ? 0 : (q.kind == 1 ? gq : gq + gk))) * kHeads;
   q.kind_heads = q.kind == 0 ? p.hq : p.hkv;
@@ -432,11 +445,6 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       uint32_t gcount = 0;  // stages issued by this CTA
       bool aborted = false;
-      // with several token tiles every weight tile is read once per token
-      // tile, a wave of tiles apart: keep the weights in L2 ahead of the
-      // x tiles and the rows the epilogues write
-      const bool keep_w = p.m_tiles > 1;
-      const uint64_t w_policy = l2_policy_evict_last();
       for (int t = blockIdx.x; t < p.n_tiles && !aborted; t += gridDim.x) {
         const QkvTile tl = qkv_tile<kHeads>(p, t);
         const CUtensorMap* wmap = tl.kind == 0 ? &wqmap : (tl.kind == 1 ? &wkmap : &wvmap);
@@ -456,10 +464,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
           mbar_arrive_expect_tx(&full[st], SM::kStageBytes);
           const int kx = (tl.s0 + s) * kQkvBK;
           tma_load_2d(stage, &xmap, kx, tl.m0, &full[st]);
-          if (keep_w)
-            tma_load_2d_hint(stage + SM::kOffW, wmap, kx, row0, &full[st], w_policy);
-          else
-            tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
+          tma_load_2d(stage + SM::kOffW, wmap, kx, row0, &full[st]);
           if (kSplit) tma_load_2d(stage + SM::kOffLo, &xlomap, kx, tl.m0, &full[st]);
           ++gcount;
         }
@@ -705,6 +710,11 @@ int launch_qkv(const QkvParams& prm_in, const CUtensorMap (&maps)[5], int n_grou
   QkvParams prm = prm_in;
   prm.n_groups = n_groups;
   prm.m_tiles = m_tiles;
+  // weights of one block of head groups: at most ~40 MB of L2, blocks of
+  // equal size
+  const int64_t w_group_bytes = (int64_t)QkvCfg<kSplit, kHeads>::kBN * prm.hidden * 2;
+  const int64_t n_blocks = std::max<int64_t>(1, (n_groups * w_group_bytes + (40LL << 20) - 1) / (40LL << 20));
+  prm.group_block = (int)((n_groups + n_blocks - 1) / n_blocks);
   const int64_t n_tiles = (int64_t)n_groups * m_tiles * k_splits;
   if (n_tiles > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
   prm.n_tiles = (int)n_tiles;
