@@ -414,26 +414,50 @@ def advance(s):
         s["ctx_host"] = s["ctx_host"] + 1
 
 
-def exchange_layer(s, l, pl, q, out_full=None):
+def exchange_layer(s, l, pl, q, out_full=None, k_new=None, v_new=None):
     """KV-head-sharded layer with the exchange fused into the decode: this
     rank's heads go straight into every rank's full-head buffer, then a
-    device wait for every rank's flag of this (step, layer)."""
+    device wait for every rank's flag of this (step, layer). Epochs come from
+    each rank's device counter (the same sequence of calls on every rank), so
+    the step can also be replayed from a CUDA graph."""
     ex = s["exchange"]
-    s["epoch"] += 1
-    ex.decode(l, q, s["bt"], s["ctx"], s["epoch"], phys_layer=pl)
-    ex.wait(s["epoch"])
+    ex.decode(l, q, s["bt"], s["ctx"], 0, phys_layer=pl, k_new=k_new, v_new=v_new)
+    ex.wait(0)
     if out_full is not None:
         out_full.copy_(ex.output(l, q.shape[0]))
 
 
 def fused_append(w, s) -> bool:
     """16-bit pools store the new token's K/V inside the decode launch
-    (sckv_decode_attn_append); one-byte pools and the KV-head-sharded
-    layouts run the append kernel first."""
-    return w["kv"] in ("fp16", "bf16") and "exchange" not in s and "gather" not in s
+    (sckv_decode_attn_append, or the exchange decode); one-byte pools run
+    the append kernel first."""
+    return w["kv"] in ("fp16", "bf16")
+
+
+def layer_calls(w, s, l, q, k, v, out, out_full=None):
+    """One layer of the decode step through the public calls."""
+    pool = s["pool"]
+    pl = l % s["n_phys"]
+    fused = fused_append(w, s)
+    if not fused:
+        pool.append(k, v, s["cu"], s["start"], s["bt"], layer0=pl)
+    if "exchange" in s:
+        exchange_layer(s, l, pl, q, out_full=out_full, k_new=k if fused else None, v_new=v if fused else None)
+        return
+    if fused:
+        pool.decode_attn_append(pl, q, k, v, s["bt"], s["ctx"], out=out, workspace=s["ws"])
+    else:
+        pool.decode_attn(pl, q, s["bt"], s["ctx"], out=out, workspace=s["ws"])
+    if "gather" in s and out_full is not None:
+        out_full.copy_(s["gather"].gather(out))
 
 
 def run_step(w, s, attn_events=None):
+    if "graph" in s and attn_events is None:
+        # the whole step captured once (KV-head-sharded exchange layout)
+        s["graph"].replay()
+        advance(s)
+        return
     pool = s["pool"]
     gather = s.get("gather")
     fused = fused_append(w, s)
@@ -444,11 +468,12 @@ def run_step(w, s, attn_events=None):
         if attn_events is not None:
             attn_events.append(torch.cuda.Event(enable_timing=True))
             attn_events[-1].record()
-        if fused:
+        if "exchange" in s:
+            exchange_layer(s, l, pl, s["q"][l], k_new=s["kn"][l] if fused else None,
+                           v_new=s["vn"][l] if fused else None)
+        elif fused:
             pool.decode_attn_append(pl, s["q"][l], s["kn"][l], s["vn"][l], s["bt"], s["ctx"], out=s["out"][l],
                                     workspace=s["ws"])
-        elif "exchange" in s:
-            exchange_layer(s, l, pl, s["q"][l])
         else:
             pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
         if attn_events is not None:
@@ -472,12 +497,24 @@ def bench_ours(args, w_full, world, rank, local):
         from synapcore_b200.distributed import HeadShardedExchange
 
         s["exchange"] = HeadShardedExchange(pool, world, rank, w["layers"], w["batch"], w_full["hq"], w["qdt"])
-        s["epoch"] = 0
         s["full"] = torch.empty((w["layers"], w["batch"], w_full["hq"], w["d"]), dtype=w["qdt"], device="cuda")
     for _ in range(args.warmup):
         run_step(w, s)
     torch.cuda.synchronize()
     pool.raise_on_status()
+    if "exchange" in s:
+        # 16 small layer launches per rank and step: replay the step from a
+        # CUDA graph (captured on every rank, nothing runs during capture)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fused = fused_append(w, s)
+            for l in range(w["layers"]):
+                pl = l % s["n_phys"]
+                if not fused:
+                    pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
+                exchange_layer(s, l, pl, s["q"][l], k_new=s["kn"][l] if fused else None,
+                               v_new=s["vn"][l] if fused else None)
+        s["graph"] = g
     reset_contexts(s)
     total_bytes = 0
     launch_bytes = []
@@ -547,18 +584,8 @@ def bench_ours(args, w_full, world, rank, local):
             comp.wait_event(ev["out_done"][b])
         d_q, d_k, d_v = d_in[b]
         for l in range(L):
-            pl = l % s["n_phys"]
-            if fused:
-                pool.decode_attn_append(pl, d_q[l], d_k[l], d_v[l], s["bt"], s["ctx"], out=d_out[b][l],
-                                        workspace=s["ws"])
-                continue
-            pool.append(d_k[l], d_v[l], s["cu"], s["start"], s["bt"], layer0=pl)
-            if "exchange" in s:
-                exchange_layer(s, l, pl, d_q[l], out_full=d_res[b][l])
-                continue
-            pool.decode_attn(pl, d_q[l], s["bt"], s["ctx"], out=d_out[b][l], workspace=s["ws"])
-            if "gather" in s:
-                d_res[b][l].copy_(s["gather"].gather(d_out[b][l]))
+            layer_calls(w, s, l, d_q[l], d_k[l], d_v[l], d_out[b][l],
+                        out_full=d_res[b][l] if ("gather" in s or "exchange" in s) else None)
         ev["in_free"][b].record(comp)
         ev["out_ready"][b].record(comp)
         advance(s)
@@ -664,6 +691,7 @@ def bench_ours(args, w_full, world, rank, local):
         # every rank's writes into this rank's buffer ended before its last
         # wait; the barrier keeps all ranks' mappings alive until all are done
         torch.cuda.synchronize()
+        s.pop("graph", None)  # the captured step refers to the exchange's buffers
         barrier(world)
         st = s["exchange"].status()
         if st[0] != 0:

@@ -364,11 +364,17 @@ SCKV_API void sckv_exchange_destroy(sckv_exchange* ex);
  * out_offset + (b * num_q_heads_total + rank * num_q_heads + h) * 128 + d of
  * EVERY rank's exchange buffer (out_dtype F32 / F16 / BF16; num_q_heads_total
  * = world * num_q_heads), then, once those stores are complete, sets this
- * rank's flag to `epoch` (non-zero, increasing per call, the same on every
- * rank for the same layer and step) on every rank. Replaces the decode +
- * NCCL all-gather pair of the layout. All ranks' buffers must be open. */
+ * rank's flag to the call's epoch on every rank. epoch: non-zero, increasing
+ * per call, the same on every rank for the same layer and step; or 0 to
+ * take the next value of this rank's device-side epoch counter (last
+ * signalled + 1), which keeps the call capturable in a CUDA graph. k_new /
+ * v_new (both NULL or both set; F16 / BF16 pools): the new token's rows of
+ * this rank's kv heads, appended in the same launch as by
+ * sckv_decode_attn_append. Replaces the decode + NCCL all-gather pair of the
+ * layout. All ranks' buffers must be open. */
 SCKV_API int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int layer,
                              const void* q, int q_dtype, int num_q_heads,
+                             const void* k_new, const void* v_new, int src_dtype,
                              const int32_t* block_table, int64_t bt_stride,
                              int max_blocks, const int32_t* ctx_lens, int n_seqs,
                              float scale, int out_dtype, int64_t out_offset,
@@ -378,9 +384,10 @@ SCKV_API int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int l
 
 /* Stream-ordered wait until every rank's flag here reached `epoch` (then the
  * full-head output of that call is in this rank's buffer for every kernel
- * launched after it on `stream`). Bounded: after limit_us (0 = 2 s) the
- * kernel records SCKV_ERR_TIMEOUT (detail = the late rank) in the exchange's
- * status word and returns. */
+ * launched after it on `stream`); epoch 0 waits for the last epoch this rank
+ * signalled (read on the device when the wait runs). Bounded: after
+ * limit_us (0 = 2 s) the kernel records SCKV_ERR_TIMEOUT (detail = the late
+ * rank) in the exchange's status word and returns. */
 SCKV_API int sckv_exchange_wait(sckv_exchange* ex, uint32_t epoch, unsigned limit_us, void* stream);
 
 /* The exchange's status word (code, detail, kernel, count); clear != 0 resets it. */

@@ -114,8 +114,8 @@ _SIGNATURES = [
     ("sckv_exchange_open_peer", c_int, [c_void_p, c_int, c_void_p]),
     ("sckv_exchange_destroy", None, [c_void_p]),
     ("sckv_decode_attn_exchange", c_int,
-     [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p, c_int, c_float, c_int,
-      c_int64, c_int, c_uint32, c_void_p, c_size_t, c_int, c_void_p]),
+     [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int,
+      c_void_p, c_int, c_float, c_int, c_int64, c_int, c_uint32, c_void_p, c_size_t, c_int, c_void_p]),
     ("sckv_exchange_wait", c_int, [c_void_p, c_uint32, c_uint32, c_void_p]),
     ("sckv_exchange_status", c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     ("sckv_reserve_decode", c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p]),

@@ -620,23 +620,33 @@ extern "C" int sckv_decode_attn_append(sckv_pool* pool, int layer, const void* q
 }
 
 extern "C" int sckv_decode_attn_exchange(sckv_pool* pool, sckv_exchange* ex, int layer, const void* q, int q_dtype,
-                                         int num_q_heads, const int32_t* block_table, int64_t bt_stride,
-                                         int max_blocks, const int32_t* ctx_lens, int n_seqs, float scale,
-                                         int out_dtype, int64_t out_offset, int num_q_heads_total, uint32_t epoch,
-                                         void* workspace, size_t workspace_bytes, int chunk_pages, void* stream) {
+                                         int num_q_heads, const void* k_new, const void* v_new, int src_dtype,
+                                         const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                                         const int32_t* ctx_lens, int n_seqs, float scale, int out_dtype,
+                                         int64_t out_offset, int num_q_heads_total, uint32_t epoch, void* workspace,
+                                         size_t workspace_bytes, int chunk_pages, void* stream) {
   if (pool == nullptr || ex == nullptr || ex->device != pool->device) return SCKV_ERR_INVALID_ARG;
   for (int r = 0; r < ex->world; ++r)
     if (!ex->opened[r]) return SCKV_ERR_INVALID_ARG;  // every peer's buffers must be mapped
   const int head0 = ex->rank * num_q_heads;
-  if (num_q_heads <= 0 || num_q_heads_total != ex->world * num_q_heads || out_offset < 0 || epoch == 0)
+  if (num_q_heads <= 0 || num_q_heads_total != ex->world * num_q_heads || out_offset < 0)
     return SCKV_ERR_INVALID_ARG;
+  if ((k_new == nullptr) != (v_new == nullptr)) return SCKV_ERR_INVALID_ARG;
+  if (k_new != nullptr) {
+    if (pool->kv_dtype != SCKV_DTYPE_F16 && pool->kv_dtype != SCKV_DTYPE_BF16) return SCKV_ERR_UNSUPPORTED;
+    if (src_dtype != SCKV_DTYPE_F16 && src_dtype != SCKV_DTYPE_BF16 && src_dtype != SCKV_DTYPE_F32)
+      return SCKV_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) return SCKV_ERR_ALIGNMENT;
+  }
   const size_t esz = out_dtype == SCKV_DTYPE_F32 ? 4 : 2;
   const int64_t end = out_offset + (int64_t)n_seqs * num_q_heads_total * kHD;
   if (n_seqs <= 0 || (size_t)end * esz > ex->out_bytes) return SCKV_ERR_INVALID_ARG;
   if (((out_offset * (int64_t)esz) & 15) != 0) return SCKV_ERR_ALIGNMENT;
   const ExchangeTarget xt{ex, out_offset, num_q_heads_total, head0};
+  const FusedAppend fa{k_new, v_new, src_dtype};
   int rc = decode_attn_impl(pool, layer, q, q_dtype, num_q_heads, block_table, bt_stride, max_blocks, ctx_lens,
-                            n_seqs, scale, ex->out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, &xt);
+                            n_seqs, scale, ex->out, out_dtype, workspace, workspace_bytes, chunk_pages, stream, &xt,
+                            k_new != nullptr ? &fa : nullptr);
   if (rc != SCKV_OK) return rc;
   SCKV_DEVICE_GUARD(pool->device);
   return launch_exchange_signal(ex, epoch, as_stream(stream));

@@ -18,6 +18,10 @@
 //     rank's epoch reached the awaited one, bounded in time; on expiry it
 //     records SCKV_ERR_TIMEOUT (detail = the rank that is late) in the
 //     exchange's status word and returns, so the context stays usable.
+// Epochs are either passed by the caller or, with epoch 0, taken from a
+// device counter of this rank's signals (next = last + 1; the wait then
+// awaits the last one signalled), so a step of several layers can be
+// captured once in a CUDA graph and replayed.
 // No TMA or multicast touches peer memory; only ordinary stores and the flag
 // loads / stores do.
 #include <cstring>
@@ -28,29 +32,35 @@
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr size_t kCtlBytes = 256;  // flags [8] u32 at 0, status [4] i32 at 128
+constexpr size_t kCtlBytes = 256;  // flags [8] u32 at 0, status [4] i32 at 128, epoch counter u32 at 192
 
 struct SignalArgs {
   uint32_t* flags[kMaxRanks];
+  uint32_t* counter;
   int world;
   int rank;
-  uint32_t epoch;
+  uint32_t epoch;  // 0: the counter's next
 };
 
 __global__ void exchange_signal_kernel(SignalArgs a) {
   const int r = threadIdx.x;
+  const uint32_t e = a.epoch != 0 ? a.epoch : *a.counter + 1u;
+  __syncthreads();  // every thread has read the counter before it moves
+  if (r == 0) *a.counter = e;
   if (r >= a.world) return;
   // the decode launches before this kernel in the stream have completed;
   // their stores to every rank's buffer become visible system-wide before
   // the flag does
   __threadfence_system();
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[r] + a.rank), "r"(a.epoch) : "memory");
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[r] + a.rank), "r"(e) : "memory");
 }
 
-__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int32_t* status,
-                                     unsigned long long limit_ns) {
+__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch_arg, const uint32_t* counter,
+                                     int32_t* status, unsigned long long limit_ns) {
   const int r = threadIdx.x;
-  if (r < world) {
+  // epoch 0: the last epoch this rank signalled (none yet: nothing to wait for)
+  const uint32_t epoch = epoch_arg != 0 ? epoch_arg : *counter;
+  if (r < world && epoch != 0) {
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
       uint32_t v;
@@ -75,6 +85,7 @@ namespace sckv_detail {
 int launch_exchange_signal(const sckv_exchange* ex, uint32_t epoch, cudaStream_t stream) {
   SignalArgs a{};
   for (int r = 0; r < ex->world; ++r) a.flags[r] = ex->peer_flags[r];
+  a.counter = ex->counter;
   a.world = ex->world;
   a.rank = ex->rank;
   a.epoch = epoch;
@@ -108,6 +119,7 @@ extern "C" int sckv_exchange_create(int device, int world, int rank, size_t out_
   }
   ex->flags = reinterpret_cast<uint32_t*>(ctl);
   ex->status = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ctl) + 128);
+  ex->counter = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(ctl) + 192);
   ex->peer_out[rank] = ex->out;
   ex->peer_flags[rank] = ex->flags;
   ex->opened[rank] = 1;
@@ -150,11 +162,12 @@ extern "C" int sckv_exchange_open_peer(sckv_exchange* ex, int peer, const uint8_
 }
 
 extern "C" int sckv_exchange_wait(sckv_exchange* ex, uint32_t epoch, unsigned limit_us, void* stream) {
-  if (!valid_ex(ex) || epoch == 0) return SCKV_ERR_INVALID_ARG;
+  if (!valid_ex(ex)) return SCKV_ERR_INVALID_ARG;
   const unsigned long long limit_ns =
       (limit_us == 0 || limit_us > 2000000u) ? SCKV_WAIT_LIMIT_NS : (unsigned long long)limit_us * 1000ull;
   SCKV_DEVICE_GUARD(ex->device);
-  exchange_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(ex->flags, ex->world, epoch, ex->status, limit_ns);
+  exchange_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(ex->flags, ex->world, epoch, ex->counter, ex->status,
+                                                         limit_ns);
   SCKV_LAUNCH_CHECK();
   return SCKV_OK;
 }

@@ -109,6 +109,7 @@ struct sckv_exchange {
   size_t out_bytes;
   uint32_t* flags;   // [world]: the last epoch each rank signalled here
   int32_t* status;   // [4]: code, detail, kernel, count (as a pool's status word)
+  uint32_t* counter; // the last epoch this rank signalled (device; epoch 0 calls continue from it)
   void* peer_out[8];
   uint32_t* peer_flags[8];
   int opened[8];

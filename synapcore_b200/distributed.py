@@ -84,10 +84,17 @@ class HeadShardedExchange:
     slice of every output row into every rank's buffer and then raises this
     rank's flag for the call's epoch on every rank; `wait(epoch)` queues a
     bounded device wait for all ranks' flags, after which `output(layer, B)`
-    holds the full [B, Hq, D] result. Epochs are step * layers + layer + 1,
-    identical on all ranks. A layer's slice is rewritten only in the next
-    step, after this rank has waited for every rank's signal of every later
-    layer, so no rank overwrites a slice another still reads."""
+    holds the full [B, Hq, D] result. Epochs grow by one per call and are
+    identical on all ranks: pass them explicitly, or pass 0 to both calls to
+    let each rank's device counter supply them (then a whole step can be
+    captured in a CUDA graph and replayed). `k_new` / `v_new` [B, Hkv/world,
+    D] append the step's new token in the same launch (16-bit pools). A
+    layer's slice is rewritten in the next step as soon as the writer has
+    waited for every rank's signal of the following layer, so each rank must
+    read layer l's output before it signals layer l + 1 (a model's next
+    layer consumes it anyway); a caller that reads only after a whole step
+    (e.g. a replayed graph with no consumer inside) holds the other ranks at
+    a barrier until it has read."""
 
     def __init__(self, pool, world: int, rank: int, layers: int, max_seqs: int, num_q_heads_total: int,
                  out_dtype: torch.dtype = torch.float32, group: Optional["torch.distributed.ProcessGroup"] = None):
@@ -124,8 +131,9 @@ class HeadShardedExchange:
         self._view = _device_view(ptr, self.layers * self.slice_elems, out_dtype, pool.device)
         self._ws: Optional[torch.Tensor] = None
 
-    def decode(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor, epoch: int,
+    def decode(self, layer: int, q: torch.Tensor, block_table: torch.Tensor, ctx_lens: torch.Tensor, epoch: int = 0,
                phys_layer: Optional[int] = None, scale: Optional[float] = None, chunk_pages: int = 0,
+               k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
                stream: Optional[torch.cuda.Stream] = None) -> None:
         from .pool import _stream_ptr, torch_dtype_code
 
@@ -133,6 +141,17 @@ class HeadShardedExchange:
         B, hq, d = q.shape
         if B > self.max_seqs or hq * self.world != self.hq_total:
             raise ValueError("q must be [<= max_seqs, Hq / world, D]")
+        k_ptr = v_ptr = None
+        src_code = 0
+        if (k_new is None) != (v_new is None):
+            raise ValueError("pass both k_new and v_new, or neither")
+        if k_new is not None:
+            k_new, v_new = k_new.contiguous(), v_new.contiguous()
+            if tuple(k_new.shape) != (B, self.pool.num_kv_heads, d) or k_new.shape != v_new.shape:
+                raise ValueError(f"k_new/v_new must be [B, {self.pool.num_kv_heads}, {d}]")
+            if k_new.dtype != v_new.dtype:
+                raise TypeError("k_new and v_new must have the same dtype")
+            k_ptr, v_ptr, src_code = k_new.data_ptr(), v_new.data_ptr(), torch_dtype_code(k_new.dtype)
         mb = block_table.shape[1]
         need = self.pool.decode_workspace_bytes(B, hq, mb, chunk_pages)
         if self._ws is None or self._ws.numel() < need:
@@ -140,12 +159,12 @@ class HeadShardedExchange:
         scale = float(d) ** -0.5 if scale is None else float(scale)
         pl = layer if phys_layer is None else phys_layer
         self.N.check(self.lib.sckv_decode_attn_exchange(
-            self.pool.handle, self.handle, pl, q.data_ptr(), torch_dtype_code(q.dtype), hq, block_table.data_ptr(),
-            block_table.stride(0), mb, ctx_lens.data_ptr(), B, scale, self.code, layer * self.slice_elems,
-            self.hq_total, int(epoch), self._ws.data_ptr(), self._ws.numel(), chunk_pages, _stream_ptr(stream)),
-            "sckv_decode_attn_exchange")
+            self.pool.handle, self.handle, pl, q.data_ptr(), torch_dtype_code(q.dtype), hq, k_ptr, v_ptr, src_code,
+            block_table.data_ptr(), block_table.stride(0), mb, ctx_lens.data_ptr(), B, scale, self.code,
+            layer * self.slice_elems, self.hq_total, int(epoch), self._ws.data_ptr(), self._ws.numel(), chunk_pages,
+            _stream_ptr(stream)), "sckv_decode_attn_exchange")
 
-    def wait(self, epoch: int, limit_us: int = 0, stream: Optional[torch.cuda.Stream] = None) -> None:
+    def wait(self, epoch: int = 0, limit_us: int = 0, stream: Optional[torch.cuda.Stream] = None) -> None:
         from .pool import _stream_ptr
 
         self.N.check(self.lib.sckv_exchange_wait(self.handle, int(epoch), int(limit_us), _stream_ptr(stream)),

@@ -91,10 +91,11 @@ def test_head_sharded_decode_equals_single_gpu(tmp_path):
         assert np.max(np.abs(got - ref)) <= 2e-3 * np.max(np.abs(ref))
 
 
-def _exchange_worker(rank, world, port, out_path, steps=3):
+def _exchange_worker(rank, world, port, out_path, steps=3, graph=False):
     """KV-head-sharded decode with the exchange fused into the kernel: every
     rank runs its heads, waits for every rank's flag, and rank 0 records the
-    full output of each (step, layer)."""
+    full output of each (step, layer). graph=True captures one step with
+    device-counter epochs in a CUDA graph and replays it per step."""
     import torch.distributed as dist
 
     from synapcore_b200.distributed import HeadShardedExchange, head_range, query_head_range
@@ -118,9 +119,32 @@ def _exchange_worker(rank, world, port, out_path, steps=3):
         ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
         ex = HeadShardedExchange(pool, world, rank, L, len(ctx), hq, torch.float32)
         outs = []
+        q_loc = torch.from_numpy(np.ascontiguousarray(q[:, qr.start:qr.stop])).to(dev)
+        q_d = q_loc.clone()
+        g = None
+        if graph:
+            # every rank makes the same eager call first (launch set-up outside
+            # the capture), then captures the step
+            ex.decode(0, q_d, bt_d, ctx_d, 0)
+            ex.wait(0)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for layer in range(L):
+                    ex.decode(layer, q_d, bt_d, ctx_d, 0)
+                    ex.wait(0)
         for step in range(steps):
             # each step scales q differently, so a stale slice would show
-            q_d = (torch.from_numpy(np.ascontiguousarray(q[:, qr.start:qr.stop])) * (1.0 + 0.25 * step)).to(dev)
+            q_d.copy_(q_loc * (1.0 + 0.25 * step))
+            if g is not None:
+                g.replay()
+                for layer in range(L):
+                    outs.append(ex.output(layer, len(ctx)).clone())
+                # the whole step is read after its last signal: keep the other
+                # rank's next step from rewriting the slices until then
+                torch.cuda.synchronize()
+                dist.barrier()
+                continue
             for layer in range(L):
                 epoch = step * L + layer + 1
                 ex.decode(layer, q_d, bt_d, ctx_d, epoch)
@@ -131,6 +155,7 @@ def _exchange_worker(rank, world, port, out_path, steps=3):
         assert ex.status()[0] == 0
         if rank == 0:
             np.save(out_path, torch.stack(outs).cpu().numpy())
+        del g
         dist.barrier()
     finally:
         if ex is not None:
@@ -141,8 +166,10 @@ def _exchange_worker(rank, world, port, out_path, steps=3):
 
 
 @pytest.mark.timeout(300)
-def test_head_sharded_exchange_equals_single_gpu(tmp_path):
-    """Two ranks, fused NVLink exchange: every (step, layer) output equals the
+@pytest.mark.parametrize("graph", [False, True])
+def test_head_sharded_exchange_equals_single_gpu(tmp_path, graph):
+    """Two ranks, fused NVLink exchange (explicit epochs, or device-counter
+    epochs in a replayed CUDA graph): every (step, layer) output equals the
     single-GPU decode of all heads."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -152,7 +179,7 @@ def test_head_sharded_exchange_equals_single_gpu(tmp_path):
 
     out = tmp_path / "exchange.npy"
     steps = 3
-    mp.start_processes(_exchange_worker, args=(2, _free_port(), str(out), steps), nprocs=2, join=True,
+    mp.start_processes(_exchange_worker, args=(2, _free_port(), str(out), steps, graph), nprocs=2, join=True,
                        start_method="spawn")
     got_all = np.load(out)
     L, hq, hkv, D, P, ctx, k, v, bt, q = _case()
@@ -219,6 +246,74 @@ def test_exchange_single_rank_and_bounded_wait(cuda_device):
             assert torch.isfinite(again).all()
             ex.close()
             pool.close()
+    finally:
+        if own_group:
+            dist.destroy_process_group()
+
+
+def test_exchange_device_epochs_in_a_graph_with_fused_append(cuda_device):
+    """One rank: a step of two layers (exchange decode with the new token's
+    K/V appended in the same launch, then the wait), both taking their epochs
+    from the device counter, captured once in a CUDA graph and replayed
+    twice. Every replay equals sckv_append + sckv_decode_attn bit for bit,
+    pool bytes included."""
+    import torch.distributed as dist
+
+    from synapcore_b200.distributed import HeadShardedExchange
+    from synapcore_b200.pool import KVPool
+
+    own_group = not dist.is_initialized()
+    if own_group:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        L, hq, hkv, D, P = 2, 16, 4, 128, 120
+        rng = np.random.default_rng(8)
+        ctx0 = np.array([37, 700, 513, 16, 1, 255], np.int64)
+        n_pages = (ctx0 + 2 + 15) // 16  # room for the two replayed tokens
+        mb = int(n_pages.max())
+        perm = rng.permutation(P)
+        bt = np.zeros((len(ctx0), mb), np.int32)
+        off = 0
+        for b, n in enumerate(n_pages):  # private pages: nothing appended is read by another sequence
+            bt[b, :n] = perm[off:off + n]
+            off += n
+        kv = torch.from_numpy(rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)).to(cuda_device)
+        ref_pool = KVPool(L, hkv, D, P, "fp16", device=cuda_device)
+        pool = KVPool(L, hkv, D, P, "fp16", device=cuda_device)
+        for p_ in (ref_pool, pool):
+            p_.write_pages(torch.arange(P, dtype=torch.int32, device=cuda_device), kv, kv * 0.5)
+        bt_d = torch.from_numpy(bt).to(cuda_device)
+        ctx_d = torch.tensor(ctx0 + 1, dtype=torch.int32, device=cuda_device)
+        cu = torch.arange(len(ctx0) + 1, dtype=torch.int32, device=cuda_device)
+        q = torch.from_numpy(rng.standard_normal((L, len(ctx0), hq, D)).astype(np.float16)).to(cuda_device)
+        k_new = torch.from_numpy(rng.standard_normal((L, len(ctx0), hkv, D)).astype(np.float16)).to(cuda_device)
+        v_new = torch.from_numpy(rng.standard_normal((L, len(ctx0), hkv, D)).astype(np.float16)).to(cuda_device)
+        ex = HeadShardedExchange(pool, 1, 0, L, 8, hq, torch.float32)
+        # one eager call sets up launch attributes outside the capture (it only reads the pool)
+        ex.decode(0, q[0], bt_d, ctx_d, 0)
+        ex.wait(0)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for layer in range(L):
+                ex.decode(layer, q[layer], bt_d, ctx_d, 0, k_new=k_new[layer], v_new=v_new[layer])
+                ex.wait(0)
+        for step in range(2):
+            g.replay()
+            for layer in range(L):
+                ref_pool.append(k_new[layer], v_new[layer], cu, ctx_d - 1, bt_d, layer0=layer)
+                ref = ref_pool.decode_attn(layer, q[layer], bt_d, ctx_d, out_dtype=torch.float32)
+                torch.cuda.synchronize()
+                assert torch.equal(ex.output(layer, len(ctx0)), ref), (step, layer)
+            assert torch.equal(pool.data, ref_pool.data), step
+            ctx_d += 1  # the next step's token
+        assert ex.status()[0] == 0
+        pool.raise_on_status()
+        del g
+        ex.close()
+        pool.close()
+        ref_pool.close()
     finally:
         if own_group:
             dist.destroy_process_group()
