@@ -1748,7 +1748,9 @@ def bench_mix(args, w, world, rank, local):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args.workload),
-                     "peak_kind": peak_kind, "kernel": "decode_kernel (+combine) per layer launch",
+                     "peak_kind": peak_kind,
+                     "kernel": ("decode_kernel with the fused append" if w["kv"] in ("fp16", "bf16") else
+                                "decode_mma_kernel") + " (+combine) per layer launch",
                      "bytes_per_launch": int(dec_launch_bytes), "avg_launch_ms": round(dec_avg_ms, 4)},
         "prefill_roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
                              "frac": round(tflops / tc_peak, 4),
