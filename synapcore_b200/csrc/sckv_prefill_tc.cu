@@ -60,7 +60,8 @@ constexpr uint32_t kColO = 256;
 
 // warps: 0 claims items, loads Q and half of each K tile; 3 the other half
 // of K; 2 and 12 the two halves of V; 1 issues the MMAs; 4-7 and 8-11 are
-// the softmax warpgroups of Q tiles 0 and 1; 13-15 idle
+// the softmax warpgroups of Q tiles 0 and 1; 13-15 convert Q in place when
+// it arrives by TMA in the other 16-bit type (else idle)
 constexpr int kWarpK0 = 0, kWarpMma = 1, kWarpV0 = 2, kWarpK1 = 3, kWarpV1 = 12;
 
 constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of a Q tile: 16 KiB
@@ -81,7 +82,7 @@ struct TcCfg {
   static constexpr int kOffV = kOffK + kStages * kSlotBytes;       // V ring [kStages]
   static constexpr int kOffStage = kOffV + kStages * kSlotBytes;   // [4 producer warps][2][kStageSlot]
   static constexpr int kOffBar = kOffStage + (kB8 ? 4 * 2 * kStageSlot : 0);
-  static constexpr int kNumBars = 4 * kStages + 4 + 4 + 4 + 2 + 3 + 4 + (kB8 ? 8 : 0);
+  static constexpr int kNumBars = 4 * kStages + 4 + 4 + 4 + 2 + 3 + 4 + (kB8 ? 8 : 0) + 1;
   static constexpr int kOffItemRing = kOffBar + kNumBars * 8;      // int[4]
   static constexpr int kOffTmemSlot = kOffItemRing + 16;
   static constexpr int kOffAbort = kOffTmemSlot + 4;
@@ -108,7 +109,10 @@ struct TcParams {
   int layer;
   int q_dtype;
   int out_dtype;
-  int q_tma;  // q arrives by TMA (its type is the MMA's)
+  // how Q reaches shared memory: 0 the softmax threads load and convert it;
+  // 1 TMA, q has the MMA's type; 2 TMA of the other 16-bit type, then warps
+  // 13-15 convert the tile in place (bf16 <-> f16, rounded as load_q8 does)
+  int q_tma;
   const void* kv_scales;  // one-byte pools: FP8 fp32 [L][P][K|V][H], int8 fp16 [L][P][K|V][H][16]
   unsigned long long* next_item;  // work counter, zero at launch
   float scale_log2;
@@ -258,6 +262,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint64_t* item_full = q_full + 3;
   // one-byte pools: [producer warp role 2 kv + part][2] staged page codes landed (TMA)
   uint64_t* stage_full = item_full + 4;
+  // Q converted in place (q_tma 2; 96 threads of warps 13-15): the MMAs wait for this instead of q_full
+  uint64_t* q_conv = stage_full + (C::kB8 ? 8 : 0);
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + kOffItemRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + kOffAbort);
@@ -290,6 +296,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads;
         if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads;
         if (bar == q_full && !p.q_tma) count = kQTiles * kSoftmaxThreads;
+        if (bar == q_conv) count = 3 * 32;
         mbar_init(bar, count);
       }
       *abort_flag = 0;
@@ -343,6 +350,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int role = 2 * kv + part;
     const bool leader = warp == kWarpK0;
     if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    if (lane == 0 && leader && p.q_tma)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&qmap)) : "memory");
     const int64_t layer_base = (int64_t)p.layer * p.max_pages;
     uint64_t* fulls = kv ? v_full : k_full;
     uint64_t* empties = kv ? v_empty : k_empty;
@@ -359,6 +368,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     int g = 0;        // tiles of this warp's ring so far
     uint32_t sg = 0;  // staged tiles issued
     uint32_t sc = 0;  // staged tiles decoded
+    int q_issued = 0;  // items whose Q the leader loaded by TMA
     bool aborted = false;
     for (int k = 0;; ++k) {
       int item;
@@ -381,6 +391,29 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       }
       if (item >= n_items) break;
       const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
+      if (leader && p.q_tma) {
+        // Q of the item by TMA once every S product of the previous item
+        // (the only reader of the Q tiles) has finished
+        int okq = 1;
+        if (lane == 0) {
+          if (k > 0 && (*abort_flag || !mbar_wait_bounded(q_empty, (k - 1) & 1, SCKV_WAIT_LIMIT_NS))) {
+            okq = 0;
+          } else {
+            const int live = it.n_w[1] > 0 ? 2 : 1;
+            mbar_arrive_expect_tx(q_full, (uint32_t)live * 2u * kQHalf);
+            for (int w = 0; w < live; ++w) {
+              const int tok = it.q_base + it.tok0 + w * BQ;
+              tma_load_3d(smem_u32(base + w * kQTileBytes), &qmap, 0, it.h * G, tok, q_full);
+              tma_load_3d(smem_u32(base + w * kQTileBytes + kQHalf), &qmap, 64, it.h * G, tok, q_full);
+            }
+            ++q_issued;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, okq, 0)) {
+          aborted = true;
+          continue;  // publishes the stop marker next
+        }
+      }
       const int32_t* bt_row = p.block_table + (int64_t)it.seq * p.bt_stride;
       // this warp's page ids of a local tile (0 past the item's last page)
       auto fetch_ids = [&](int j, int32_t& a, int32_t& b) {
@@ -500,9 +533,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
       *abort_flag = 1;
     }
-    // staged copies still in flight land before the CTA retires
+    // staged copies (and Q copies) still in flight land before the CTA retires
     if (lane == 0)
       for (uint32_t t = sc; t < sg; ++t) mbar_wait_bounded(&sfull[t & 1], (t >> 1) & 1, SCKV_WAIT_LIMIT_NS);
+    if (lane == 0 && q_issued > 0) mbar_wait_bounded(q_full, (q_issued - 1) & 1, SCKV_WAIT_LIMIT_NS);
   } else if (warp == kWarpK0 || warp == kWarpK1 || warp == kWarpV0 || warp == kWarpV1) {
     // ------------------------------------------------------------ producers
     // one TMA issue holds its warp ~0.1 us, so K and V each get two warps,
@@ -686,7 +720,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       const int item = item_ring[k & 3];
       if (item >= n_items) break;
       const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
-      if (*abort_flag || !warp_wait(q_full, k & 1)) {
+      if (*abort_flag || !warp_wait(p.q_tma == 2 ? q_conv : q_full, k & 1)) {
         ok = false;
         break;
       }
@@ -930,6 +964,52 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
       if (lane == 0) *abort_flag = 1;
     }
+  } else if (warp >= 13 && p.q_tma == 2) {
+    // ------------------------------------------------------------ Q conversion
+    // Q arrived by TMA in the other 16-bit type: convert both Q tiles in
+    // place, 16-byte chunk by chunk (the 128-byte swizzle only permutes
+    // chunks), while the softmax warps finish the previous item. A tile
+    // with no token of the item holds stale values that no MMA reads.
+    const int ct = threadIdx.x - 13 * 32;  // 0..95
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      if (*abort_flag || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
+        ok = false;
+        break;
+      }
+      if (item_ring[k & 3] >= n_items) break;
+      if (*abort_flag || !warp_wait(q_full, k & 1)) {
+        ok = false;
+        break;
+      }
+      for (int c = ct; c < kQTiles * kQTileBytes / 16; c += 3 * 32) {
+        uint4* chunk = reinterpret_cast<uint4*>(base + c * 16);
+        const uint4 raw = *chunk;
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float lo, hi;
+          if (kBF16) {  // f16 q, bf16 MMA (sckv_prefill_attn takes bf16 q for bf16 pools today)
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+            lo = f.x;
+            hi = f.y;
+          } else {  // bf16 q, f16 MMA
+            lo = __uint_as_float(w4[i] << 16);
+            hi = __uint_as_float(w4[i] & 0xFFFF0000u);
+          }
+          o4[i] = pack2<kBF16>(lo, hi);
+        }
+        *chunk = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+      // the converted tiles are read by the tensor cores (async proxy)
+      fence_proxy_async_smem();
+      mbar_arrive(q_conv);
+    }
+    if (!ok) {
+      if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
+      if (lane == 0) *abort_flag = 1;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1001,12 +1081,15 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
   const int64_t max_tiles = (int64_t)(n_tokens + BQ2 - 1) / BQ2 + n_seqs;  // >= sum of ceil(T_s / BQ2)
   const int64_t max_items = max_tiles * pool->num_kv_heads;
   if (max_items > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
-  // q in the MMA's element type arrives by TMA: a 3-D view (dim, head,
-  // token) whose boxes of 64 dims x G heads x 128/G tokens are exactly an
-  // item's 128 rows, in row order
+  // 16-bit q arrives by TMA (converted in place by warps 13-15 when it is
+  // not the MMA's type): a 3-D view (dim, head, token) whose boxes of 64
+  // dims x G heads x 128/G tokens are exactly an item's 128 rows, in row order
   CUtensorMap qmap;
   prm.q_tma = 0;
-  if (q_dtype == pool->kv_dtype) {
+  // the MMA's element type: bf16 for bf16 pools, f16 otherwise (one-byte
+  // pages are decoded into f16)
+  const int mma_dtype = pool->kv_dtype == SCKV_DTYPE_BF16 ? SCKV_DTYPE_BF16 : SCKV_DTYPE_F16;
+  if (q_dtype == SCKV_DTYPE_F16 || q_dtype == SCKV_DTYPE_BF16) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (encode != nullptr) {
       const cuuint64_t dims[3] = {(cuuint64_t)kHDim, (cuuint64_t)num_q_heads, (cuuint64_t)n_tokens};
@@ -1016,7 +1099,7 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
       if (encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(q), dims, strides, box, estr,
                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-        prm.q_tma = 1;
+        prm.q_tma = q_dtype == mma_dtype ? 1 : 2;
     }
   }
   switch (pool->kv_dtype) {
