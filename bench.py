@@ -262,7 +262,7 @@ def dist_setup(n_gpus: int):
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device(f"cuda:{local}"))
-    else:
+    elif torch.cuda.is_available():  # the reference arm runs on host cores and needs no GPU
         torch.cuda.set_device(0)
     return world, rank, local
 
