@@ -64,12 +64,14 @@ WORKLOADS = {
                         qdt=torch.float16, batch=8, ctx=4096, pool_pages=2200),
     "qwen3-fp8-small": dict(model="Qwen3-8B attention", layers=2, hq=32, hkv=8, d=128, kv="fp8_e4m3",
                             qdt=torch.bfloat16, batch=16, ctx=16384, pool_pages=16 * 1024 + 64),
-    # config 2 with the reference arena's int8 mode, and with FP8 pages
+    # the OLMoE decode (16 layers, 64 x 4,096 tokens) with the reference
+    # arena's int8 mode, and with FP8 pages
     "olmoe-int8": dict(model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="int8",
                        qdt=torch.float16, batch=64, ctx=4096, pool_pages=18750),
     "olmoe-fp8": dict(model="OLMoE-1B-7B attention", layers=16, hq=16, hkv=16, d=128, kv="fp8_e4m3",
                       qdt=torch.float16, batch=64, ctx=4096, pool_pages=18750),
-    # config 4 with the reference arena's int8 mode (per-token fp16 scales)
+    # the Qwen3-8B decode (36 layers, 128 x 16,384 tokens) with the reference
+    # arena's int8 mode (per-token fp16 scales)
     "qwen3-int8": dict(model="Qwen3-8B attention", layers=36, hq=32, hkv=8, d=128, kv="int8",
                        qdt=torch.bfloat16, batch=128, ctx=16384, pool_pages=128 * 1024 + 512),
     "qwen3-int8-1l": dict(model="Qwen3-8B attention", layers=1, hq=32, hkv=8, d=128, kv="int8",
@@ -98,7 +100,8 @@ WORKLOADS = {
     "olmoe-mix-small": dict(kind="mix", model="OLMoE-1B-7B attention", layers=2, hq=16, hkv=16, d=128,
                             kv="fp16", qdt=torch.float16, batch=32, ctx=(16, 8192), new_per_step=8,
                             prompt=(64, 2048), fork_frac=0.25, prefix=1024, pool_pages=9000, evict_at=0.9),
-    # the paging kernels at OLMoE scale (config 1's append + gather, sized up):
+    # the paging kernels at OLMoE scale (the append + gather of sequences of
+    # 37 / 128 / 255 / 512 tokens, sized up):
     # per step append 64 sequences x 64 new tokens into all 16 layers, gather
     # 256 random all-layer pages into contiguous K/V, copy 256 pages (CoW)
     "olmoe-paging": dict(kind="paging", model="OLMoE-1B-7B attention", layers=16, hkv=16, d=128, kv="fp16",
@@ -122,7 +125,7 @@ WORKLOADS = {
                       kv="bf16", batch=128, tokens_per_seq=1, ctx=16384),
     "qwen3-qkv-prefill": dict(kind="qkv", model="Qwen3-8B attention", layers=36, hidden=4096, hq=32, hkv=8, d=128,
                               kv="bf16", batch=8, tokens_per_seq=1024, ctx=0),
-    # the whole attention layer at BASELINE config 4's shape and FP8 pool,
+    # the whole attention layer at the Qwen3-8B FP8 decode shape (128 x 16,384 tokens),
     # through PagedAttentionLayer.decode: fused q/k/v projection + QK-norm +
     # RoPE (rows staged, FP8 append), decode attention over 16,384 tokens,
     # o_proj; fp32 normed input x and fp16 weights as the reference engine
