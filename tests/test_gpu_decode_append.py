@@ -57,6 +57,7 @@ def _clone(pool, cuda_device):
     ("bf16", 32, 8, torch.bfloat16, torch.bfloat16),   # tensor-core kernel, Qwen3-style GQA
     ("bf16", 32, 8, torch.bfloat16, torch.float32),
     ("int8", 16, 16, torch.float16, torch.float16),    # one-byte pools: append, then decode
+    ("int8", 32, 8, torch.bfloat16, torch.float32),
     ("fp8_e4m3", 32, 8, torch.bfloat16, torch.bfloat16),
 ])
 @pytest.mark.parametrize("chunk_pages", [0, 3])
