@@ -134,3 +134,41 @@ def test_decode_append_rejects_bad_rows(cuda_device):
     with pytest.raises(TypeError):
         pool.decode_attn_append(0, q, torch.zeros((2, 2, 128), device=cuda_device),
                                 torch.zeros((2, 2, 128), dtype=torch.float16, device=cuda_device), bt, ctx)
+
+
+@pytest.mark.parametrize("kv_dtype,hq,hkv", [("fp16", 16, 16), ("bf16", 32, 8)])
+def test_decode_append_bad_page_matches_two_calls(cuda_device, kv_dtype, hq, hkv):
+    """A sequence whose last block holds an out-of-range page id: the bounds
+    checks report SCKV_ERR_BOUNDS, its row is stored nowhere, page 0 is read
+    in its place — and the fused call still equals append + decode bit for
+    bit, outputs and pool bytes (the other sequences are untouched by it)."""
+    from synapcore_b200 import _native as N
+
+    ctx = [40, 17, 100, 64]
+    P = 60
+    pool, _, _, q = _make_case(cuda_device, kv_dtype, hq, hkv, ctx, pool_pages=P, seed=21)
+    twin = _clone(pool, cuda_device)
+    rng = np.random.default_rng(4)
+    bt = _private_table(ctx, P, rng)
+    bad = 1
+    bt[bad, (ctx[bad] - 1) // PAGE_TOKENS] = P + 5  # out of range
+    B, D = len(ctx), 128
+    qdt = torch.bfloat16 if kv_dtype == "bf16" else torch.float16
+    bt_d = torch.from_numpy(bt).to(cuda_device)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=cuda_device)
+    q_t = torch.from_numpy(q).to(qdt).to(cuda_device)
+    k_new = torch.from_numpy(rng.standard_normal((B, hkv, D)).astype(np.float32)).to(qdt).to(cuda_device)
+    v_new = torch.from_numpy(rng.standard_normal((B, hkv, D)).astype(np.float32)).to(qdt).to(cuda_device)
+    layer = 0
+    # the calls return at once; the kernels' bounds checks record the bad id
+    pool.append(k_new, v_new, cu, ctx_d - 1, bt_d, layer0=layer)
+    out = pool.decode_attn(layer, q_t, bt_d, ctx_d, out_dtype=torch.float32)
+    got = twin.decode_attn_append(layer, q_t, k_new, v_new, bt_d, ctx_d, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert pool.status()[0] == N.SCKV_ERR_BOUNDS
+    assert twin.status()[0] == N.SCKV_ERR_BOUNDS
+    assert torch.equal(got, out)
+    assert torch.equal(twin.data, pool.data)
+    pool.clear_status()
+    twin.clear_status()
