@@ -1980,6 +1980,12 @@ def main():
                          "(default) or a separate NCCL all-gather")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
+    # stdout carries exactly the one JSON line: anything a library prints on
+    # file descriptor 1 (e.g. NCCL's version banner when a communicator
+    # comes up) goes to stderr, and the line is written to the saved stdout
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
@@ -1997,7 +2003,8 @@ def main():
         else:
             res = bench_ours(args, w, world, rank, local)
         if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+            sys.stdout.flush()
+            os.write(json_fd, (json.dumps(res) + "\n").encode())
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -27,3 +27,22 @@ def test_projection_byte_and_flop_counts():
     o = bench.WORKLOADS["qwen3-oproj"]
     assert bench.qkv_bytes(o, 128) == 2 * 4096 * 4096 + 4 * 128 * 4096 + 4 * 128 * 4096
     assert bench.qkv_flops(o, 128) == 2 * 128 * 4096 * 4096
+
+
+def test_stdout_is_exactly_one_json_line():
+    """The reference arm (host cores, no GPU needed) prints one JSON line on
+    stdout and nothing else; library output goes to stderr."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, str(repo / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--cpu-seconds", "1"], capture_output=True, text=True, timeout=600,
+                         cwd=str(repo))
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = res.stdout.splitlines()
+    assert len(lines) == 1, res.stdout[:2000]
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0
