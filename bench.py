@@ -437,20 +437,26 @@ def fused_append(w, s) -> bool:
     return w["kv"] in ("fp16", "bf16")
 
 
-def layer_calls(w, s, l, q, k, v, out, out_full=None):
-    """One layer of the decode step through the public calls."""
+def layer_calls(w, s, l, q, k, v, out, out_full=None, events=None):
+    """One layer of the decode step through the public calls; `events` (a
+    list) gets a CUDA event on each side of the attention launch."""
     pool = s["pool"]
     pl = l % s["n_phys"]
     fused = fused_append(w, s)
     if not fused:
         pool.append(k, v, s["cu"], s["start"], s["bt"], layer0=pl)
+    if events is not None:
+        events.append(torch.cuda.Event(enable_timing=True))
+        events[-1].record()
     if "exchange" in s:
         exchange_layer(s, l, pl, q, out_full=out_full, k_new=k if fused else None, v_new=v if fused else None)
-        return
-    if fused:
+    elif fused:
         pool.decode_attn_append(pl, q, k, v, s["bt"], s["ctx"], out=out, workspace=s["ws"])
     else:
         pool.decode_attn(pl, q, s["bt"], s["ctx"], out=out, workspace=s["ws"])
+    if events is not None:
+        events.append(torch.cuda.Event(enable_timing=True))
+        events[-1].record()
     if "gather" in s and out_full is not None:
         out_full.copy_(s["gather"].gather(out))
 
@@ -461,29 +467,9 @@ def run_step(w, s, attn_events=None):
         s["graph"].replay()
         advance(s)
         return
-    pool = s["pool"]
-    gather = s.get("gather")
-    fused = fused_append(w, s)
     for l in range(w["layers"]):
-        pl = l % s["n_phys"]
-        if not fused:
-            pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
-        if attn_events is not None:
-            attn_events.append(torch.cuda.Event(enable_timing=True))
-            attn_events[-1].record()
-        if "exchange" in s:
-            exchange_layer(s, l, pl, s["q"][l], k_new=s["kn"][l] if fused else None,
-                           v_new=s["vn"][l] if fused else None)
-        elif fused:
-            pool.decode_attn_append(pl, s["q"][l], s["kn"][l], s["vn"][l], s["bt"], s["ctx"], out=s["out"][l],
-                                    workspace=s["ws"])
-        else:
-            pool.decode_attn(pl, s["q"][l], s["bt"], s["ctx"], out=s["out"][l], workspace=s["ws"])
-        if attn_events is not None:
-            attn_events.append(torch.cuda.Event(enable_timing=True))
-            attn_events[-1].record()
-        if gather is not None:
-            s["full"][l].copy_(gather.gather(s["out"][l]))
+        layer_calls(w, s, l, s["q"][l], s["kn"][l], s["vn"][l], s["out"][l],
+                    out_full=s["full"][l] if "gather" in s else None, events=attn_events)
     advance(s)
 
 
@@ -510,13 +496,8 @@ def bench_ours(args, w_full, world, rank, local):
         # CUDA graph (captured on every rank, nothing runs during capture)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            fused = fused_append(w, s)
             for l in range(w["layers"]):
-                pl = l % s["n_phys"]
-                if not fused:
-                    pool.append(s["kn"][l], s["vn"][l], s["cu"], s["start"], s["bt"], layer0=pl)
-                exchange_layer(s, l, pl, s["q"][l], k_new=s["kn"][l] if fused else None,
-                               v_new=s["vn"][l] if fused else None)
+                layer_calls(w, s, l, s["q"][l], s["kn"][l], s["vn"][l], s["out"][l])
         s["graph"] = g
     reset_contexts(s)
     total_bytes = 0
