@@ -255,12 +255,21 @@ class ContinuousBatchScheduler:
         share the engine's prefix cache. Keyword options: max_context (tokens
         per sequence, default 4096), max_pages (default: at most 8 GiB of
         pages), device, compute_dtype (engine_adapter.EngineModel). In this
-        mode `last_logits` are host numpy arrays, as in the reference."""
+        mode `last_logits` are host numpy arrays, as in the reference.
+
+    capture_decode=True replays each decode step from a CUDA graph, one per
+    (batch size, layers), for models whose step is device work only (torch
+    ops with no host reads; the reference-engine adapter routes experts on
+    the host and cannot be captured). The first step at a batch size runs
+    eagerly and is then captured; later ones copy their token ids and
+    positions into the graph's inputs and replay it. Row moves and page
+    reservation stay outside the graph."""
 
     def __init__(self, model, cache=None, max_batch_size: int = 8,
                  prefix_index: Optional[PrefixPageIndex] = None, eos_token_id: Optional[int] = None,
                  attn_scale: Optional[float] = None, *, max_context: int = 4096, max_pages: Optional[int] = None,
-                 device=None, compute_dtype: torch.dtype = torch.float64, keep_finished_cached: bool = False):
+                 device=None, compute_dtype: torch.dtype = torch.float64, keep_finished_cached: bool = False,
+                 capture_decode: bool = False):
         if isinstance(cache, int) and not isinstance(cache, bool):
             max_batch_size, cache = cache, None  # ContinuousBatchScheduler(engine, 4)
         self.engine = None
@@ -294,6 +303,11 @@ class ContinuousBatchScheduler:
         self.elapsed_ms = 0.0
         self.device = cache.device
         self._dispatch0 = self._dispatch_counts()
+        if capture_decode and self.engine is not None:
+            raise ValueError("capture_decode needs a model whose decode step is device work only")
+        self.capture_decode = bool(capture_decode)
+        # (batch size, layers) -> (graph, token ids, positions, logits, next ids)
+        self._decode_graphs: Dict[tuple, tuple] = {}
 
     # ----------------------------------------------------------- requests
     def submit_request(self, request_id: str, prompt_ids: List[int], max_new_tokens: int = 16,
@@ -437,9 +451,31 @@ class ContinuousBatchScheduler:
         def attend(l, q, k, v):
             return cache.decode_append_attention(l, q, k, v, B, scale=self.attn_scale, out_dtype=torch.float32)
 
-        h = self._layers(self.model.embed(meta[0]), meta[1], attend, n_layers)
-        logits = self.model.logits(h)
-        out = torch.argmax(logits, dim=-1).tolist()
+        def step(ids, pos):
+            logits = self.model.logits(self._layers(self.model.embed(ids), pos, attend, n_layers))
+            return logits, torch.argmax(logits, dim=-1)
+
+        key = (B, n_layers)
+        g = self._decode_graphs.get(key) if self.capture_decode else None
+        if g is not None:
+            graph, ids_buf, pos_buf, logits, nxt = g
+            ids_buf.copy_(meta[0])
+            pos_buf.copy_(meta[1])
+            graph.replay()
+            logits = logits.clone()  # the graph's output buffer is rewritten by the next replay
+        else:
+            logits, nxt = step(meta[0], meta[1])
+            if self.capture_decode:
+                # this step ran eagerly (kernels and workspaces are set up);
+                # capture the same step for the next ones at this batch size.
+                # Nothing runs during capture.
+                ids_buf, pos_buf = meta[0].clone(), meta[1].clone()
+                torch.cuda.synchronize(self.device)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    g_logits, g_nxt = step(ids_buf, pos_buf)
+                self._decode_graphs[key] = (graph, ids_buf, pos_buf, g_logits, g_nxt)
+        out = nxt.tolist()
         logits_host = logits.cpu().numpy() if self.engine is not None else None
         for r, req in enumerate(reqs):
             req.pos_offset += 1

@@ -103,7 +103,7 @@ def test_decode_attention_rows_match_isolated(cuda_device):
     c.check()
 
 
-def _run_scheduler(dev, max_batch):
+def _run_scheduler(dev, max_batch, capture=False):
     from stub_model import TorchStubModel, make_weights, prompts
     from synapcore_b200.paged_cache import PagedKVCache
     from synapcore_b200.scheduler import ContinuousBatchScheduler, PrefixPageIndex
@@ -111,7 +111,8 @@ def _run_scheduler(dev, max_batch):
     model = TorchStubModel(make_weights(), dev)
     cache = PagedKVCache(2, 2, 128, max_pages=256, max_seqs=8, max_blocks_per_seq=16, device=dev)
     index = PrefixPageIndex(cache, GOLD["prefix_cache_t4"]["seed_root"])
-    s = ContinuousBatchScheduler(model, cache, max_batch_size=max_batch, prefix_index=index)
+    s = ContinuousBatchScheduler(model, cache, max_batch_size=max_batch, prefix_index=index,
+                                 capture_decode=capture)
     for i, p in enumerate(prompts()):
         s.submit_request(f"req_{i}", p, max_new_tokens=5, stop_token_ids=set())
     steps = s.run_until_complete()
@@ -119,13 +120,18 @@ def _run_scheduler(dev, max_batch):
     return s, steps, index, cache
 
 
-@pytest.mark.parametrize("mode,max_batch", [("batched", 4), ("isolated", 1)])
-def test_scheduler_matches_reference_scheduler(cuda_device, mode, max_batch):
+@pytest.mark.parametrize("mode,max_batch,capture", [("batched", 4, False), ("isolated", 1, False),
+                                                    ("batched", 4, True), ("isolated", 1, True)])
+def test_scheduler_matches_reference_scheduler(cuda_device, mode, max_batch, capture):
+    """capture=True replays the decode steps from CUDA graphs (one per batch
+    size): the same goldens hold."""
     import sys
 
     sys.path.insert(0, str(Path(__file__).resolve().parent))
     g = GOLD["scheduler"][mode]
-    s, steps, index, cache = _run_scheduler(cuda_device, max_batch)
+    s, steps, index, cache = _run_scheduler(cuda_device, max_batch, capture)
+    if capture:
+        assert s._decode_graphs  # the decode steps did replay graphs
     done = s.completed_requests
     assert {k: v.generated_ids for k, v in done.items()} == g["generated"]
     assert {k: v.kv_prefix_skipped for k, v in done.items()} == g["prefix_skipped"]
