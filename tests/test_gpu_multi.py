@@ -317,3 +317,124 @@ def test_exchange_device_epochs_in_a_graph_with_fused_append(cuda_device):
     finally:
         if own_group:
             dist.destroy_process_group()
+
+
+def _append_case(seed=5, steps=3):
+    """A pool case whose sequences own their pages (a page being appended into
+    is read by no other sequence), plus each step's new K/V rows."""
+    rng = np.random.default_rng(seed)
+    L, hq, hkv, D, P = 2, 16, 4, 128, 96
+    ctx0 = [37, 200, 130, 15]
+    mb = max((c + steps + 15) // 16 for c in ctx0)
+    k = rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)
+    v = rng.standard_normal((P, L, hkv, 16, D)).astype(np.float16)
+    bt = rng.permutation(P)[:len(ctx0) * mb].reshape(len(ctx0), mb).astype(np.int32)
+    q = rng.standard_normal((len(ctx0), hq, D)).astype(np.float16)
+    kn = rng.standard_normal((steps, L, len(ctx0), hkv, D)).astype(np.float16)
+    vn = rng.standard_normal((steps, L, len(ctx0), hkv, D)).astype(np.float16)
+    return L, hq, hkv, D, P, ctx0, k, v, bt, q, kn, vn
+
+
+def _exchange_append_worker(rank, world, port, out_path, steps):
+    """The KV-head-sharded step as the bench runs it: every layer's exchange
+    decode appends the step's new token (this rank's kv heads) in the same
+    launch, epochs come from the device counter, and the whole step is one
+    replayed CUDA graph. Rank 0 records every (step, layer) output."""
+    import torch.distributed as dist
+
+    from synapcore_b200.distributed import HeadShardedExchange, head_range, query_head_range
+    from synapcore_b200.pool import KVPool
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    ex = None
+    g = None
+    try:
+        L, hq, hkv, D, P, ctx0, k, v, bt, q, kn, vn = _append_case(steps=steps)
+        kvr = head_range(hkv, world, rank)
+        qr = query_head_range(hq, hkv, world, rank)
+        pool = KVPool(L, len(kvr), D, P, "fp16", device=dev)
+        pool.write_pages(torch.arange(P, dtype=torch.int32, device=dev),
+                         torch.from_numpy(np.ascontiguousarray(k[:, :, kvr.start:kvr.stop])).to(dev),
+                         torch.from_numpy(np.ascontiguousarray(v[:, :, kvr.start:kvr.stop])).to(dev))
+        bt_d = torch.from_numpy(bt).to(dev)
+        ctx_d = torch.tensor(ctx0, dtype=torch.int32, device=dev) + 1  # step 0's token sits at ctx0
+        q_d = torch.from_numpy(np.ascontiguousarray(q[:, qr.start:qr.stop])).to(dev)
+        k_d = torch.zeros((L, len(ctx0), len(kvr), D), dtype=torch.float16, device=dev)
+        v_d = torch.zeros_like(k_d)
+        ex = HeadShardedExchange(pool, world, rank, L, len(ctx0), hq, torch.float32)
+        outs = []
+        for step in range(steps):
+            k_d.copy_(torch.from_numpy(np.ascontiguousarray(kn[step, :, :, kvr.start:kvr.stop])))
+            v_d.copy_(torch.from_numpy(np.ascontiguousarray(vn[step, :, :, kvr.start:kvr.stop])))
+            if g is None:
+                # step 0 runs eagerly (launch set-up), then the step is captured
+                for layer in range(L):
+                    ex.decode(layer, q_d, bt_d, ctx_d, 0, k_new=k_d[layer], v_new=v_d[layer])
+                    ex.wait(0)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for layer in range(L):
+                        ex.decode(layer, q_d, bt_d, ctx_d, 0, k_new=k_d[layer], v_new=v_d[layer])
+                        ex.wait(0)
+            else:
+                g.replay()
+            for layer in range(L):
+                outs.append(ex.output(layer, len(ctx0)).clone())
+            torch.cuda.synchronize()
+            dist.barrier()  # every rank has read this step before any rank starts the next
+            ctx_d += 1
+        pool.raise_on_status()
+        assert ex.status()[0] == 0
+        if rank == 0:
+            np.save(out_path, torch.stack(outs).cpu().numpy())
+        del g
+        dist.barrier()
+    finally:
+        if ex is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_head_sharded_graph_step_with_fused_append_equals_single_gpu(tmp_path):
+    """Two ranks replaying the KV-head-sharded decode step with the new
+    token's append fused into each layer's exchange decode: every (step,
+    layer) output equals sckv_append + sckv_decode_attn of all heads on one
+    GPU."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from synapcore_b200.pool import KVPool
+
+    out = tmp_path / "exchange_append.npy"
+    steps = 3
+    mp.start_processes(_exchange_append_worker, args=(2, _free_port(), str(out), steps), nprocs=2, join=True,
+                       start_method="spawn")
+    got_all = np.load(out)
+    L, hq, hkv, D, P, ctx0, k, v, bt, q, kn, vn = _append_case(steps=steps)
+    dev = torch.device("cuda", 0)
+    pool = KVPool(L, hkv, D, P, "fp16", device=dev)
+    pool.write_pages(torch.arange(P, dtype=torch.int32, device=dev), torch.from_numpy(k).to(dev),
+                     torch.from_numpy(v).to(dev))
+    bt_d = torch.from_numpy(bt).to(dev)
+    q_d = torch.from_numpy(q).to(dev)
+    B = len(ctx0)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    i = 0
+    for step in range(steps):
+        ctx_d = torch.tensor([c + step + 1 for c in ctx0], dtype=torch.int32, device=dev)
+        for layer in range(L):
+            pool.append(torch.from_numpy(kn[step, layer]).to(dev), torch.from_numpy(vn[step, layer]).to(dev), cu,
+                        ctx_d - 1, bt_d, layer0=layer)
+            ref = pool.decode_attn(layer, q_d, bt_d, ctx_d, out_dtype=torch.float32).cpu().numpy()
+            assert np.max(np.abs(got_all[i] - ref)) <= 2e-3 * np.max(np.abs(ref)), (step, layer)
+            i += 1
+    pool.raise_on_status()
