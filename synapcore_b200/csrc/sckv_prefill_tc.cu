@@ -636,8 +636,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         mbar_wait_bounded(&fulls[t % kStagesTc], (t / kStagesTc) & 1, SCKV_WAIT_LIMIT_NS);
       if (q_issued > 0) mbar_wait_bounded(q_full, (q_issued - 1) & 1, SCKV_WAIT_LIMIT_NS);
     }
-  } else if (warp == kWarpMma) {
+  } else if (warp == kWarpMma && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread issues every MMA and commit and does its own bounded waits:
+    // warp-wide waits and the reconvergence around single-lane issues cost
+    // more than the issues themselves (lanes 1-31 go straight to the final
+    // barrier and join the tensor-memory release there).
+    auto wait1 = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return mbar_wait_bounded(bar, parity, SCKV_WAIT_LIMIT_NS);
+    };
     constexpr uint32_t kIdescS = instr_desc_f16(kBF16, kKeysTc, false);
     constexpr uint32_t kIdescPV = instr_desc_f16(kBF16, kHDim, true);
     // descriptors of the first Q tile, K slot and V slot; every operand of
@@ -652,7 +659,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // PV of local K/V tile i (global gi): O[w] (+)= P[w] . V for each live Q tile
     auto issue_pv = [&](const TcItem& it, int gi, int i, const int (&gw0)[kQTiles]) -> bool {
       const int st = gi % kStagesTc;
-      if (!warp_wait(&v_full[st], (gi / kStagesTc) & 1)) return false;
+      if (!wait1(&v_full[st], (gi / kStagesTc) & 1)) return false;
       tc_fence_after();
       uint8_t* vslot = base + kOffV + st * kSlotBytes;
       const int key0 = i * kKeysTc;
@@ -661,13 +668,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         // were never written or hold an older tile
         const int r0 = max(0, it.vlim - key0);
         const int n16 = (kKeysTc - r0) * 8;  // 16-byte chunks per half
-        for (int c = lane; c < 2 * n16; c += 32) {
+        for (int c = 0; c < 2 * n16; ++c) {
           const int half = c / n16, rc = c - half * n16;
           *reinterpret_cast<uint4*>(vslot + half * kTileHalf + (r0 + (rc >> 3)) * 128 + (rc & 7) * 16) =
               make_uint4(0u, 0u, 0u, 0u);
         }
         fence_proxy_async_smem();
-        __syncwarp();
       }
       const uint64_t v_desc = desc_advance(v_desc0, (uint32_t)(st * kSlotBytes));
       bool live[kQTiles];
@@ -678,15 +684,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const int gw = gw0[w] + i;
         bw[w] = gw & 1;
         if (!live[w]) continue;
-        if (!warp_wait(&p_full[w * 2 + bw[w]], (gw >> 1) & 1)) return false;
+        if (!wait1(&p_full[w * 2 + bw[w]], (gw >> 1) & 1)) return false;
         if (i == 0 && items_w[w] > 0) {
           // O[w] still holds this warpgroup's previous item until its
           // epilogue has read it
-          if (!warp_wait(&o_empty[w], (items_w[w] - 1) & 1)) return false;
+          if (!wait1(&o_empty[w], (items_w[w] - 1) & 1)) return false;
         }
       }
       tc_fence_after();
-      if (lane == 0) {
+      {
         // the two Q tiles' accumulation chains interleave, so each MMA's
         // dependency on the previous one into the same O overlaps the other's
 #pragma unroll
@@ -707,20 +713,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         for (int w = 0; w < kQTiles; ++w)
           if (live[w]) umma_commit(&pv_done[w * 2 + bw[w]]);
       }
-      __syncwarp();
-      if (lane == 0) umma_commit(&v_empty[st]);
-      __syncwarp();
+      umma_commit(&v_empty[st]);
       return true;
     };
     for (int k = 0; ok; ++k) {
-      if (*abort_flag || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
+      if (*abort_flag || !wait1(&item_full[k & 3], (k >> 2) & 1)) {
         ok = false;
         break;
       }
       const int item = item_ring[k & 3];
       if (item >= n_items) break;
       const TcItem it = tc_item(p, tile_cum, total_tiles, item, BQ);
-      if (*abort_flag || !warp_wait(p.q_tma == 2 ? q_conv : q_full, k & 1)) {
+      if (*abort_flag || !wait1(p.q_tma == 2 ? q_conv : q_full, k & 1)) {
         ok = false;
         break;
       }
@@ -729,12 +733,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       for (int j = 0; j < it.n_k; ++j) {
         const int gj = gk + j;
         const int st = gj % kStagesTc;
-        if (*abort_flag || !warp_wait(&k_full[st], (gj / kStagesTc) & 1)) {
+        if (*abort_flag || !wait1(&k_full[st], (gj / kStagesTc) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (lane == 0) {
+        {
           const uint64_t k_desc = desc_advance(k_desc0, (uint32_t)(st * kSlotBytes));
           // the two Q tiles' 8-step chains interleave: an N = 64 product is
           // short, so back-to-back MMAs into one accumulator would each wait
@@ -757,7 +761,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           umma_commit(&k_empty[st]);
           if (j == it.n_k - 1) umma_commit(q_empty);  // Q no longer read once these S are done
         }
-        __syncwarp();
         if (j >= 1 && !issue_pv(it, gj - 1, j - 1, gw0)) {
           ok = false;
           break;
@@ -775,13 +778,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       }
     }
     if (!ok) {
-      if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
-      if (lane == 0) *abort_flag = 1;
+      if (!*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
+      *abort_flag = 1;
     }
     // drain: every MMA issued above has finished before TMEM is released
-    if (lane == 0) umma_commit(mma_done);
-    __syncwarp();
-    warp_wait(mma_done, 0);
+    umma_commit(mma_done);
+    wait1(mma_done, 0);
   } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ softmax
     const int w = (warp - 4) >> 2;       // Q tile of this warpgroup
@@ -1011,6 +1013,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (lane == 0) *abort_flag = 1;
     }
   }
+  // the MMA warp's lane 0 rejoins lanes 1-31 (which skipped the issuer loop)
+  // so the block barrier and the tensor-memory release run converged
+  if (warp == kWarpMma) __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kWarpMma) {
