@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint64_t* v_full = bars + 2 * kStagesTc;      // [S] V tile landed
   uint64_t* v_empty = bars + 3 * kStagesTc;     // [S] every PV product of the V tile finished (commit)
   uint64_t* s_full = bars + 4 * kStagesTc;      // [w][2] S of warpgroup w's tile in TMEM (commit)
-  uint64_t* p_full = s_full + 4;                // [w][2] P of warpgroup w's tile in TMEM (128 threads)
+  uint64_t* p_full = s_full + 4;                // [w][2] P of warpgroup w's tile in TMEM (one arrival per warp)
   // [w][2] PV of warpgroup w's tile g finished (commit to pv_done[w][g & 1]).
   // A softmax thread waits for PV(g) only after S(g) (epilogue) or S(g + 1)
   // (O rescale) landed; that commit covers every MMA issued before it,
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   // P(g + 2). So the barrier is at PV(g)'s phase or one past it and the
   // parity wait is unambiguous however rarely the thread waits on it.
   uint64_t* pv_done = p_full + 4;
-  uint64_t* o_empty = pv_done + 4;              // [w] warpgroup w's O was read out (128 threads)
+  uint64_t* o_empty = pv_done + 4;              // [w] warpgroup w's O was read out (one arrival per warp)
   uint64_t* q_full = o_empty + 2;               // Q of the item in shared memory (TMA, or 256 softmax threads)
   uint64_t* q_empty = q_full + 1;               // every S of the item finished (commit): Q may be replaced
   uint64_t* mma_done = q_full + 2;              // every issued MMA finished (drain)
@@ -293,8 +293,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         uint32_t count = 1;
         if (bar >= k_full && bar < k_full + kStagesTc) count = 2;   // two K producer warps
         if (bar >= v_full && bar < v_full + kStagesTc) count = 2;   // two V producer warps
-        if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads;
-        if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads;
+        if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads / 32;   // one arrival per warp
+        if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads / 32;
         if (bar == q_full && !p.q_tma) count = kQTiles * kSoftmaxThreads;
         if (bar == q_conv) count = 3 * 32;
         mbar_init(bar, count);
@@ -915,8 +915,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           l += ls0 + ls1;
           tc_wait_st();
         }
+        // every thread's P stores completed (wait::st) and are ordered before
+        // the warp's sync; one arrival per warp releases them to the MMA thread
         tc_fence_before();
-        mbar_arrive(&my_p_full[b]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&my_p_full[b]);
       }
       if (!ok) break;
       // ---- epilogue: O / l for this thread's row, once the tile's last PV finished
@@ -959,7 +962,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&o_empty[w]);  // O[w] may be overwritten by the next item's PV
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[w]);  // O[w] may be overwritten by the next item's PV
       g += n;
     }
     if (!ok) {
