@@ -60,8 +60,10 @@ constexpr uint32_t kColO = 256;
 
 // warps: 0 claims items, loads Q and half of each K tile; 3 the other half
 // of K; 2 and 12 the two halves of V; 1 issues the MMAs; 4-7 and 8-11 are
-// the softmax warpgroups of Q tiles 0 and 1; 13-15 convert Q in place when
-// it arrives by TMA in the other 16-bit type (else idle)
+// the softmax warpgroups of Q tiles 0 and 1; 14 and 15 convert Q in place
+// when it arrives by TMA in the other 16-bit type (else idle). Warp 13 stays
+// idle: it would share SM sub-partition 1 (warp % 4) with the MMA-issuing
+// thread, whose issue rate paces the kernel.
 constexpr int kWarpK0 = 0, kWarpMma = 1, kWarpV0 = 2, kWarpK1 = 3, kWarpV1 = 12;
 
 constexpr int kQHalf = kRowsTc * 128;         // one 64-dim half of a Q tile: 16 KiB
@@ -111,7 +113,7 @@ struct TcParams {
   int out_dtype;
   // how Q reaches shared memory: 0 the softmax threads load and convert it;
   // 1 TMA, q has the MMA's type; 2 TMA of the other 16-bit type, then warps
-  // 13-15 convert the tile in place (bf16 <-> f16, rounded as load_q8 does)
+  // 14 and 15 convert the tile in place (bf16 <-> f16, rounded as load_q8 does)
   int q_tma;
   const void* kv_scales;  // one-byte pools: FP8 fp32 [L][P][K|V][H], int8 fp16 [L][P][K|V][H][16]
   unsigned long long* next_item;  // work counter, zero at launch
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint64_t* item_full = q_full + 3;
   // one-byte pools: [producer warp role 2 kv + part][2] staged page codes landed (TMA)
   uint64_t* stage_full = item_full + 4;
-  // Q converted in place (q_tma 2; 96 threads of warps 13-15): the MMAs wait for this instead of q_full
+  // Q converted in place (q_tma 2; 64 threads of warps 14, 15): the MMAs wait for this instead of q_full
   uint64_t* q_conv = stage_full + (C::kB8 ? 8 : 0);
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + kOffItemRing);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmemSlot);
@@ -296,7 +298,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         if (bar >= p_full && bar < p_full + 4) count = kSoftmaxThreads / 32;   // one arrival per warp
         if (bar >= o_empty && bar < o_empty + 2) count = kSoftmaxThreads / 32;
         if (bar == q_full && !p.q_tma) count = kQTiles * kSoftmaxThreads;
-        if (bar == q_conv) count = 3 * 32;
+        if (bar == q_conv) count = 2 * 32;
         mbar_init(bar, count);
       }
       *abort_flag = 0;
@@ -970,13 +972,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (lane == 0 && !*abort_flag) sckv_report(p.status, SCKV_ERR_TIMEOUT, blockIdx.x, KID_PREFILL);
       if (lane == 0) *abort_flag = 1;
     }
-  } else if (warp >= 13 && p.q_tma == 2) {
+  } else if (warp >= 14 && p.q_tma == 2) {
     // ------------------------------------------------------------ Q conversion
     // Q arrived by TMA in the other 16-bit type: convert both Q tiles in
     // place, 16-byte chunk by chunk (the 128-byte swizzle only permutes
     // chunks), while the softmax warps finish the previous item. A tile
     // with no token of the item holds stale values that no MMA reads.
-    const int ct = threadIdx.x - 13 * 32;  // 0..95
+    const int ct = threadIdx.x - 14 * 32;  // 0..63
     bool ok = true;
     for (int k = 0; ok; ++k) {
       if (*abort_flag || !warp_wait(&item_full[k & 3], (k >> 2) & 1)) {
@@ -988,7 +990,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         ok = false;
         break;
       }
-      for (int c = ct; c < kQTiles * kQTileBytes / 16; c += 3 * 32) {
+      for (int c = ct; c < kQTiles * kQTileBytes / 16; c += 2 * 32) {
         uint4* chunk = reinterpret_cast<uint4*>(base + c * 16);
         const uint4 raw = *chunk;
         const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -1090,7 +1092,7 @@ int launch_prefill_tc(const sckv_pool* pool, int layer, const void* q, int q_dty
   const int64_t max_tiles = (int64_t)(n_tokens + BQ2 - 1) / BQ2 + n_seqs;  // >= sum of ceil(T_s / BQ2)
   const int64_t max_items = max_tiles * pool->num_kv_heads;
   if (max_items > INT32_MAX) return SCKV_ERR_UNSUPPORTED;
-  // 16-bit q arrives by TMA (converted in place by warps 13-15 when it is
+  // 16-bit q arrives by TMA (converted in place by warps 14, 15 when it is
   // not the MMA's type): a 3-D view (dim, head, token) whose boxes of 64
   // dims x G heads x 128/G tokens are exactly an item's 128 rows, in row order
   CUtensorMap qmap;
