@@ -171,6 +171,33 @@ __device__ __forceinline__ uint4 load_q8(const void* q, int64_t idx, int dtype) 
   return r;
 }
 
+// sm_100 arithmetic the softmax threads use to save issue slots: a 3-input
+// max, and packed pairs of fp32 values (two independent round-to-nearest
+// fp32 operations per instruction, the same results as two scalar ones).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // One work item's geometry, derived identically by every role. An item is
 // (sequence, pair of 128-row Q tiles, kv head); Q tile w holds tokens
 // tok0 + w BQ .. tok0 + (w + 1) BQ - 1.
@@ -856,14 +883,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         float pm = -INFINITY;
         if (key0 + kKeysTc - 1 <= tile_lim) {
 #pragma unroll
-          for (int c = 0; c < kKeysTc; ++c) pm = fmaxf(pm, sv[c]);
+          for (int c = 0; c < kKeysTc; c += 2) pm = fmax3(pm, sv[c], sv[c + 1]);
         } else {
 #pragma unroll
-          for (int c = 0; c < kKeysTc; ++c) {
-            const float v = (key0 + c <= lim) ? sv[c] : -INFINITY;
-            sv[c] = v;
-            pm = fmaxf(pm, v);
-          }
+          for (int c = 0; c < kKeysTc; ++c) sv[c] = (key0 + c <= lim) ? sv[c] : -INFINITY;
+#pragma unroll
+          for (int c = 0; c < kKeysTc; c += 2) pm = fmax3(pm, sv[c], sv[c + 1]);
         }
         pm *= p.scale_log2;
         // stale running max (log2 units): move it only when a tile's max
@@ -902,16 +927,22 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           uint32_t ph[32], plo[32];
           // a row that sees no key yet (m = -inf) has every score -inf: 2^-inf = 0
           const float mm = (m == -INFINITY) ? 0.f : m;
-          float ls0 = 0.f, ls1 = 0.f;
+          // per key pair: one packed FMA, two exponentials, one packed add
+          // into the (even, odd) sums
+          const uint64_t scale2 = f32x2(p.scale_log2, p.scale_log2), negm2 = f32x2(-mm, -mm);
+          uint64_t ls2 = f32x2(0.f, 0.f);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const float p0 = ex2_approx(fmaf(sv[2 * c], p.scale_log2, -mm));
-            const float p1 = ex2_approx(fmaf(sv[2 * c + 1], p.scale_log2, -mm));
-            ls0 += p0;
-            ls1 += p1;
+            float x0, x1;
+            f32x2_split(fma_f32x2(f32x2(sv[2 * c], sv[2 * c + 1]), scale2, negm2), x0, x1);
+            const float p0 = ex2_approx(x0);
+            const float p1 = ex2_approx(x1);
+            ls2 = add_f32x2(ls2, f32x2(p0, p1));
             ph[c] = pack2<kBF16>(p0, p1);
             if (kBF16) plo[c] = pack2<true>(p0 - round16<true>(p0), p1 - round16<true>(p1));
           }
+          float ls0, ls1;
+          f32x2_split(ls2, ls0, ls1);
           tmem_st32(t_row + col_s + b * kKeysTc, ph);
           if (kBF16) tmem_st32(t_row + col_s + b * kKeysTc + 32, plo);
           l += ls0 + ls1;
