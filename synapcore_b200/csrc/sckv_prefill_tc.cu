@@ -930,6 +930,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           // per key pair: one packed FMA, two exponentials, one packed add
           // into the (even, odd) sums
           const uint64_t scale2 = f32x2(p.scale_log2, p.scale_log2), negm2 = f32x2(-mm, -mm);
+          const uint64_t minus1 = f32x2(-1.f, -1.f);
           uint64_t ls2 = f32x2(0.f, 0.f);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -939,7 +940,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const float p1 = ex2_approx(x1);
             ls2 = add_f32x2(ls2, f32x2(p0, p1));
             ph[c] = pack2<kBF16>(p0, p1);
-            if (kBF16) plo[c] = pack2<true>(p0 - round16<true>(p0), p1 - round16<true>(p1));
+            if (kBF16) {
+              // lo = p - bf16(p), exact: the hi pair widened back from ph by
+              // bit operations, then one packed fma(hi, -1, p)
+              const uint64_t hi2 = f32x2(__uint_as_float(ph[c] << 16), __uint_as_float(ph[c] & 0xFFFF0000u));
+              float l0, l1;
+              f32x2_split(fma_f32x2(hi2, minus1, f32x2(p0, p1)), l0, l1);
+              plo[c] = pack2<true>(l0, l1);
+            }
           }
           float ls0, ls1;
           f32x2_split(ls2, ls0, ls1);
