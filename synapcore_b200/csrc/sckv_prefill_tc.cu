@@ -197,6 +197,18 @@ __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// a packed pair times a packed factor, rounded to a 16-bit pair
+template <bool kBF16>
+__device__ __forceinline__ uint32_t mul_pack2(float x, float y, uint64_t f2) {
+  float a, b;
+  f32x2_split(mul_f32x2(f32x2(x, y), f2), a, b);
+  return pack2<kBF16>(a, b);
+}
 
 // One work item's geometry, derived identically by every role. An item is
 // (sequence, pair of 128-row Q tiles, kv head); Q tile w holds tokens
@@ -515,6 +527,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
           uint8_t* dst = slot + hf * kTileHalf + (2 * part + i) * 2048 + r * 128;
           const float sv = i == 0 ? scl_dec0 : scl_dec1;
           const __half2 s2 = __float2half2_rn(sv);  // int8: the stored fp16 scale, exact
+          const uint64_t sv2 = f32x2(sv, sv);        // FP8: the fp32 scale, one packed multiply per pair
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             // 16 codes: dims 64 hf + 16 c .. + 15 (128-byte swizzle: chunk ^ row)
@@ -533,8 +546,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
               } else {
                 const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
                 const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-                lo = pack2<false>(a.x * sv, a.y * sv);
-                hi = pack2<false>(b.x * sv, b.y * sv);
+                lo = mul_pack2<false>(a.x, a.y, sv2);
+                hi = mul_pack2<false>(b.x, b.y, sv2);
               }
               o[2 * q] = lo;
               o[2 * q + 1] = hi;
@@ -971,6 +984,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       }
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const uint64_t inv2 = f32x2(inv, inv);
       const int64_t obase = ((int64_t)(it.q_base + rtok) * p.hq + rhead) * kHDim;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
@@ -994,8 +1008,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
               uint32_t* wp = &wv.x;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
-                const float a = __uint_as_float(r[c + 2 * kk]) * inv, bb = __uint_as_float(r[c + 2 * kk + 1]) * inv;
-                wp[kk] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
+                const float a = __uint_as_float(r[c + 2 * kk]), bb = __uint_as_float(r[c + 2 * kk + 1]);
+                wp[kk] = obf ? mul_pack2<true>(a, bb, inv2) : mul_pack2<false>(a, bb, inv2);
               }
               *reinterpret_cast<uint4*>(o + c) = wv;
             }
