@@ -893,16 +893,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         // row max of the raw scores (the scale is positive); tiles every row
         // of the Q tile sees in full skip the causal mask
         const int key0 = j * kKeysTc;
-        float pm = -INFINITY;
-        if (key0 + kKeysTc - 1 <= tile_lim) {
-#pragma unroll
-          for (int c = 0; c < kKeysTc; c += 2) pm = fmax3(pm, sv[c], sv[c + 1]);
-        } else {
+        if (key0 + kKeysTc - 1 > tile_lim) {
 #pragma unroll
           for (int c = 0; c < kKeysTc; ++c) sv[c] = (key0 + c <= lim) ? sv[c] : -INFINITY;
-#pragma unroll
-          for (int c = 0; c < kKeysTc; c += 2) pm = fmax3(pm, sv[c], sv[c + 1]);
         }
+        // (one max loop for both cases: the kernel's roles share one
+        // instruction cache, so duplicated unrolled code costs)
+        float pm = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kKeysTc; c += 2) pm = fmax3(pm, sv[c], sv[c + 1]);
         pm *= p.scale_log2;
         // stale running max (log2 units): move it only when a tile's max
         // exceeds it by more than 8
