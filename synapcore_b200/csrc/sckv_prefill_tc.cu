@@ -3,33 +3,43 @@
 //
 // Same contract as prefill_kernel in sckv_prefill.cu (models/adapters.py:
 // 1209-1229, causal mask :1218-1224, query t of a sequence at position
-// start + t sees keys 0..start + t), for f16 and bf16 pools.
+// start + t sees keys 0..start + t), for every pool type (one-byte pages
+// are decoded into f16 tiles by the producer warps).
 //
 // Work item = (sequence, two tiles of 128 query rows, kv head). The rows
 // are (token, q head) pairs of the G heads that read the kv head, so a tile
 // holds 128 / G tokens; both tiles share every K/V tile loaded. One
 // persistent CTA per SM (512 TMEM columns) claims items from a work counter;
-// 16 warps:
+// 16 warps (a warp runs on SM sub-partition warp % 4):
 //   warps 0, 3  claim items (warp 0), load the item's Q (one TMA box per
-//              64-dim half and tile when q has the pool's type, else the
-//              softmax warps write it) and stream K: 4 pages (64 keys) per
-//              tile, one 2 KiB box per (page, 64-dim half), 128-byte swizzle,
-//              into a 4-slot ring laid out as the UMMA K-major canonical tile
-//              (consecutive pages are consecutive rows); each warp copies two
-//              pages of a tile (one TMA issue holds its warp ~0.1 us).
+//              64-dim half and tile for 16-bit q; f32 q is written by the
+//              softmax threads) and stream K: 4 pages (64 keys) per tile,
+//              one 2 KiB box per (page, 64-dim half), 128-byte swizzle, into
+//              a ring laid out as the UMMA K-major canonical tile
+//              (consecutive pages are consecutive rows); each warp copies
+//              two pages of a tile (one TMA issue holds its warp ~0.1 us).
+//              One-byte pools stage the codes by TMA and decode them with
+//              all lanes.
 //   warps 2, 12 stream V the same way into their own ring.
-//   warp 1     allocates the tensor memory and issues the MMAs:
+//   warp 1     allocates the tensor memory; its lane 0 alone issues the
+//              MMAs and commits and does its own bounded waits:
 //                S[w][b] (128 x 64 fp32) = Q[w] . K^T   8 x tcgen05.mma (K = 16)
 //                O[w]    (128 x 128 fp32) += P[w][b] . V  4 x tcgen05.mma (A from TMEM)
 //              for both Q tiles w, S double-buffered; K(j) is released when
 //              both S(j) finished, V(j) after both PV(j). Completion is
-//              signalled with tcgen05.commit on mbarriers.
+//              signalled with tcgen05.commit on mbarriers. Its issue rate
+//              paces the kernel, so its sub-partition (1) holds no producer
+//              and no Q conversion.
 //   warps 4-7, 8-11  softmax of Q tile 0, 1: thread i owns query row i (TMEM
 //              lane i): loads its 64 scores with tcgen05.ld, masks (only tiles
 //              the causal limit cuts), keeps a stale running max (moves only
 //              by more than 2^8, rescaling O in TMEM when it does), writes
-//              P = 2^(s*scale - m) as f16 / bf16 back over S (tcgen05.st), and
-//              at the end of the item normalises its O row and stores it.
+//              P = 2^(s*scale - m) as f16 / bf16 back over S (tcgen05.st;
+//              3-input max and packed fp32 FMA / add), one barrier arrival
+//              per warp, and at the end of the item normalises its O row and
+//              stores it.
+//   warps 14, 15  convert Q in place when it arrives in the other 16-bit
+//              type than the MMAs'.
 // bf16 pools split P into bf16 hi + lo parts (two PV products) so P's
 // rounding stays below 2^-16 relative; f16 pools use P in f16.
 // Slots past the sequence's last token (they may hold anything) are zeroed
